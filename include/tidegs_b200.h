@@ -1,0 +1,334 @@
+/*
+ * tidegs_b200.h -- C ABI of libtidegs_b200.so, the sm_100a implementation of
+ * TideGS's resident-block optimizer / materialization / write-back hot path.
+ *
+ * Conventions shared by every entry point:
+ *   - Plain pointers and sizes only. Every pointer named dev_* / inside an args
+ *     struct is a DEVICE pointer unless its comment says "host".
+ *   - The library allocates nothing and keeps no per-call state: every buffer,
+ *     including scratch words, is owned by the caller. Calls are re-entrant and
+ *     may come from several host threads on different streams.
+ *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream).
+ *     All work is enqueued on it; no entry point synchronizes the device.
+ *   - Return value: 0 (TGS_OK) or a TGS_ERR_* code. The message of the last
+ *     failure on the calling host thread is returned by tgs_last_error().
+ *   - Device-side errors (bad index, unsorted ids, wait that timed out) are
+ *     written to a caller-owned int32[4] "error word" on the device:
+ *       err[0] = error code (0 = none), err[1] = first offending index (low 32),
+ *       err[2] = first offending index (high 32), err[3] = auxiliary value.
+ *     A kernel that finds err[0] != 0 at entry does nothing, so a failed
+ *     validation never leaves the optimizer state half-updated.
+ *
+ * Row layout: one Gaussian = 59 fp32 columns split into six components, in the
+ * reference's COMPONENT_SPECS order (strategies/tide_engine/
+ * gpu_resident_optimizer.py:82-89):
+ *   component  0 xyz(3)  1 opacity(1)  2 scaling(3)  3 rotation(4)
+ *              4 features_dc(3)  5 features_rest(45)
+ * Packed [rows, 59] host/SSD blocks use one of the two reference column orders
+ * (storage/block_reader.py:43-44):
+ *   TGS_LAYOUT_UNIFIED = xyz|opacity|scaling|rotation|dc|rest
+ *   TGS_LAYOUT_CACHE   = xyz|scaling|rotation|opacity|dc|rest
+ */
+#ifndef TIDEGS_B200_H
+#define TIDEGS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TGS_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define TGS_API __attribute__((visibility("default")))
+#else
+#define TGS_API
+#endif
+
+#define TGS_NUM_COMPONENTS 6
+#define TGS_ROW_WIDTH 59
+/* Resident-Adam state row: 64 (m, v) fp32 pairs = 512 bytes. Pairs 0..58 hold
+ * the 59 columns in UNIFIED order, float 124 (pair 62's first word) holds the
+ * admission stamp of the row as uint32 bits, the rest is padding. */
+#define TGS_STATE_ROW_FLOATS 128
+
+enum {
+  TGS_OK = 0,
+  TGS_ERR_INVALID_ARG = 1,
+  TGS_ERR_CUDA = 2,
+  TGS_ERR_UNSUPPORTED = 3
+};
+
+/* Device error codes written to err[0]. */
+enum {
+  TGS_DEV_OK = 0,
+  TGS_DEV_ID_OUT_OF_RANGE = 1,   /* a local row id is < 0 or >= param_rows */
+  TGS_DEV_ID_NOT_SORTED = 2,     /* local row ids are not strictly ascending */
+  TGS_DEV_ID_NOT_RESIDENT = 3,   /* a local row id lies in no resident block */
+  TGS_DEV_WAIT_TIMEOUT = 4,      /* a bounded mbarrier wait gave up */
+  TGS_DEV_BAD_SLICE = 5          /* a copy segment/plan is inconsistent */
+};
+
+enum { TGS_LAYOUT_CACHE = 0, TGS_LAYOUT_UNIFIED = 1 };
+
+/* ------------------------------------------------------------------------ */
+/* Library information                                                       */
+/* ------------------------------------------------------------------------ */
+
+/* ABI version (TGS_ABI_VERSION of the build). */
+TGS_API int tgs_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated
+ * to len). Returns the full message length. */
+TGS_API int tgs_last_error(char* buf, size_t len);
+
+/* ------------------------------------------------------------------------ */
+/* GPU-resident Adam                                                         */
+/* Replaces: strategies/tide_engine/gpu_resident_optimizer.py                */
+/*   _working_set_state_rows   :266-300  (row -> block position -> state row) */
+/*   _update_touched_slot_metadata :302-337 (per-slot step, bias tables)     */
+/*   _fused_resident_adam_kernel   :16-70, called 6x by step :420-509        */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  /* Working-set layout: P resident block positions sorted by slice start.
+   * Position p covers local rows [pos_start[p], pos_end[p]) and owns optimizer
+   * slot pos_slot[p]; its state rows are pos_slot[p]*block_size + row-start. */
+  const int64_t* pos_start;   /* [P] */
+  const int64_t* pos_end;     /* [P] */
+  const int32_t* pos_slot;    /* [P] */
+  int32_t n_positions;        /* P */
+  int64_t block_size;
+  int64_t param_rows;         /* M: rows of every parameter component */
+
+  /* Touched rows: the compacted gradient's row i belongs to local row
+   * local_ids[i]; ids must be strictly ascending (torch.nonzero order). */
+  const int64_t* local_ids;   /* [n] */
+  int64_t n_rows;             /* n */
+
+  /* Per-slot device tables (slots = n_slots). */
+  int32_t* slot_step;         /* [slots] steps taken since admission */
+  const uint32_t* slot_stamp; /* [slots] admission stamp of the slot (>=1) */
+  float* slot_bias;           /* [slots][2] (1-b1^t, sqrt(1-b2^t)) of this step */
+  const float* step_table;    /* [table_len][2] (1-b1^t, sqrt(1-b2^t)) for t */
+  int32_t step_table_len;     /* t >= len uses entry len-1 (saturated) */
+  int32_t n_slots;
+
+  int32_t* pos_count;         /* [P] out: touched rows per position */
+  int32_t* err;               /* [4] device error word (zeroed by the call) */
+} TgsResidentCountArgs;
+
+/* Validates local_ids (range, strict order, residency), counts touched rows
+ * per position, and for every touched position increments its slot's step
+ * counter and fills slot_bias from step_table. Enqueues: memset of pos_count
+ * and err, 2 kernels. Replaces gpu_resident_optimizer.py:266-337. */
+TGS_API int tgs_resident_adam_count(const TgsResidentCountArgs* args, void* stream);
+
+typedef struct {
+  float* param[TGS_NUM_COMPONENTS];       /* [M, W_c] contiguous */
+  const float* grad[TGS_NUM_COMPONENTS];  /* [n, W_c] contiguous */
+  float lr[TGS_NUM_COMPONENTS];           /* learning rate per component */
+  float beta1, beta2, eps;
+  /* 1 - beta evaluated in double precision by the caller, then rounded to
+   * fp32 (as the reference's torch step does with its Python-float betas). */
+  float one_minus_beta1, one_minus_beta2;
+  float batch_size;                       /* grad is divided by it */
+
+  const int64_t* pos_start;               /* as in TgsResidentCountArgs */
+  const int64_t* pos_end;
+  const int32_t* pos_slot;
+  int32_t n_positions;
+  int64_t block_size;
+  const int64_t* local_ids;
+  int64_t n_rows;
+
+  float* state;                           /* [slots*block_size, 128] 16B-aligned */
+  const uint32_t* slot_stamp;             /* [slots] */
+  const float* slot_bias;                 /* [slots][2] from tgs_resident_adam_count */
+  const int32_t* err;                     /* [4] skip everything when err[0]!=0 */
+} TgsResidentAdamArgs;
+
+/* One fused launch updating all 59 columns of every touched row, in the op
+ * order of the reference's torch step (gpu_resident_optimizer.py:355-364):
+ *   g = grad / batch_size
+ *   m = b1*m + (1-b1)*g ;  v = b2*v + ((1-b2)*g)*g
+ *   p = p - (m / (sqrt(v) / denom_scale[slot] + eps)) * ((1 / bias1[slot]) * lr_c)
+ * with every operation rounded separately (no FMA contraction). A state row
+ * whose stamp differs from its slot's stamp is read as m = v = 0 (cold
+ * restart after re-admission, gpu_resident_optimizer.py:249-261).
+ * Replaces the six _fused_resident_adam_kernel launches of step :474-499. */
+TGS_API int tgs_resident_adam_apply(const TgsResidentAdamArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* SelectiveAdam / SelectiveSophia (dense [N, W] groups + per-row mask)      */
+/* Replaces: optimizer.py:46-87 SelectiveAdam.step and                       */
+/*   submodules/clm_kernels/adam.cu:12-77 selective_adam_update (one launch  */
+/*   per group there, one launch for all groups here).                       */
+/* ------------------------------------------------------------------------ */
+
+#define TGS_MAX_GROUPS 16
+
+typedef struct {
+  float* param;        /* [N * width] contiguous */
+  const float* grad;   /* [N * width] */
+  float* exp_avg;      /* [N * width] (Sophia: m) */
+  float* exp_avg_sq;   /* [N * width] (Sophia: h, the Hessian-diagonal EMA) */
+  const float* noise;  /* Sophia only: [N * width] u ~ N(0,1) for the estimator */
+  int64_t width;       /* elements per row, = numel / N */
+  float lr, beta1, beta2, eps;
+  float rho;           /* Sophia clip scale */
+  float weight_decay;  /* Sophia decoupled weight decay (0 = off) */
+} TgsDenseGroup;
+
+typedef struct {
+  TgsDenseGroup groups[TGS_MAX_GROUPS];
+  int32_t n_groups;
+  const uint8_t* visibility;  /* [N] bool: row r is updated iff visibility[r] */
+  int64_t n_rows;             /* N */
+  int32_t hessian_step;       /* Sophia: 1 = update h from the estimator */
+} TgsDenseArgs;
+
+/* Reference arithmetic (adam.cu:33-37), no bias correction, no FMA:
+ *   m = b1*m + (1-b1)*g ; v = b2*v + ((1-b2)*g)*g ; p = p + ((-lr)*m)/(sqrt(v)+eps) */
+TGS_API int tgs_selective_adam(const TgsDenseArgs* args, void* stream);
+
+/* Sophia (Liu et al. 2023, Algorithm 3) on visible rows; no reference
+ * counterpart exists in TideGS:
+ *   m = b1*m + (1-b1)*g
+ *   if hessian_step: q = u*g ; h = b2*h + (1-b2)*(q*q)
+ *   if wd != 0: p = p - (lr*wd)*p
+ *   p = p - lr * clamp(m / max(rho*h, eps), -1, 1)                         */
+TGS_API int tgs_sophia_step(const TgsDenseArgs* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Materialization                                                           */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  const float* packed;                 /* [n_rows, 59] device, TGS_LAYOUT_* */
+  int64_t n_rows;
+  int32_t layout;
+  float* comp[TGS_NUM_COMPONENTS];     /* [*, W_c] SoA targets */
+  int64_t target_offset;               /* first target row */
+  /* Optional global-id fill (global_ids == NULL to skip): row r of the batch
+   * gets block_ids[r / block_size] * block_size + r % block_size. */
+  int64_t* global_ids;                 /* [*] written at target_offset + r */
+  const int64_t* block_ids;            /* [ceil(n_rows / block_size)] */
+  int64_t block_size;
+  int32_t* err;                        /* [4] device error word (may be NULL) */
+} TgsUnpackArgs;
+
+/* Packed [rows,59] -> six SoA components (+ global ids), TMA bulk tile loads.
+ * Replaces double_buffer_gpu.py:150-209 _unpack_streamed_rows_kernel and
+ * :130-148 _fill_cold_global_ids_kernel (fused). */
+TGS_API int tgs_unpack_rows(const TgsUnpackArgs* args, void* stream);
+
+typedef struct {
+  const float* src_comp[TGS_NUM_COMPONENTS]; /* source SoA components */
+  const int64_t* src_global_ids;             /* may be NULL (then not copied) */
+  float* dst_comp[TGS_NUM_COMPONENTS];
+  int64_t* dst_global_ids;                   /* may be NULL */
+  const int64_t* src_start;   /* [n_blocks] first source row of block k */
+  const int64_t* dst_start;   /* [n_blocks] first target row of block k */
+  const int64_t* row_count;   /* [n_blocks] rows of block k */
+  int32_t n_blocks;
+  int64_t max_rows;           /* max(row_count) (grid sizing) */
+  int32_t* err;               /* [4] device error word (may be NULL) */
+} TgsCopyBlocksArgs;
+
+/* Block-granular slot remap: for each block, copies its rows of all six
+ * components and its global ids from source slice to target slice with TMA
+ * bulk copies (cp.async.bulk global->shared->global, no multicast) where the
+ * segment is 16-byte aligned, vector copies elsewhere.
+ * Replaces double_buffer_gpu.py:40-128 _copy_resident_rows_kernel /
+ * :811-872 _copy_resident_blocks. */
+TGS_API int tgs_copy_blocks(const TgsCopyBlocksArgs* args, void* stream);
+
+/* dst[offset + r] = block_ids[r / block_size] * block_size + r % block_size
+ * for r < n_rows. Replaces double_buffer_gpu.py:130-148 / :924-961. */
+TGS_API int tgs_fill_global_ids(int64_t* dst, int64_t offset, const int64_t* block_ids,
+                        int64_t n_rows, int64_t block_size, void* stream);
+
+/* block_starts[k] = -1 for all k < num_blocks, then block_starts[ids[i]] =
+ * starts[i] for ids in range. Replaces double_buffer_gpu.py:212-234. */
+TGS_API int tgs_build_block_starts(int64_t* block_starts, int64_t num_blocks,
+                           const int64_t* ids, const int64_t* starts,
+                           int64_t n, void* stream);
+
+/* out[i] = block_starts[b] + (g - b*block_size) with b = floor(g/block_size)
+ * when 0 <= b < num_blocks and block_starts[b] >= 0, else -1.
+ * Replaces double_buffer_gpu.py:237-256 _global_ids_to_local and
+ * gpu_working_set.py:312-333 global_to_local. */
+TGS_API int tgs_global_to_local(int64_t* out, const int64_t* global_ids, int64_t n,
+                        const int64_t* block_starts, int64_t num_blocks,
+                        int64_t block_size, void* stream);
+
+/* Order-preserving compaction of global_to_local: writes only the ids that
+ * map to a resident row (>= 0), in input order, to out; *dev_count receives
+ * their number. scratch must hold tgs_compact_scratch_words(n) int64 words.
+ * Replaces `filter_local[filter_local >= 0]` at double_buffer_gpu.py:1145-1157. */
+TGS_API int64_t tgs_compact_scratch_words(int64_t n);
+TGS_API int tgs_global_to_local_compact(int64_t* out, int64_t* dev_count,
+                                const int64_t* global_ids, int64_t n,
+                                const int64_t* block_starts, int64_t num_blocks,
+                                int64_t block_size, int64_t* scratch,
+                                void* stream);
+
+/* Issues one cudaMemcpyAsync per block (host -> device) so pinned host blocks
+ * reach the device staging buffer without a CPU-side pack. host_src[k] is a
+ * host pointer, dev_dst[k] a device pointer, bytes[k] the size (all host
+ * arrays). Replaces the torch.cat pack of storage/block_reader.py:55-87 +
+ * the single H2D at double_buffer_gpu.py:1053 when blocks are pinned. */
+TGS_API int tgs_h2d_blocks(void* const* dev_dst, const void* const* host_src,
+                   const int64_t* bytes, int32_t n, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Dirty tracking and write-back                                             */
+/* ------------------------------------------------------------------------ */
+
+/* Bit-packed dirty bitmap: bit (id & 31) of word id >> 5.
+ * value != 0 sets the bits of ids, value == 0 clears them.
+ * Replaces double_buffer_gpu.py:494-508 / :530-543 (bool bitmap index_fill_). */
+TGS_API int tgs_dirty_mark(uint32_t* bitmap, const int64_t* ids, int64_t n, int32_t value,
+                   void* stream);
+
+/* Order-preserving warp-ballot compaction: out_ids = [ids[i] for i if bit set],
+ * *dev_count = its length. Single CTA; n up to ~1M.
+ * Replaces double_buffer_gpu.py:510-523 dirty_blocks_for_eviction. */
+TGS_API int tgs_dirty_select(const uint32_t* bitmap, const int64_t* ids, int64_t n,
+                     int64_t* out_ids, int64_t* dev_count, void* stream);
+
+/* All set bits of the first num_blocks bits, ascending.
+ * Replaces double_buffer_gpu.py:525-528 dirty_blocks (nonzero). */
+TGS_API int tgs_dirty_list(const uint32_t* bitmap, int64_t num_blocks, int64_t* out_ids,
+                   int64_t* dev_count, void* stream);
+
+typedef struct {
+  const float* comp[TGS_NUM_COMPONENTS]; /* source SoA components */
+  const int64_t* src_start;   /* [n_plans] first source row of plan k */
+  const int64_t* row_count;   /* [n_plans] */
+  const int64_t* out_start;   /* [n_plans] first output row (exclusive cumsum) */
+  int32_t n_plans;
+  int64_t max_rows;           /* max(row_count) */
+  float* out;                 /* [sum rows, 59] CACHE layout */
+  int32_t layout;             /* output column order, normally TGS_LAYOUT_CACHE */
+} TgsPackArgs;
+
+/* SoA -> packed CACHE rows for write-back, AoS tile assembled in shared memory
+ * and written with TMA bulk stores where aligned.
+ * Replaces gpu_working_set.py:35-86 _pack_resident_rows_kernel (:948-967). */
+TGS_API int tgs_pack_rows(const TgsPackArgs* args, void* stream);
+
+/* bounds[k] = (min x, min y, min z, max x, max y, max z) over xyz rows
+ * [start[k], start[k]+count[k]). Replaces gpu_working_set.py:88-115
+ * _resident_block_bounds_kernel (:990-1061). */
+TGS_API int tgs_block_bounds(const float* xyz, const int64_t* start, const int64_t* count,
+                     int32_t n_plans, float* bounds, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TIDEGS_B200_H */

@@ -1,0 +1,76 @@
+"""CPU: the C-ABI library loads, exports every symbol include/tidegs_b200.h
+declares, and validates arguments on the host (no kernel launches here)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from tidegs_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "tidegs_b200.h"
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^TGS_API\s+[\w\s\*]+?\b(tgs_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_the_entry_points():
+    syms = declared_symbols()
+    assert "tgs_resident_adam_apply" in syms and "tgs_pack_rows" in syms
+    assert len(syms) >= 19
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert lib.tgs_version() == _lib.ABI_VERSION
+
+
+def test_bindings_cover_only_declared_symbols():
+    assert set(_lib.SIGNATURES) <= set(declared_symbols())
+
+
+def test_null_args_are_rejected_with_a_message():
+    lib = _lib.load()
+    assert lib.tgs_resident_adam_count(None, None) == 1
+    assert "NULL" in _lib.last_error()
+    assert lib.tgs_unpack_rows(None, None) == 1
+    with pytest.raises(RuntimeError, match="tgs_copy_blocks"):
+        _lib.call("tgs_copy_blocks", None, None)
+
+
+def test_empty_work_is_a_no_op_without_device():
+    lib = _lib.load()
+    args = _lib.DenseArgs()
+    args.n_groups = 0
+    args.n_rows = 0
+    assert lib.tgs_selective_adam(ctypes.byref(args), None) == 0
+    assert lib.tgs_fill_global_ids(None, 0, None, 0, 4, None) == 0
+    assert lib.tgs_block_bounds(None, None, None, 0, None, None) == 0
+    assert lib.tgs_compact_scratch_words(0) == 1
+    assert lib.tgs_compact_scratch_words(2049) == 3
+
+
+def test_struct_layouts_match_the_header_sizes():
+    # field counts mirror the C structs; offsets follow the platform C ABI
+    assert ctypes.sizeof(_lib.DenseGroup) == 5 * 8 + 8 + 6 * 4
+    assert ctypes.sizeof(_lib.DenseArgs) == 16 * ctypes.sizeof(_lib.DenseGroup) + 8 + 8 + 8 + 8
+    assert _lib.ResidentAdamArgs.lr.offset == 96
+    assert _lib.ResidentAdamArgs.batch_size.offset == 96 + 24 + 5 * 4
+
+
+def test_no_cpu_fallback_without_cuda():
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("CUDA present")
+    from tidegs_b200 import GPUResidentAdam
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        GPUResidentAdam(device="cuda")
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        GPUResidentAdam(device="cpu")

@@ -1,0 +1,27 @@
+"""tidegs_b200: B200-native (sm_100a) resident-block optimizer, slot
+materialization and dirty write-back for TideGS.
+
+Drop-in classes (same names and behaviour as the reference's):
+    GPUResidentAdam                      strategies/tide_engine/gpu_resident_optimizer.py
+    SelectiveAdam, ResidentAdamContext   optimizer.py
+    DoubleBufferGPUWorkingSet, GPUBuffer strategies/tide_engine/double_buffer_gpu.py
+    GPUWorkingSet, PendingBlockWriteback strategies/tide_engine/gpu_working_set.py
+plus SelectiveSophia (no reference counterpart) and PinnedBlockPool.
+
+All compute runs in libtidegs_b200.so (include/tidegs_b200.h); importing the
+package does not touch the GPU, constructing any class requires CUDA and the
+built library.
+"""
+from .block_reader import (BlockBatch, BlockLayout, BlockReader, PinnedBlockPool,
+                           UnifiedParamsBlockReader, parse_block_row_components)
+from .double_buffer_gpu import DoubleBufferGPUWorkingSet, GPUBuffer, ResidentHandoffResult
+from .gpu_resident_optimizer import GPUResidentAdam
+from .gpu_working_set import GPUWorkingSet, PendingBlockBounds, PendingBlockWriteback
+from .optimizer import ResidentAdamContext, SelectiveAdam, SelectiveSophia
+
+__all__ = [
+    "BlockBatch", "BlockLayout", "BlockReader", "PinnedBlockPool", "UnifiedParamsBlockReader",
+    "parse_block_row_components", "DoubleBufferGPUWorkingSet", "GPUBuffer",
+    "ResidentHandoffResult", "GPUResidentAdam", "GPUWorkingSet", "PendingBlockBounds",
+    "PendingBlockWriteback", "ResidentAdamContext", "SelectiveAdam", "SelectiveSophia",
+]

@@ -1,0 +1,517 @@
+// Optimizer kernels: GPU-resident Adam over resident block slots, and the
+// dense masked SelectiveAdam / SelectiveSophia steps.
+//
+// Reference behaviour followed:
+//   strategies/tide_engine/gpu_resident_optimizer.py:16-70   (per-element Adam math)
+//   strategies/tide_engine/gpu_resident_optimizer.py:266-337 (row->slot, step tables)
+//   submodules/clm_kernels/adam.cu:12-41                     (SelectiveAdam math)
+#include "tgs_common.cuh"
+
+namespace tgs {
+namespace {
+
+// First index p in [0, n) with a[p] > x (n if none).
+__device__ __forceinline__ int upper_bound_i64(const int64_t* __restrict__ a, int n, int64_t x) {
+  int lo = 0, hi = n;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(a + mid) > x) hi = mid; else lo = mid + 1;
+  }
+  return lo;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel A: validate ids and count touched rows per resident position.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) resident_count_kernel(
+    const int64_t* __restrict__ ids, int64_t n, int64_t param_rows,
+    const int64_t* __restrict__ pos_start, const int64_t* __restrict__ pos_end, int n_pos,
+    int32_t* __restrict__ pos_count, int32_t* __restrict__ err) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  int p = -1;
+  if (i < n) {
+    const int64_t id = ids[i];
+    int code = TGS_DEV_OK;
+    if (id < 0 || id >= param_rows) {
+      code = TGS_DEV_ID_OUT_OF_RANGE;
+    } else if (i > 0 && ids[i - 1] >= id) {
+      code = TGS_DEV_ID_NOT_SORTED;
+    } else {
+      p = upper_bound_i64(pos_end, n_pos, id);
+      if (p >= n_pos || __ldg(pos_start + p) > id) code = TGS_DEV_ID_NOT_RESIDENT;
+    }
+    if (code != TGS_DEV_OK) {
+      report_error(err, code, i);
+      p = -1;
+    }
+  }
+  // Rows are sorted, so a warp's rows fall in very few positions: aggregate
+  // per position before touching global memory.
+  const unsigned have = __ballot_sync(0xffffffffu, p >= 0);
+  if (p >= 0) {
+    const unsigned peers = __match_any_sync(have, p);
+    if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(pos_count + p, __popc(peers));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel B: per touched position, advance its slot's step and publish the
+// bias-correction pair of that step (table precomputed on the host in double
+// precision exactly as gpu_resident_optimizer.py:325-328 does).
+// ---------------------------------------------------------------------------
+__global__ void resident_slot_kernel(const int32_t* __restrict__ pos_count,
+                                     const int32_t* __restrict__ pos_slot, int n_pos,
+                                     int32_t* __restrict__ slot_step, float2* __restrict__ slot_bias,
+                                     const float2* __restrict__ table, int table_len,
+                                     const int32_t* __restrict__ err) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= n_pos || load_error(err) != 0) return;
+  if (pos_count[p] > 0) {
+    const int s = pos_slot[p];
+    const int t = slot_step[s] + 1;
+    slot_step[s] = t;
+    slot_bias[s] = table[t < table_len ? t : table_len - 1];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel C: fused 59-column resident Adam. One warp updates one row at a time:
+// lane l owns UNIFIED columns 2l and 2l+1, so the row's 512-byte (m,v) state
+// row is one fully coalesced float4 access per lane. A warp takes 32 rows,
+// resolves their slot/state row once (one row per lane, binary search over
+// the resident layout), then streams them U rows at a time with all loads of
+// the U rows issued before any store.
+// ---------------------------------------------------------------------------
+struct ResidentApplyParams {
+  float* param[kNumComp];
+  const float* grad[kNumComp];
+  float lr[kNumComp];
+  float beta1, beta2, omb1, omb2, eps, batch_size;
+  const int64_t* pos_start;
+  const int64_t* pos_end;
+  const int32_t* pos_slot;
+  int n_pos;
+  int64_t block_size;
+  const int64_t* ids;
+  int64_t n;
+  float4* state;
+  const uint32_t* slot_stamp;
+  const float2* slot_bias;
+  const int32_t* err;
+};
+
+constexpr int kApplyThreads = 256;
+constexpr int kApplyUnroll = 4;
+
+struct AdamScalars {
+  float beta1, beta2, omb1, omb2, eps, batch_size;
+};
+
+// Reference torch-fallback order (gpu_resident_optimizer.py:355-364), one
+// rounding per operation; step_scale = (1/bias1) * lr.
+__device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float graw,
+                                          const AdamScalars& h, float step_scale,
+                                          float denom_scale) {
+  const float g = fdiv(graw, h.batch_size);
+  m = fadd(fmul(h.beta1, m), fmul(h.omb1, g));
+  v = fadd(fmul(h.beta2, v), fmul(fmul(h.omb2, g), g));
+  const float denom = fadd(fdiv(fsqrt(v), denom_scale), h.eps);
+  p = fsub(p, fmul(fdiv(m, denom), step_scale));
+}
+
+// Selects entry c of a 6-entry kernel-parameter array with constant offsets
+// (a dynamic index would copy the whole parameter block to local memory).
+template <typename T>
+__device__ __forceinline__ T pick6(const T (&arr)[kNumComp], int c) {
+  switch (c) {
+    case 0: return arr[0];
+    case 1: return arr[1];
+    case 2: return arr[2];
+    case 3: return arr[3];
+    case 4: return arr[4];
+    default: return arr[5];
+  }
+}
+
+__global__ void __launch_bounds__(kApplyThreads, 3) resident_adam_kernel(const ResidentApplyParams a) {
+  if (load_error(a.err) != 0) return;
+  const int lane = threadIdx.x & 31;
+  const unsigned full = 0xffffffffu;
+  const AdamScalars hp = {a.beta1, a.beta2, a.omb1, a.omb2, a.eps, a.batch_size};
+
+  // Per-lane column bindings (fixed for the whole kernel).
+  const float* gbase[2];
+  float* pbase[2];
+  int width[2];
+  float lr[2];
+  bool act[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int j = 2 * lane + e;
+    act[e] = j < kRowWidth;
+    const int c = act[e] ? unified_comp_of(j) : 0;
+    const int k = act[e] ? j - unified_offset(c) : 0;
+    gbase[e] = pick6(a.grad, c) + k;
+    pbase[e] = pick6(a.param, c) + k;
+    width[e] = comp_width(c);
+    lr[e] = pick6(a.lr, c);
+  }
+
+  const int warps_per_cta = kApplyThreads / 32;
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * warps_per_cta + (threadIdx.x >> 5);
+  const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * warps_per_cta;
+
+  for (int64_t chunk = warp_id; chunk * 32 < a.n; chunk += warp_stride) {
+    const int64_t row0 = chunk * 32;
+    const int nr = static_cast<int>(min64(32, a.n - row0));
+
+    int64_t my_id = 0, my_sr = 0;
+    float my_b1 = 1.f, my_ds = 1.f;
+    uint32_t my_stamp = 0;
+    if (lane < nr) {
+      my_id = a.ids[row0 + lane];
+      const int p = upper_bound_i64(a.pos_end, a.n_pos, my_id);
+      const int s = __ldg(a.pos_slot + p);
+      my_sr = static_cast<int64_t>(s) * a.block_size + (my_id - __ldg(a.pos_start + p));
+      const float2 bb = a.slot_bias[s];
+      my_b1 = bb.x;
+      my_ds = bb.y;
+      my_stamp = __ldg(a.slot_stamp + s);
+    }
+
+    for (int r = 0; r < nr; r += kApplyUnroll) {
+      // Load phase: only the streamed operands stay live across the unrolled
+      // rows; row metadata is re-broadcast in the update phase (shuffles are
+      // cheaper than the registers they would pin).
+      float4 st[kApplyUnroll];
+      float g0[kApplyUnroll], g1[kApplyUnroll], p0[kApplyUnroll], p1[kApplyUnroll];
+#pragma unroll
+      for (int u = 0; u < kApplyUnroll; ++u) {
+        const int rr = r + u;  // warp-uniform
+        const int64_t id = __shfl_sync(full, my_id, rr & 31);
+        const int64_t sr = __shfl_sync(full, my_sr, rr & 31);
+        st[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        g0[u] = g1[u] = p0[u] = p1[u] = 0.f;
+        if (rr < nr) {
+          const int64_t gi = row0 + rr;
+          st[u] = a.state[sr * 32 + lane];
+          if (act[0]) {
+            g0[u] = gbase[0][gi * width[0]];
+            p0[u] = pbase[0][id * width[0]];
+          }
+          if (act[1]) {
+            g1[u] = gbase[1][gi * width[1]];
+            p1[u] = pbase[1][id * width[1]];
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kApplyUnroll; ++u) {
+        const int rr = r + u;
+        if (rr >= nr) break;  // warp-uniform
+        const int64_t id = __shfl_sync(full, my_id, rr);
+        const int64_t sr = __shfl_sync(full, my_sr, rr);
+        const float b1 = __shfl_sync(full, my_b1, rr);
+        const float ds = __shfl_sync(full, my_ds, rr);
+        const uint32_t stamp = __shfl_sync(full, my_stamp, rr);
+        // A row whose stamp is not its slot's current stamp has not been
+        // touched since the block was (re)admitted: its moments are zero.
+        const bool fresh =
+            __shfl_sync(full, __float_as_uint(st[u].x) == stamp ? 1 : 0, 31) != 0;
+        float m0 = fresh ? st[u].x : 0.f, v0 = fresh ? st[u].y : 0.f;
+        float m1 = fresh ? st[u].z : 0.f, v1 = fresh ? st[u].w : 0.f;
+        const float inv_b1 = fdiv(1.0f, b1);
+        if (act[0]) adam_elem(p0[u], m0, v0, g0[u], hp, fmul(inv_b1, lr[0]), ds);
+        if (act[1]) adam_elem(p1[u], m1, v1, g1[u], hp, fmul(inv_b1, lr[1]), ds);
+        float4 out;
+        if (lane < 29) {
+          out = make_float4(m0, v0, m1, v1);
+        } else if (lane == 29) {
+          out = make_float4(m0, v0, 0.f, 0.f);
+        } else if (lane == 30) {
+          out = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+          out = make_float4(__uint_as_float(stamp), 0.f, 0.f, 0.f);
+        }
+        a.state[sr * 32 + lane] = out;
+        if (act[0]) pbase[0][id * width[0]] = p0[u];
+        if (act[1]) pbase[1][id * width[1]] = p1[u];
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dense masked optimizers (SelectiveAdam, SelectiveSophia). All groups run in
+// one launch: CTAs [cta_begin[g], cta_begin[g+1]) serve group g. A thread
+// handles 4 consecutive elements (one float4 when the group is 16-byte
+// aligned); the row of the first element comes from a multiply-high by a
+// precomputed reciprocal, the others by increment.
+// ---------------------------------------------------------------------------
+struct DenseGroupParams {
+  float* param;
+  const float* grad;
+  float* m;
+  float* v;
+  const float* noise;
+  int64_t width;
+  uint64_t magic;  // floor(2^64 / width) + 1, valid for width >= 2
+  int64_t total;   // N * width
+  float lr, beta1, beta2, omb1, omb2, eps, rho, wd;
+  int vec_ok;
+};
+
+struct DenseParams {
+  DenseGroupParams g[TGS_MAX_GROUPS];
+  int cta_begin[TGS_MAX_GROUPS + 1];
+  int n_groups;
+  const uint8_t* vis;
+  int hessian_step;
+};
+
+constexpr int kDenseThreads = 256;
+constexpr int kDenseVecPerThread = 4;
+
+__device__ __forceinline__ void selective_adam_elem(float& p, float& m, float& v, float g,
+                                                    const DenseGroupParams& G) {
+  m = fadd(fmul(G.beta1, m), fmul(G.omb1, g));
+  v = fadd(fmul(G.beta2, v), fmul(fmul(G.omb2, g), g));
+  const float step = fdiv(fmul(-G.lr, m), fadd(fsqrt(v), G.eps));
+  p = fadd(p, step);
+}
+
+__device__ __forceinline__ void sophia_elem(float& p, float& m, float& h, float g, float u,
+                                            bool hess, const DenseGroupParams& G) {
+  m = fadd(fmul(G.beta1, m), fmul(G.omb1, g));
+  if (hess) {
+    const float q = fmul(u, g);
+    h = fadd(fmul(G.beta2, h), fmul(G.omb2, fmul(q, q)));
+  }
+  if (G.wd != 0.f) p = fsub(p, fmul(fmul(G.lr, G.wd), p));
+  float ratio = fdiv(m, fmaxf(fmul(G.rho, h), G.eps));
+  ratio = fminf(fmaxf(ratio, -1.f), 1.f);
+  p = fsub(p, fmul(G.lr, ratio));
+}
+
+template <bool kSophia>
+__global__ void __launch_bounds__(kDenseThreads) dense_kernel(const DenseParams a) {
+  int gi = 0;
+#pragma unroll 1
+  while (gi + 1 < a.n_groups && static_cast<int>(blockIdx.x) >= a.cta_begin[gi + 1]) ++gi;
+  const DenseGroupParams& G = a.g[gi];
+  const int64_t local_cta = static_cast<int64_t>(blockIdx.x) - a.cta_begin[gi];
+  const int64_t ctas = a.cta_begin[gi + 1] - a.cta_begin[gi];
+  const int64_t nvec = (G.total + 3) / 4;
+  const bool hess = kSophia && a.hessian_step != 0;
+
+  for (int64_t q = local_cta * kDenseThreads + threadIdx.x; q < nvec;
+       q += ctas * kDenseThreads) {
+    const int64_t e0 = q * 4;
+    int64_t row = G.width == 1 ? e0 : static_cast<int64_t>(__umul64hi(static_cast<uint64_t>(e0), G.magic));
+    int64_t col = e0 - row * G.width;
+    bool vis[4];
+    bool any = false;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const bool in = e0 + k < G.total;
+      vis[k] = in && a.vis[row] != 0;
+      any |= vis[k];
+      if (++col == G.width) {
+        col = 0;
+        ++row;
+      }
+    }
+    if (!any) continue;
+    float pv[4], gv[4], mv[4], vv[4], uv[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool full_vec = G.vec_ok && e0 + 4 <= G.total;
+    if (full_vec) {
+      const float4 p4 = *reinterpret_cast<const float4*>(G.param + e0);
+      const float4 g4 = *reinterpret_cast<const float4*>(G.grad + e0);
+      const float4 m4 = *reinterpret_cast<const float4*>(G.m + e0);
+      const float4 v4 = *reinterpret_cast<const float4*>(G.v + e0);
+      pv[0] = p4.x; pv[1] = p4.y; pv[2] = p4.z; pv[3] = p4.w;
+      gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+      mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
+      vv[0] = v4.x; vv[1] = v4.y; vv[2] = v4.z; vv[3] = v4.w;
+      if (hess) {
+        const float4 u4 = *reinterpret_cast<const float4*>(G.noise + e0);
+        uv[0] = u4.x; uv[1] = u4.y; uv[2] = u4.z; uv[3] = u4.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        pv[k] = gv[k] = mv[k] = vv[k] = 0.f;
+        if (vis[k]) {
+          pv[k] = G.param[e0 + k];
+          gv[k] = G.grad[e0 + k];
+          mv[k] = G.m[e0 + k];
+          vv[k] = G.v[e0 + k];
+          if (hess) uv[k] = G.noise[e0 + k];
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (!vis[k]) continue;
+      if (kSophia) sophia_elem(pv[k], mv[k], vv[k], gv[k], uv[k], hess, G);
+      else selective_adam_elem(pv[k], mv[k], vv[k], gv[k], G);
+    }
+    if (full_vec) {
+      // Invisible lanes carry their unchanged values back.
+      *reinterpret_cast<float4*>(G.param + e0) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+      *reinterpret_cast<float4*>(G.m + e0) = make_float4(mv[0], mv[1], mv[2], mv[3]);
+      *reinterpret_cast<float4*>(G.v + e0) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (!vis[k]) continue;
+        G.param[e0 + k] = pv[k];
+        G.m[e0 + k] = mv[k];
+        G.v[e0 + k] = vv[k];
+      }
+    }
+  }
+}
+
+int launch_dense(const TgsDenseArgs* args, void* stream, bool sophia) {
+  const char* who = sophia ? "tgs_sophia_step" : "tgs_selective_adam";
+  TGS_CHECK_ARG(args != nullptr, "%s: args is NULL", who);
+  TGS_CHECK_ARG(args->n_groups >= 0 && args->n_groups <= TGS_MAX_GROUPS,
+                "%s: n_groups=%d outside [0, %d]", who, args->n_groups, TGS_MAX_GROUPS);
+  TGS_CHECK_ARG(args->n_rows >= 0, "%s: n_rows=%lld < 0", who, (long long)args->n_rows);
+  if (args->n_rows == 0 || args->n_groups == 0) return TGS_OK;
+  TGS_CHECK_ARG(args->visibility != nullptr, "%s: visibility is NULL", who);
+
+  DenseParams p;
+  memset(&p, 0, sizeof(p));
+  p.n_groups = args->n_groups;
+  p.vis = args->visibility;
+  p.hessian_step = args->hessian_step;
+  int64_t cta_total = 0;
+  for (int gi = 0; gi < args->n_groups; ++gi) {
+    const TgsDenseGroup& in = args->groups[gi];
+    DenseGroupParams& G = p.g[gi];
+    TGS_CHECK_ARG(in.param && in.grad && in.exp_avg && in.exp_avg_sq,
+                  "%s: group %d has a NULL tensor", who, gi);
+    TGS_CHECK_ARG(in.width >= 1 && in.width <= (1 << 20), "%s: group %d width=%lld invalid", who,
+                  gi, (long long)in.width);
+    TGS_CHECK_ARG(!(sophia && args->hessian_step && in.noise == nullptr),
+                  "%s: group %d needs a noise tensor on a Hessian step", who, gi);
+    G.param = in.param;
+    G.grad = in.grad;
+    G.m = in.exp_avg;
+    G.v = in.exp_avg_sq;
+    G.noise = in.noise;
+    G.width = in.width;
+    G.magic = in.width >= 2 ? (~0ull / static_cast<uint64_t>(in.width)) + 1ull : 0ull;
+    G.total = args->n_rows * in.width;
+    TGS_CHECK_ARG(G.total < (1ll << 44), "%s: group %d too large", who, gi);
+    G.lr = in.lr;
+    G.beta1 = in.beta1;
+    G.beta2 = in.beta2;
+    // (1 - b) rounded in fp32, as the reference computes it in device fp32.
+    G.omb1 = 1.0f - in.beta1;
+    G.omb2 = 1.0f - in.beta2;
+    G.eps = in.eps;
+    G.rho = in.rho;
+    G.wd = in.weight_decay;
+    G.vec_ok = aligned16(in.param) && aligned16(in.grad) && aligned16(in.exp_avg) &&
+               aligned16(in.exp_avg_sq) && (!sophia || in.noise == nullptr || aligned16(in.noise));
+    const int64_t nvec = (G.total + 3) / 4;
+    const int64_t ctas = std::max<int64_t>(
+        1, ceil_div<int64_t>(nvec, static_cast<int64_t>(kDenseThreads) * kDenseVecPerThread));
+    p.cta_begin[gi] = static_cast<int>(cta_total);
+    cta_total += ctas;
+  }
+  TGS_CHECK_ARG(cta_total < (1ll << 31), "%s: grid too large", who);
+  p.cta_begin[args->n_groups] = static_cast<int>(cta_total);
+  cudaStream_t s = as_stream(stream);
+  if (sophia) dense_kernel<true><<<static_cast<unsigned>(cta_total), kDenseThreads, 0, s>>>(p);
+  else dense_kernel<false><<<static_cast<unsigned>(cta_total), kDenseThreads, 0, s>>>(p);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+}  // namespace
+}  // namespace tgs
+
+using namespace tgs;
+
+extern "C" int tgs_resident_adam_count(const TgsResidentCountArgs* a, void* stream) {
+  TGS_CHECK_ARG(a != nullptr, "tgs_resident_adam_count: args is NULL");
+  TGS_CHECK_ARG(a->n_positions >= 1, "tgs_resident_adam_count: working set contains no resident blocks");
+  TGS_CHECK_ARG(a->n_rows >= 0 && a->block_size >= 1 && a->param_rows >= 0,
+                "tgs_resident_adam_count: bad sizes n=%lld block=%lld rows=%lld",
+                (long long)a->n_rows, (long long)a->block_size, (long long)a->param_rows);
+  TGS_CHECK_ARG(a->pos_start && a->pos_end && a->pos_slot && a->pos_count && a->err &&
+                    a->slot_step && a->slot_bias && a->step_table && a->step_table_len >= 2,
+                "tgs_resident_adam_count: NULL table or step_table_len < 2");
+  TGS_CHECK_ARG(a->n_rows == 0 || a->local_ids != nullptr, "tgs_resident_adam_count: local_ids is NULL");
+  cudaStream_t s = as_stream(stream);
+  TGS_CUDA(cudaMemsetAsync(a->pos_count, 0, sizeof(int32_t) * a->n_positions, s));
+  TGS_CUDA(cudaMemsetAsync(a->err, 0, sizeof(int32_t) * 4, s));
+  if (a->n_rows == 0) return TGS_OK;
+  const int64_t blocks = ceil_div<int64_t>(a->n_rows, 256);
+  TGS_CHECK_ARG(blocks < (1ll << 31), "tgs_resident_adam_count: n_rows too large");
+  resident_count_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+      a->local_ids, a->n_rows, a->param_rows, a->pos_start, a->pos_end, a->n_positions,
+      a->pos_count, a->err);
+  TGS_LAUNCH_CHECK();
+  resident_slot_kernel<<<ceil_div(a->n_positions, 256), 256, 0, s>>>(
+      a->pos_count, a->pos_slot, a->n_positions, a->slot_step,
+      reinterpret_cast<float2*>(a->slot_bias), reinterpret_cast<const float2*>(a->step_table),
+      a->step_table_len, a->err);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* stream) {
+  TGS_CHECK_ARG(a != nullptr, "tgs_resident_adam_apply: args is NULL");
+  if (a->n_rows == 0) return TGS_OK;
+  TGS_CHECK_ARG(a->n_rows > 0 && a->n_positions >= 1 && a->block_size >= 1,
+                "tgs_resident_adam_apply: bad sizes");
+  TGS_CHECK_ARG(a->local_ids && a->pos_start && a->pos_end && a->pos_slot && a->state &&
+                    a->slot_stamp && a->slot_bias && a->err,
+                "tgs_resident_adam_apply: NULL pointer");
+  TGS_CHECK_ARG(aligned16(a->state), "tgs_resident_adam_apply: state must be 16-byte aligned");
+  TGS_CHECK_ARG(a->batch_size != 0.0f, "tgs_resident_adam_apply: batch_size is 0");
+  ResidentApplyParams p;
+  for (int c = 0; c < kNumComp; ++c) {
+    TGS_CHECK_ARG(a->param[c] && a->grad[c], "tgs_resident_adam_apply: component %d is NULL", c);
+    p.param[c] = a->param[c];
+    p.grad[c] = a->grad[c];
+    p.lr[c] = a->lr[c];
+  }
+  p.beta1 = a->beta1;
+  p.beta2 = a->beta2;
+  p.omb1 = a->one_minus_beta1;
+  p.omb2 = a->one_minus_beta2;
+  p.eps = a->eps;
+  p.batch_size = a->batch_size;
+  p.pos_start = a->pos_start;
+  p.pos_end = a->pos_end;
+  p.pos_slot = a->pos_slot;
+  p.n_pos = a->n_positions;
+  p.block_size = a->block_size;
+  p.ids = a->local_ids;
+  p.n = a->n_rows;
+  p.state = reinterpret_cast<float4*>(a->state);
+  p.slot_stamp = a->slot_stamp;
+  p.slot_bias = reinterpret_cast<const float2*>(a->slot_bias);
+  p.err = a->err;
+  const int64_t warps_needed = ceil_div<int64_t>(a->n_rows, 32);
+  const int64_t ctas_needed = ceil_div<int64_t>(warps_needed, kApplyThreads / 32);
+  const int64_t cap = static_cast<int64_t>(sm_count()) * 3;
+  const int grid = static_cast<int>(std::min<int64_t>(ctas_needed, cap));
+  resident_adam_kernel<<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+extern "C" int tgs_selective_adam(const TgsDenseArgs* args, void* stream) {
+  return launch_dense(args, stream, false);
+}
+
+extern "C" int tgs_sophia_step(const TgsDenseArgs* args, void* stream) {
+  return launch_dense(args, stream, true);
+}

@@ -44,6 +44,15 @@ UNIT = "Gaussian updates/s"
 B = 16384
 SLOTS = 2048
 TURNOVER = 512
+
+
+def set_slots(slots: int) -> None:
+    """Resident slots per GPU; the turnover stays at 25 % of them."""
+    global SLOTS, TURNOVER
+    SLOTS = int(slots)
+    TURNOVER = max(1, SLOTS // 4)
+
+
 WIDTHS = {"xyz": 3, "opacity": 1, "scaling": 3, "rotation": 4, "features_dc": 3,
           "features_rest": 45}
 NAMES = tuple(WIDTHS)
@@ -165,9 +174,10 @@ class Schedule:
         """Union over 16 cameras of contiguous runs of slots, ~30 % visible."""
         rng = np.random.default_rng(10_000 + step % self.n_sets)
         vis = np.zeros(SLOTS, bool)
+        scale = SLOTS / 2048.0
         for _ in range(16):
-            length = int(rng.integers(24, 56))
-            start = int(rng.integers(0, SLOTS - length))
+            length = max(1, int(rng.integers(24, 56) * scale))
+            start = int(rng.integers(0, max(1, SLOTS - length)))
             vis[start:start + length] = True
         return np.nonzero(vis)[0]
 
@@ -329,10 +339,23 @@ class DeviceStep:
         return ms, rows
 
 
+class _Skipped(Exception):
+    pass
+
+
 # ---------------------------------------------------------------------------
 # e2e leg: Python drop-in classes, host pool -> HBM -> host
 # ---------------------------------------------------------------------------
 class ApiStep:
+    profile = None
+
+    def _mark(self, name, t):
+        if self.profile is not None:
+            now = time.perf_counter()
+            self.profile[name] = self.profile.get(name, 0.0) + now - t
+            return now
+        return t
+
     def __init__(self, device, sched: Schedule, pool_blocks: int):
         import types
 
@@ -394,6 +417,7 @@ class ApiStep:
 
     def step(self, k: int) -> int:
         db, ws = self.db, self.ws
+        t = time.perf_counter()
         loaded = list(db.active_buffer.loaded_blocks)
         # visible rows: the blocks at visible slice positions of the active buffer
         pos = self.sched.visible_positions(k)
@@ -402,9 +426,11 @@ class ApiStep:
         n = ids_host.size
         grads = {name: g[:n] for name, g in self.grads.items()}
         stats = self.opt.step(k, self.gaussians, ids, grads)
+        t = self._mark("adam_step", t)
         updated = stats["updated_block_ids"]
         db.mark_dirty_blocks(updated)
         bounds = ws.stage_block_bounds(updated)
+        t = self._mark("dirty_mark_bounds", t)
         # turnover: evict 512 of the loaded blocks, stream 512 new ones
         rng = np.random.default_rng(30_000 + k)
         evict_idx = rng.choice(len(loaded), TURNOVER, replace=False)
@@ -413,24 +439,33 @@ class ApiStep:
         cand = [b for b in self.sched.pool_ids.tolist() if b not in resident]
         incoming = sorted(rng.choice(cand, TURNOVER, replace=False).tolist())
         keep = sorted(resident - set(evicted))
+        t = self._mark("plan", t)
         db.start_prefetch(iteration=k + 1, visible_block_ids=keep + incoming,
                           resident_block_ids=keep, evicted_block_ids=evicted,
                           block_reader=self.pool, defer_resident_copy=True)
+        t = self._mark("start_prefetch", t)
         wb_ids = db.dirty_blocks_for_eviction(evicted)
+        t = self._mark("dirty_select", t)
         pending = ws.stage_updated_blocks(wb_ids)
+        t = self._mark("stage_writeback", t)
         if pending is not None:
             payload = pending.wait()
-            self.d2h_bytes += sum(t.numel() * 4 for t in payload.values())
+            self.d2h_bytes += sum(v.numel() * 4 for v in payload.values())
             pending.release()
+        t = self._mark("writeback_wait", t)
         db.mark_blocks_written_back(wb_ids)
         if bounds is not None:
             bounds.wait()
             self.d2h_bytes += bounds.cpu_bounds.numel() * 4
         db.finalize_retained_blocks(keep, target="loading")
+        t = self._mark("bounds_finalize", t)
         db.wait_for_prefetch(k + 1)
+        t = self._mark("wait_prefetch", t)
         db.swap_buffers()
+        t = self._mark("swap", t)
         self._activate()
         self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
+        self._mark("activate", t)
         self.h2d_bytes += TURNOVER * B * 59 * 4 + ids_host.nbytes
         return n
 
@@ -515,11 +550,19 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="tidegs_b200", choices=["tidegs_b200", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=4)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--e2e-warmup", type=int, default=3)
+    ap.add_argument("--e2e-profile", action="store_true",
+                    help="print a per-phase wall-time breakdown of the e2e step to stderr")
     ap.add_argument("--pool-blocks", type=int, default=1024)
+    ap.add_argument("--slots", type=int, default=SLOTS,
+                    help="resident slots per GPU (default: the configs[3] value; smaller "
+                         "values make small profiling cases of the same step)")
+    ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
+    set_slots(args.slots)
     world, rank, local = dist_setup()
     if args.impl == "reference":
         return run_reference_arm(args, world, rank)
@@ -562,16 +605,20 @@ def main(argv=None):
     # e2e leg through the Python API (host pool -> HBM -> host)
     e2e = None
     try:
+        if args.no_e2e:
+            raise _Skipped("--no-e2e")
         api = ApiStep(device, sched, args.pool_blocks)
-        api.step(0)
+        for k in range(args.e2e_warmup):
+            api.step(k)
         torch.cuda.synchronize()
         barrier(world)
         api.h2d_bytes = api.d2h_bytes = 0
+        api.profile = {} if args.e2e_profile else None
         e_rows = 0
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
-        for k in range(1, 1 + args.e2e_steps):
+        for k in range(args.e2e_warmup, args.e2e_warmup + args.e2e_steps):
             e_rows += api.step(k)
         t1.record()
         torch.cuda.synchronize()
@@ -581,7 +628,13 @@ def main(argv=None):
                "d2h_bytes_per_step": int(api.d2h_bytes / args.e2e_steps),
                "ms_per_step": e_ms / args.e2e_steps, "steps": args.e2e_steps,
                "host_pool_blocks": args.pool_blocks}
+        if api.profile is not None and rank == 0:
+            print("e2e phase wall ms/step: " + json.dumps(
+                {k: round(v * 1e3 / args.e2e_steps, 2) for k, v in api.profile.items()}),
+                file=sys.stderr, flush=True)
         del api
+    except _Skipped as why:
+        e2e = {"value": None, "unit": UNIT, "skipped": str(why)}
     except Exception as exc:  # report, never hide
         e2e = {"value": None, "unit": UNIT, "error": f"{type(exc).__name__}: {exc}"}
 

@@ -276,6 +276,23 @@ TGS_API int tgs_global_to_local_compact(int64_t* out, int64_t* dev_count,
                                 int64_t block_size, int64_t* scratch,
                                 void* stream);
 
+/* Same result as tgs_global_to_local_compact, but the call allocates nothing
+ * and takes no scratch argument. It has no counterpart in the reference.
+ * It serves callers that cannot provide scratch device memory when they call:
+ * an engine that lays out all of its device memory once at start-up has no
+ * allocator to call, and cudaMalloc/cudaFree on the fly would synchronize the
+ * device in the middle of an overlapped pipeline. The scratch lives in a
+ * fixed array inside the library (128 KiB per device, held until the process
+ * exits), which bounds n to 33,554,432 ids; larger n is rejected with
+ * TGS_ERR_INVALID_ARG and a message. The first call on a device looks up the
+ * array's device address (with that device current); make that first call
+ * before any stream capture. All calls on a device share the array, so calls
+ * that overlap on the GPU race: serialize them. */
+TGS_API int tgs_global_to_local_compact_noalloc(int64_t* out, int64_t* dev_count,
+                                                const int64_t* global_ids, int64_t n,
+                                                const int64_t* block_starts, int64_t num_blocks,
+                                                int64_t block_size, void* stream);
+
 /* Issues one cudaMemcpyAsync per block (host -> device) so pinned host blocks
  * reach the device staging buffer without a CPU-side pack. host_src[k] is a
  * host pointer, dev_dst[k] a device pointer, bytes[k] the size (all host

@@ -113,6 +113,7 @@ SIGNATURES = {
     "tgs_global_to_local": (C.c_int, [_vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "tgs_compact_scratch_words": (_i64, [_i64]),
     "tgs_global_to_local_compact": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp]),
+    "tgs_global_to_local_compact_noalloc": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "tgs_h2d_blocks": (C.c_int, [C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_i64), _i32, _vp]),
     "tgs_dirty_mark": (C.c_int, [_vp, _vp, _i64, _i32, _vp]),
     "tgs_dirty_select": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
@@ -163,6 +164,7 @@ KERNELS_PER_CALL = {
     "tgs_resident_adam_count": 2, "tgs_resident_adam_apply": 1, "tgs_selective_adam": 1,
     "tgs_sophia_step": 1, "tgs_unpack_rows": 1, "tgs_copy_blocks": 1, "tgs_fill_global_ids": 1,
     "tgs_build_block_starts": 1, "tgs_global_to_local": 1, "tgs_global_to_local_compact": 3,
+    "tgs_global_to_local_compact_noalloc": 3,
     "tgs_dirty_mark": 1, "tgs_dirty_select": 1, "tgs_dirty_list": 1, "tgs_pack_rows": 1,
     "tgs_block_bounds": 1,
 }

@@ -7,6 +7,8 @@
 //   strategies/tide_engine/double_buffer_gpu.py:150-209  _unpack_streamed_rows_kernel
 //   strategies/tide_engine/double_buffer_gpu.py:212-256  block starts / global->local
 //   strategies/tide_engine/gpu_working_set.py:35-115     pack + bounds kernels
+#include <mutex>
+
 #include "tgs_common.cuh"
 
 namespace tgs {
@@ -681,6 +683,88 @@ extern "C" int tgs_global_to_local_compact(int64_t* out, int64_t* dev_count,
                 "tgs_global_to_local_compact: NULL pointer");
   const int64_t tiles = ceil_div<int64_t>(n, kCompactTile);
   TGS_CHECK_ARG(tiles < (1ll << 31), "tgs_global_to_local_compact: n too large");
+  g2l_count_kernel<<<static_cast<unsigned>(tiles), kCompactThreads, 0, s>>>(
+      global_ids, n, block_starts, num_blocks, block_size, scratch);
+  TGS_LAUNCH_CHECK();
+  scan_counts_kernel<<<1, 1024, 0, s>>>(scratch, tiles, dev_count);
+  TGS_LAUNCH_CHECK();
+  g2l_write_kernel<<<static_cast<unsigned>(tiles), kCompactThreads, 0, s>>>(
+      out, global_ids, n, block_starts, num_blocks, block_size, scratch);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free global->local compaction.
+//
+// Some callers cannot hand us scratch memory: an engine whose device memory is
+// laid out once at start-up has no allocator left to call, and allocating or
+// freeing on the fly (cudaMalloc / cudaFree) would synchronize the whole
+// device in the middle of a pipeline that overlaps copies and kernels. This
+// variant of tgs_global_to_local_compact keeps its per-tile scratch in a fixed
+// array compiled into the library instead: one int64 word per 2048-id tile,
+// for at most kNoAllocMaxIds ids (16,385 words = 128 KiB). Every GPU that
+// loads the library holds that array until the process exits.
+//
+// The array is shared by every call on a device and keeps the previous call's
+// contents. Nothing in it has to start at zero: each call writes every tile
+// count it later reads, then their prefix sums. Calls whose work overlaps on
+// the GPU (two streams, or two host threads) race on the array and must be
+// serialized by the caller.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kNoAllocMaxIds = int64_t(1) << 25;  // 33,554,432 ids
+constexpr int64_t kNoAllocScratchWords = kNoAllocMaxIds / kCompactTile + 1;
+}  // namespace
+
+static __device__ __align__(256) int64_t g_noalloc_compact_scratch[kNoAllocScratchWords];
+
+namespace {
+std::mutex g_noalloc_mutex;
+int64_t* g_noalloc_scratch_ptr[64] = {nullptr};
+
+// Device address of the fixed scratch array on the current device. Host code
+// must not use the array's name as a device pointer: it is only a host-side
+// stand-in, so the address is looked up once per device, with that device
+// current.
+int noalloc_scratch(int64_t** out) {
+  int dev = -1;
+  TGS_CUDA(cudaGetDevice(&dev));
+  TGS_CHECK_ARG(dev >= 0 && dev < 64, "tgs_global_to_local_compact_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    TGS_CUDA(cudaGetSymbolAddress(&p, g_noalloc_compact_scratch));
+    g_noalloc_scratch_ptr[dev] = static_cast<int64_t*>(p);
+  }
+  *out = g_noalloc_scratch_ptr[dev];
+  return TGS_OK;
+}
+}  // namespace
+
+extern "C" int tgs_global_to_local_compact_noalloc(int64_t* out, int64_t* dev_count,
+                                                   const int64_t* global_ids, int64_t n,
+                                                   const int64_t* block_starts,
+                                                   int64_t num_blocks, int64_t block_size,
+                                                   void* stream) {
+  TGS_CHECK_ARG(n >= 0 && num_blocks >= 1 && block_size >= 1,
+                "tgs_global_to_local_compact_noalloc: bad sizes");
+  TGS_CHECK_ARG(n <= kNoAllocMaxIds,
+                "tgs_global_to_local_compact_noalloc: n=%lld ids exceeds the fixed scratch "
+                "limit of %lld ids; use tgs_global_to_local_compact with caller scratch",
+                (long long)n, (long long)kNoAllocMaxIds);
+  TGS_CHECK_ARG(dev_count != nullptr, "tgs_global_to_local_compact_noalloc: dev_count is NULL");
+  TGS_CHECK_ARG(n == 0 || (out && global_ids && block_starts),
+                "tgs_global_to_local_compact_noalloc: NULL pointer");
+  int64_t* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != TGS_OK) return rc;
+  cudaStream_t s = as_stream(stream);
+  if (n == 0) {
+    TGS_CUDA(cudaMemsetAsync(dev_count, 0, sizeof(int64_t), s));
+    return TGS_OK;
+  }
+  const int64_t tiles = ceil_div<int64_t>(n, kCompactTile);
   g2l_count_kernel<<<static_cast<unsigned>(tiles), kCompactThreads, 0, s>>>(
       global_ids, n, block_starts, num_blocks, block_size, scratch);
   TGS_LAUNCH_CHECK();

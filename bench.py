@@ -394,7 +394,12 @@ class ApiStep:
                                             param_groups=[{"betas": (0.9, 0.999), "eps": 1e-15}]))
         self._activate()
         self.opt.set_resident_blocks(order)
-        max_rows = max(sched.visible_positions(s).size for s in range(sched.n_sets)) * B
+        self.ids_pinned = []
+        for s_ in range(sched.n_sets):
+            pos = sched.visible_positions(s_)
+            ids_np = (pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)
+            self.ids_pinned.append(torch.from_numpy(ids_np).pin_memory())
+        max_rows = max(t.numel() for t in self.ids_pinned)
         self.grads = {n: torch.empty((max_rows, w), device=device).normal_(0, 1e-3)
                       for n, w in WIDTHS.items()}
         self.h2d_bytes = 0
@@ -416,21 +421,13 @@ class ApiStep:
         g._rotation, g._features_dc, g._features_rest = act.rotation, act.features_dc, act.features_rest
 
     def step(self, k: int) -> int:
+        """One iteration in the engine's order: the resident plan for k+1 is
+        known up front and its N+1 prefetch (H2D of the incoming blocks) runs
+        on the worker thread / prefetch stream while the optimizer step and
+        the write-back of iteration k run."""
         db, ws = self.db, self.ws
         t = time.perf_counter()
         loaded = list(db.active_buffer.loaded_blocks)
-        # visible rows: the blocks at visible slice positions of the active buffer
-        pos = self.sched.visible_positions(k)
-        ids_host = (pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)
-        ids = torch.from_numpy(ids_host).pin_memory().to(self.device, non_blocking=True)
-        n = ids_host.size
-        grads = {name: g[:n] for name, g in self.grads.items()}
-        stats = self.opt.step(k, self.gaussians, ids, grads)
-        t = self._mark("adam_step", t)
-        updated = stats["updated_block_ids"]
-        db.mark_dirty_blocks(updated)
-        bounds = ws.stage_block_bounds(updated)
-        t = self._mark("dirty_mark_bounds", t)
         # turnover: evict 512 of the loaded blocks, stream 512 new ones
         rng = np.random.default_rng(30_000 + k)
         evict_idx = rng.choice(len(loaded), TURNOVER, replace=False)
@@ -444,6 +441,18 @@ class ApiStep:
                           resident_block_ids=keep, evicted_block_ids=evicted,
                           block_reader=self.pool, defer_resident_copy=True)
         t = self._mark("start_prefetch", t)
+        # visible rows: the blocks at visible slice positions of the active
+        # buffer, uploaded from page-locked host memory every step
+        ids_host = self.ids_pinned[k % self.sched.n_sets]
+        ids = ids_host.to(self.device, non_blocking=True)
+        n = ids_host.numel()
+        grads = {name: g[:n] for name, g in self.grads.items()}
+        stats = self.opt.step(k, self.gaussians, ids, grads)
+        t = self._mark("adam_step", t)
+        updated = stats["updated_block_ids"]
+        db.mark_dirty_blocks(updated)
+        bounds = ws.stage_block_bounds(updated)
+        t = self._mark("dirty_mark_bounds", t)
         wb_ids = db.dirty_blocks_for_eviction(evicted)
         t = self._mark("dirty_select", t)
         pending = ws.stage_updated_blocks(wb_ids)
@@ -466,7 +475,7 @@ class ApiStep:
         self._activate()
         self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
         self._mark("activate", t)
-        self.h2d_bytes += TURNOVER * B * 59 * 4 + ids_host.nbytes
+        self.h2d_bytes += TURNOVER * B * 59 * 4 + ids_host.numel() * 8
         return n
 
 
@@ -551,7 +560,7 @@ def main(argv=None):
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="tidegs_b200", choices=["tidegs_b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--e2e-warmup", type=int, default=3)
+    ap.add_argument("--e2e-warmup", type=int, default=6)
     ap.add_argument("--e2e-profile", action="store_true",
                     help="print a per-phase wall-time breakdown of the e2e step to stderr")
     ap.add_argument("--pool-blocks", type=int, default=1024)
@@ -630,7 +639,9 @@ def main(argv=None):
                "host_pool_blocks": args.pool_blocks}
         if api.profile is not None and rank == 0:
             print("e2e phase wall ms/step: " + json.dumps(
-                {k: round(v * 1e3 / args.e2e_steps, 2) for k, v in api.profile.items()}),
+                {k: round(v * 1e3 / args.e2e_steps, 2) for k, v in api.profile.items()})
+                + " writeback staging bytes: "
+                + str(api.ws.writeback_stats["pinned_staging_bytes"]),
                 file=sys.stderr, flush=True)
         del api
     except _Skipped as why:

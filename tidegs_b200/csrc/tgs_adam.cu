@@ -5,6 +5,8 @@
 //   strategies/tide_engine/gpu_resident_optimizer.py:16-70   (per-element Adam math)
 //   strategies/tide_engine/gpu_resident_optimizer.py:266-337 (row->slot, step tables)
 //   submodules/clm_kernels/adam.cu:12-41                     (SelectiveAdam math)
+#include <math.h>
+
 #include "tgs_common.cuh"
 
 namespace tgs {
@@ -57,7 +59,9 @@ __global__ void __launch_bounds__(256) resident_count_kernel(
 // ---------------------------------------------------------------------------
 // Kernel B: per touched position, advance its slot's step and publish the
 // bias-correction pair of that step (table precomputed on the host in double
-// precision exactly as gpu_resident_optimizer.py:325-328 does).
+// precision exactly as gpu_resident_optimizer.py:325-328 does). The slot keeps
+// (1 / (1-b1^t), sqrt(1-b2^t)): the reference's `lr / bias` is evaluated as
+// reciprocal(bias) * lr, so the reciprocal is shared by all rows of the slot.
 // ---------------------------------------------------------------------------
 __global__ void resident_slot_kernel(const int32_t* __restrict__ pos_count,
                                      const int32_t* __restrict__ pos_slot, int n_pos,
@@ -70,7 +74,8 @@ __global__ void resident_slot_kernel(const int32_t* __restrict__ pos_count,
     const int s = pos_slot[p];
     const int t = slot_step[s] + 1;
     slot_step[s] = t;
-    slot_bias[s] = table[t < table_len ? t : table_len - 1];
+    const float2 e = table[t < table_len ? t : table_len - 1];
+    slot_bias[s] = make_float2(fdiv(1.0f, e.x), e.y);
   }
 }
 
@@ -79,14 +84,16 @@ __global__ void resident_slot_kernel(const int32_t* __restrict__ pos_count,
 // lane l owns UNIFIED columns 2l and 2l+1, so the row's 512-byte (m,v) state
 // row is one fully coalesced float4 access per lane. A warp takes 32 rows,
 // resolves their slot/state row once (one row per lane, binary search over
-// the resident layout), then streams them U rows at a time with all loads of
-// the U rows issued before any store.
+// the resident layout) into a per-warp shared-memory table, then streams the
+// rows U at a time, all loads of the U rows issued before any store. The
+// update itself is branch-free: every lane computes both columns and only
+// the stores are predicated.
 // ---------------------------------------------------------------------------
 struct ResidentApplyParams {
   float* param[kNumComp];
   const float* grad[kNumComp];
   float lr[kNumComp];
-  float beta1, beta2, omb1, omb2, eps, batch_size;
+  float beta1, beta2, omb1, omb2, eps, batch_size, inv_batch_size;
   const int64_t* pos_start;
   const int64_t* pos_end;
   const int32_t* pos_slot;
@@ -96,23 +103,35 @@ struct ResidentApplyParams {
   int64_t n;
   float4* state;
   const uint32_t* slot_stamp;
-  const float2* slot_bias;
+  const float2* slot_bias;  // (1/(1-b1^t), sqrt(1-b2^t)) per slot
   const int32_t* err;
 };
 
+// Occupancy target (CTAs per SM) and rows in flight per warp of the update
+// kernel; overridable at build time for tuning sweeps.
+#ifndef TGS_APPLY_MIN_BLOCKS
+#define TGS_APPLY_MIN_BLOCKS 3
+#endif
+#ifndef TGS_APPLY_UNROLL
+#define TGS_APPLY_UNROLL 4
+#endif
 constexpr int kApplyThreads = 256;
-constexpr int kApplyUnroll = 4;
+constexpr int kApplyWarps = kApplyThreads / 32;
+constexpr int kApplyUnroll = TGS_APPLY_UNROLL;
+constexpr int kApplyMinBlocks = TGS_APPLY_MIN_BLOCKS;
 
 struct AdamScalars {
-  float beta1, beta2, omb1, omb2, eps, batch_size;
+  float beta1, beta2, omb1, omb2, eps, batch_size, inv_batch_size;
 };
 
 // Reference torch-fallback order (gpu_resident_optimizer.py:355-364), one
-// rounding per operation; step_scale = (1/bias1) * lr.
+// rounding per operation; step_scale = (1/bias1) * lr. With a power-of-two
+// batch size grad/bs and grad*(1/bs) are the same exactly rounded value.
+template <bool kPow2Batch>
 __device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float graw,
                                           const AdamScalars& h, float step_scale,
                                           float denom_scale) {
-  const float g = fdiv(graw, h.batch_size);
+  const float g = kPow2Batch ? fmul(graw, h.inv_batch_size) : fdiv(graw, h.batch_size);
   m = fadd(fmul(h.beta1, m), fmul(h.omb1, g));
   v = fadd(fmul(h.beta2, v), fmul(fmul(h.omb2, g), g));
   const float denom = fadd(fdiv(fsqrt(v), denom_scale), h.eps);
@@ -133,13 +152,31 @@ __device__ __forceinline__ T pick6(const T (&arr)[kNumComp], int c) {
   }
 }
 
-__global__ void __launch_bounds__(kApplyThreads, 3) resident_adam_kernel(const ResidentApplyParams a) {
+// Per-row metadata shared by the lanes of a warp (two 16-byte halves, each
+// read with one broadcast shared-memory load).
+struct __align__(16) RowAddr {
+  int64_t id;  // local row
+  int64_t sr;  // state row
+};
+struct __align__(16) RowScale {
+  float rb1;      // 1 / (1 - b1^t) of the row's slot
+  float ds;       // sqrt(1 - b2^t)
+  uint32_t stamp; // admission stamp of the slot
+  uint32_t pad;
+};
+
+template <bool kPow2Batch>
+__global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_kernel(const ResidentApplyParams a) {
+  __shared__ RowAddr s_addr[kApplyWarps][32];
+  __shared__ RowScale s_scale[kApplyWarps][32];
   if (load_error(a.err) != 0) return;
   const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const unsigned full = 0xffffffffu;
-  const AdamScalars hp = {a.beta1, a.beta2, a.omb1, a.omb2, a.eps, a.batch_size};
+  const AdamScalars hp = {a.beta1, a.beta2, a.omb1, a.omb2, a.eps, a.batch_size, a.inv_batch_size};
 
-  // Per-lane column bindings (fixed for the whole kernel).
+  // Per-lane column bindings (fixed for the whole kernel). Lanes past column
+  // 58 bind to column 0 of xyz: they load and compute but never store.
   const float* gbase[2];
   float* pbase[2];
   int width[2];
@@ -156,88 +193,73 @@ __global__ void __launch_bounds__(kApplyThreads, 3) resident_adam_kernel(const R
     width[e] = comp_width(c);
     lr[e] = pick6(a.lr, c);
   }
+  // State float4 lanes: pair 2l in .xy (valid for l <= 29), pair 2l+1 in .zw
+  // (valid for l <= 28); lane 31's .x carries the row stamp.
+  const bool keep_lo = lane < 30;
+  const bool keep_hi = lane < 29;
+  const bool stamp_lane = lane == 31;
 
-  const int warps_per_cta = kApplyThreads / 32;
-  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * warps_per_cta + (threadIdx.x >> 5);
-  const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * warps_per_cta;
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * kApplyWarps + warp;
+  const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kApplyWarps;
 
   for (int64_t chunk = warp_id; chunk * 32 < a.n; chunk += warp_stride) {
     const int64_t row0 = chunk * 32;
     const int nr = static_cast<int>(min64(32, a.n - row0));
 
-    int64_t my_id = 0, my_sr = 0;
-    float my_b1 = 1.f, my_ds = 1.f;
-    uint32_t my_stamp = 0;
     if (lane < nr) {
-      my_id = a.ids[row0 + lane];
-      const int p = upper_bound_i64(a.pos_end, a.n_pos, my_id);
+      const int64_t id = a.ids[row0 + lane];
+      const int p = upper_bound_i64(a.pos_end, a.n_pos, id);
       const int s = __ldg(a.pos_slot + p);
-      my_sr = static_cast<int64_t>(s) * a.block_size + (my_id - __ldg(a.pos_start + p));
       const float2 bb = a.slot_bias[s];
-      my_b1 = bb.x;
-      my_ds = bb.y;
-      my_stamp = __ldg(a.slot_stamp + s);
+      s_addr[warp][lane] = {id, static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p))};
+      s_scale[warp][lane] = {bb.x, bb.y, __ldg(a.slot_stamp + s), 0u};
     }
+    __syncwarp();
 
+    const float* gptr0 = gbase[0] + row0 * width[0];
+    const float* gptr1 = gbase[1] + row0 * width[1];
     for (int r = 0; r < nr; r += kApplyUnroll) {
-      // Load phase: only the streamed operands stay live across the unrolled
-      // rows; row metadata is re-broadcast in the update phase (shuffles are
-      // cheaper than the registers they would pin).
       float4 st[kApplyUnroll];
       float g0[kApplyUnroll], g1[kApplyUnroll], p0[kApplyUnroll], p1[kApplyUnroll];
 #pragma unroll
       for (int u = 0; u < kApplyUnroll; ++u) {
         const int rr = r + u;  // warp-uniform
-        const int64_t id = __shfl_sync(full, my_id, rr & 31);
-        const int64_t sr = __shfl_sync(full, my_sr, rr & 31);
         st[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         g0[u] = g1[u] = p0[u] = p1[u] = 0.f;
         if (rr < nr) {
-          const int64_t gi = row0 + rr;
-          st[u] = a.state[sr * 32 + lane];
-          if (act[0]) {
-            g0[u] = gbase[0][gi * width[0]];
-            p0[u] = pbase[0][id * width[0]];
-          }
-          if (act[1]) {
-            g1[u] = gbase[1][gi * width[1]];
-            p1[u] = pbase[1][id * width[1]];
-          }
+          const RowAddr ra = s_addr[warp][rr];
+          st[u] = a.state[ra.sr * 32 + lane];
+          g0[u] = gptr0[rr * width[0]];
+          g1[u] = gptr1[rr * width[1]];
+          p0[u] = pbase[0][ra.id * width[0]];
+          p1[u] = pbase[1][ra.id * width[1]];
         }
       }
 #pragma unroll
       for (int u = 0; u < kApplyUnroll; ++u) {
         const int rr = r + u;
         if (rr >= nr) break;  // warp-uniform
-        const int64_t id = __shfl_sync(full, my_id, rr);
-        const int64_t sr = __shfl_sync(full, my_sr, rr);
-        const float b1 = __shfl_sync(full, my_b1, rr);
-        const float ds = __shfl_sync(full, my_ds, rr);
-        const uint32_t stamp = __shfl_sync(full, my_stamp, rr);
+        const RowAddr ra = s_addr[warp][rr];
+        const RowScale rs = s_scale[warp][rr];
         // A row whose stamp is not its slot's current stamp has not been
         // touched since the block was (re)admitted: its moments are zero.
         const bool fresh =
-            __shfl_sync(full, __float_as_uint(st[u].x) == stamp ? 1 : 0, 31) != 0;
+            __shfl_sync(full, __float_as_uint(st[u].x) == rs.stamp ? 1 : 0, 31) != 0;
         float m0 = fresh ? st[u].x : 0.f, v0 = fresh ? st[u].y : 0.f;
         float m1 = fresh ? st[u].z : 0.f, v1 = fresh ? st[u].w : 0.f;
-        const float inv_b1 = fdiv(1.0f, b1);
-        if (act[0]) adam_elem(p0[u], m0, v0, g0[u], hp, fmul(inv_b1, lr[0]), ds);
-        if (act[1]) adam_elem(p1[u], m1, v1, g1[u], hp, fmul(inv_b1, lr[1]), ds);
+        adam_elem<kPow2Batch>(p0[u], m0, v0, g0[u], hp, fmul(rs.rb1, lr[0]), rs.ds);
+        adam_elem<kPow2Batch>(p1[u], m1, v1, g1[u], hp, fmul(rs.rb1, lr[1]), rs.ds);
         float4 out;
-        if (lane < 29) {
-          out = make_float4(m0, v0, m1, v1);
-        } else if (lane == 29) {
-          out = make_float4(m0, v0, 0.f, 0.f);
-        } else if (lane == 30) {
-          out = make_float4(0.f, 0.f, 0.f, 0.f);
-        } else {
-          out = make_float4(__uint_as_float(stamp), 0.f, 0.f, 0.f);
-        }
-        a.state[sr * 32 + lane] = out;
-        if (act[0]) pbase[0][id * width[0]] = p0[u];
-        if (act[1]) pbase[1][id * width[1]] = p1[u];
+        out.x = stamp_lane ? __uint_as_float(rs.stamp) : (keep_lo ? m0 : 0.f);
+        out.y = keep_lo ? v0 : 0.f;
+        out.z = keep_hi ? m1 : 0.f;
+        out.w = keep_hi ? v1 : 0.f;
+        a.state[ra.sr * 32 + lane] = out;
+        if (act[0]) pbase[0][ra.id * width[0]] = p0[u];
+        if (act[1]) pbase[1][ra.id * width[1]] = p1[u];
       }
     }
+    __syncwarp();  // the table is rewritten by the next chunk
   }
 }
 
@@ -488,6 +510,12 @@ extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* strea
   p.omb2 = a->one_minus_beta2;
   p.eps = a->eps;
   p.batch_size = a->batch_size;
+  // A power-of-two batch size with a normal reciprocal divides exactly by a
+  // multiply (same exactly rounded result as the division).
+  int exp2 = 0;
+  const float mant = frexpf(a->batch_size, &exp2);
+  const bool pow2 = mant == 0.5f && exp2 > -125 && exp2 < 126;
+  p.inv_batch_size = pow2 ? 1.0f / a->batch_size : 0.0f;
   p.pos_start = a->pos_start;
   p.pos_end = a->pos_end;
   p.pos_slot = a->pos_slot;
@@ -501,9 +529,10 @@ extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* strea
   p.err = a->err;
   const int64_t warps_needed = ceil_div<int64_t>(a->n_rows, 32);
   const int64_t ctas_needed = ceil_div<int64_t>(warps_needed, kApplyThreads / 32);
-  const int64_t cap = static_cast<int64_t>(sm_count()) * 3;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * kApplyMinBlocks;
   const int grid = static_cast<int>(std::min<int64_t>(ctas_needed, cap));
-  resident_adam_kernel<<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
+  if (pow2) resident_adam_kernel<true><<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
+  else resident_adam_kernel<false><<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

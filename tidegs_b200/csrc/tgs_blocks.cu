@@ -28,8 +28,7 @@ struct ConstComp6 {
 // the previous tile's columns into the component arrays with coalesced stores.
 // ---------------------------------------------------------------------------
 constexpr int kTileRows = 64;
-constexpr int kTileFloats = kTileRows * kRowWidth;          // 3776
-constexpr uint32_t kTileBytes = kTileFloats * sizeof(float);  // 15104 (multiple of 16)
+constexpr int kTileFloats = kTileRows * kRowWidth;  // 3776 floats = 15104 B (multiple of 16)
 constexpr int kUnpackThreads = 256;
 
 struct UnpackParams {

@@ -431,11 +431,18 @@ class GPUWorkingSet:
         if (staging is not None and gpu_staging is not None
                 and required_rows <= self._writeback_staging_capacities[slot_idx]):
             return staging, gpu_staging, available
-        staging = _pinned_empty((required_rows, 59))
-        gpu_staging = torch.empty((required_rows, 59), dtype=torch.float32, device=self.device)
+        # Page-locking a GB-sized buffer takes hundreds of ms: grow
+        # geometrically so a write-back set that grows over the first
+        # iterations re-allocates O(log) times instead of on every new maximum.
+        previous = self._writeback_staging_capacities[slot_idx]
+        capacity = max(required_rows, 2 * previous)
+        self._writeback_staging_slots[slot_idx] = None
+        self._writeback_gpu_staging_slots[slot_idx] = None
+        staging = _pinned_empty((capacity, 59))
+        gpu_staging = torch.empty((capacity, 59), dtype=torch.float32, device=self.device)
         self._writeback_staging_slots[slot_idx] = staging
         self._writeback_gpu_staging_slots[slot_idx] = gpu_staging
-        self._writeback_staging_capacities[slot_idx] = required_rows
+        self._writeback_staging_capacities[slot_idx] = capacity
         self.writeback_stats["pinned_staging_bytes"] = sum(
             s.numel() * s.element_size() for s in self._writeback_staging_slots if s is not None)
         self.writeback_stats["pinned_staging"] = all(

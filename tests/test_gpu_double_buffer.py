@@ -323,8 +323,19 @@ def _check_buffer(buf, rec, arrays, prefix):
     assert {str(b): [s.start, s.stop] for b, s in buf.block_to_local_slice.items()} == rec["slices"]
 
 
-@pytest.mark.parametrize("pinned_pool", [False, True])
-def test_random_ab_materialization_matches_golden(golden, pinned_pool):
+class _PinnedViews:
+    """A reader exposing only page-locked per-block views."""
+
+    def __init__(self, pool):
+        self._pool = pool
+        self.layout = pool.layout
+
+    def read_blocks_pinned(self, ids):
+        return self._pool.read_blocks_pinned(ids)
+
+
+@pytest.mark.parametrize("source", ["read_batch", "pool_pointers", "pinned_views"])
+def test_random_ab_materialization_matches_golden(golden, source):
     from tidegs_b200.block_reader import BlockLayout, PinnedBlockPool
 
     meta, arrays = golden("double_buffer")
@@ -336,11 +347,14 @@ def test_random_ab_materialization_matches_golden(golden, pinned_pool):
     manager = _manager(num_total, B)
     try:
         _seed_active(manager, blocks, [0, 2, 4, 6], B, num_total)
+        pinned_pool = source != "read_batch"
         if pinned_pool:
             pool = torch.zeros((nblocks, B, 59))
             for b, rows in blocks.items():
                 pool[b, : rows.shape[0]] = rows
             reader = PinnedBlockPool(pool, B, num_total, layout=BlockLayout.CACHE)
+            if source == "pinned_views":
+                reader = _PinnedViews(reader)
         else:
             reader = _Reader(BlockLayout.CACHE, blocks)
         filt = torch.tensor([2 * B + 3, 7 * B, 5 * B + 1, 19 * B + 10, 19 * B + 12, -5, 4 * B + 15])

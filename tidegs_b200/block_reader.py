@@ -17,6 +17,7 @@ from dataclasses import dataclass
 from enum import Enum
 from typing import Dict, List, Optional, Protocol, Sequence, runtime_checkable
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -172,6 +173,19 @@ class PinnedBlockPool:
 
     def entry(self, block_id: int) -> torch.Tensor:
         return self._data[int(block_id) % self.pool_blocks]
+
+    def block_host_pointers(self, block_ids):
+        """(host addresses, row counts) of the listed blocks as int64 numpy
+        arrays, computed without creating per-block tensors; invalid ids
+        raise KeyError like an omitted block."""
+        ids = np.asarray(block_ids, dtype=np.int64)
+        bad = ids[(ids < 0) | (ids >= self.num_blocks)]
+        rows = np.minimum(self.block_size, self.total_gaussians - ids * self.block_size)
+        if bad.size or np.any(rows <= 0):
+            raise KeyError(f"BlockReader omitted blocks; first missing={bad[:8].tolist()}")
+        entry_bytes = self.block_size * 59 * 4
+        ptrs = self._data.data_ptr() + (ids % self.pool_blocks) * entry_bytes
+        return ptrs.astype(np.int64), rows.astype(np.int64)
 
     def read_blocks_pinned(self, block_ids: List[int]) -> Dict[int, torch.Tensor]:
         out = {}

@@ -544,29 +544,33 @@ class DoubleBufferGPUWorkingSet:
 
         if streamed_blocks:
             streamed_rows = sum(block_lengths[b] for b in streamed_blocks)
+            pointer_reader = getattr(block_reader, "block_host_pointers", None)
             pinned_reader = getattr(block_reader, "read_blocks_pinned", None)
             read_batch = getattr(block_reader, "read_batch", None)
-            if callable(pinned_reader):
-                # Page-locked pool: one DMA per block into device staging.
-                blocks = pinned_reader(streamed_blocks)
-                missing = [b for b in streamed_blocks if b not in blocks]
-                if missing:
-                    raise KeyError(
-                        f"BlockReader omitted {len(missing)} N+1 blocks; first missing={missing[:8]}")
+            if callable(pointer_reader) or callable(pinned_reader):
+                # Page-locked pool: one DMA per block straight into device
+                # staging, no CPU-side concatenation.
                 _, packed_gpu, staging_slot = self._acquire_host_staging(streamed_rows, host=False)
-                dst, src, nbytes, off = [], [], [], 0
-                for b in streamed_blocks:
-                    rows = block_lengths[b]
-                    host = blocks[b]
-                    if tuple(host.shape) < (rows, 59) or not host.is_contiguous():
-                        raise ValueError(f"Invalid pinned block {b}: shape {tuple(host.shape)}")
-                    dst.append(packed_gpu[off].data_ptr())
-                    src.append(host.data_ptr())
-                    nbytes.append(rows * 59 * 4)
-                    off += rows
-                _ops.h2d_blocks(dst, src, nbytes, self.device)
+                want = np.asarray([block_lengths[b] for b in streamed_blocks], np.int64)
+                if callable(pointer_reader):
+                    src, rows = pointer_reader(streamed_blocks)
+                    if np.any(rows < want):
+                        raise ValueError("Invalid pinned blocks: fewer rows than the scene holds")
+                else:
+                    blocks = pinned_reader(streamed_blocks)
+                    missing = [b for b in streamed_blocks if b not in blocks]
+                    if missing:
+                        raise KeyError(f"BlockReader omitted {len(missing)} N+1 blocks; "
+                                       f"first missing={missing[:8]}")
+                    for b in streamed_blocks:
+                        host = blocks[b]
+                        if host.shape[0] < block_lengths[b] or not host.is_contiguous():
+                            raise ValueError(f"Invalid pinned block {b}: shape {tuple(host.shape)}")
+                    src = np.asarray([blocks[b].data_ptr() for b in streamed_blocks], np.int64)
+                nbytes = want * (59 * 4)
+                dst = packed_gpu.data_ptr() + np.concatenate([[0], np.cumsum(nbytes)[:-1]])
+                _ops.h2d_blocks(dst.tolist(), src.tolist(), nbytes.tolist(), self.device)
                 self.stats["direct_block_dma_calls"] += len(streamed_blocks)
-                self._h2d_refs = blocks
             else:
                 if callable(read_batch):
                     staging, packed_gpu, staging_slot = self._acquire_host_staging(streamed_rows)

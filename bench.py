@@ -184,8 +184,7 @@ class Schedule:
     def turnover(self, step: int):
         rng = np.random.default_rng(20_000 + step)
         evict_pos = np.sort(rng.choice(SLOTS, TURNOVER, replace=False))
-        resident = set(self.slot_block.tolist())
-        candidates = np.array([b for b in self.pool_ids.tolist() if b not in resident], np.int64)
+        candidates = np.setdiff1d(self.pool_ids, self.slot_block, assume_unique=True)
         incoming = np.sort(rng.choice(candidates, TURNOVER, replace=False))
         dirty = rng.random(TURNOVER) < 0.5
         return evict_pos, incoming, dirty
@@ -206,13 +205,30 @@ def fill_params(comps, gen):
 # ---------------------------------------------------------------------------
 # Device leg: library entry points, inputs resident in HBM
 # ---------------------------------------------------------------------------
+def rank_visible_positions(sched: "Schedule", step: int, world: int, rank: int) -> np.ndarray:
+    """Slot positions of `sched`'s owner whose blocks rank `rank` renders at
+    `step`: the owner's visible runs (~30 % of its slots, as on one GPU) split
+    into `world` contiguous parts, each widened by 15 % of a part on both
+    sides so that neighbouring ranks' cameras overlap."""
+    pos = sched.visible_positions(step)
+    if world == 1:
+        return pos
+    part = -(-pos.size // world)
+    margin = int(0.15 * part)
+    lo = max(0, rank * part - margin)
+    hi = min(pos.size, (rank + 1) * part + margin)
+    return pos[lo:hi]
+
+
 class DeviceStep:
-    def __init__(self, device, sched: Schedule):
+    def __init__(self, device, sched: Schedule, scheds=None, world: int = 1):
         from tidegs_b200 import _lib, _ops
 
         self._lib, self._ops = _lib, _ops
         self.device = device
         self.sched = sched
+        self.world = world
+        self.scheds = scheds if scheds is not None else [sched]
         gen = torch.Generator(device=device).manual_seed(1234 + sched.rank)
         rows = SLOTS * B
         self.arena = {n: torch.empty((rows, w), device=device) for n, w in WIDTHS.items()}
@@ -254,9 +270,49 @@ class DeviceStep:
             max_rows = max(max_rows, ids.size)
         self.grads = {n: torch.empty((max_rows, w), device=device).normal_(0, 1e-3, generator=gen)
                       for n, w in WIDTHS.items()}
+        if world > 1:
+            # gradients this rank renders for blocks of every owner, and the
+            # exchange buffers (sizes: the largest of the periodic camera sets)
+            from tidegs_b200.sharded import BlockGradExchange
+
+            self.exchange = BlockGradExchange(B, device=device)
+            send_max = recv_max = 0
+            for s_ in range(sched.n_sets):
+                mine = sum(rank_visible_positions(o, s_, world, sched.rank).size for o in self.scheds)
+                theirs = sum(rank_visible_positions(sched, s_, world, r).size for r in range(world))
+                send_max, recv_max = max(send_max, mine), max(recv_max, theirs)
+            self.rank_grads = {n: torch.empty((send_max * B, w), device=device).normal_(
+                0, 1e-3, generator=gen) for n, w in WIDTHS.items()}
+            self.send_buf = torch.empty((send_max * B, 59), device=device)
+            self.recv_buf = torch.empty((recv_max * B, 59), device=device)
+            self.exchange_rows = 0
         self.adam_ms = []
         self.updated_rows = []
         torch.cuda.synchronize()
+
+    def exchange_grads(self, k: int):
+        """Owner-sharded gradient exchange of step k (world > 1): returns the
+        owner's visible slot positions and local row ids; the reduced
+        gradients land in self.grads."""
+        from tidegs_b200.sharded import make_plan
+
+        W, me = self.world, self.sched.rank
+        vis = []
+        for r in range(W):
+            vis.append(np.concatenate([o.slot_block[rank_visible_positions(o, k, W, r)]
+                                       for o in self.scheds]))
+        own = self.sched
+        slot_of = {int(b): i for i, b in enumerate(own.slot_block)}
+        plan = make_plan(vis, W, me, B, out_order=slot_of)
+        order = np.unique(vis[me])
+        start = {int(b): i * B for i, b in enumerate(order)}
+        send = self.exchange.pack(plan, self.rank_grads, start, out=self.send_buf)
+        recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
+        self.exchange.reduce(plan, recv, out=self.grads, err=self.err)
+        pos = np.asarray([slot_of[int(b)] for b in plan.out_blocks], np.int64)
+        ids = (pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)
+        self.exchange_rows += int(send.shape[0])
+        return pos, self._ops.i64_to_device(ids, self.device)
 
     def adam(self, ids: torch.Tensor, timed: bool):
         _lib = self._lib
@@ -297,7 +353,11 @@ class DeviceStep:
     def step(self, k: int, timed: bool = False) -> int:
         _ops = self._ops
         sched = self.sched
-        pos, ids = self.vis_sets[k % sched.n_sets]
+        if self.world > 1:
+            # 0. gradients of blocks rendered on other ranks reach their owners
+            pos, ids = self.exchange_grads(k)
+        else:
+            pos, ids = self.vis_sets[k % sched.n_sets]
         # 1. optimizer over the visible rows
         self.adam(ids, timed)
         # 2. updated blocks are dirty; refresh their bounds
@@ -327,6 +387,10 @@ class DeviceStep:
                          (np.arange(TURNOVER) * B).tolist(), (evict_pos * B).tolist(),
                          [B] * TURNOVER, self.device)
         sched.slot_block[evict_pos] = incoming
+        for other in self.scheds:  # replicas of the other owners' schedules
+            if other is not sched:
+                ev, inc, _ = other.turnover(k)
+                other.slot_block[ev] = inc
         self.stamp_host[evict_pos] += 1
         self.slot_stamp.copy_(torch.from_numpy(self.stamp_host.view(np.int32)).pin_memory(),
                               non_blocking=True)
@@ -347,6 +411,11 @@ class _Skipped(Exception):
 # e2e leg: Python drop-in classes, host pool -> HBM -> host
 # ---------------------------------------------------------------------------
 class ApiStep:
+    """The step through the Python drop-ins. Slice position i of the active
+    buffer holds sched.slot_block[i]; the persistent-slot plan gives incoming
+    blocks (ascending) the freed slices (ascending), which is exactly the
+    schedule's turnover, so every rank can replicate every owner's layout."""
+
     profile = None
 
     def _mark(self, name, t):
@@ -356,16 +425,18 @@ class ApiStep:
             return now
         return t
 
-    def __init__(self, device, sched: Schedule, pool_blocks: int):
+    def __init__(self, device, scheds, rank: int, world: int, pool_blocks: int):
         import types
 
         from tidegs_b200 import (BlockLayout, DoubleBufferGPUWorkingSet, GPUResidentAdam,
-                                 GPUWorkingSet, PinnedBlockPool)
+                                 GPUWorkingSet, PinnedBlockPool, _ops)
 
         self.device = device
-        self.sched = sched
-        num_total = int(sched.pool_ids.max() + 1) * B
-        gen = torch.Generator().manual_seed(99 + sched.rank)
+        self.scheds = scheds
+        self.sched = sched = scheds[rank]
+        self.rank, self.world = rank, world
+        num_total = int(max(int(o.pool_ids.max()) for o in scheds) + 1) * B
+        gen = torch.Generator().manual_seed(99 + rank)
         data = torch.empty((pool_blocks, B, 59), pin_memory=True)
         for i in range(pool_blocks):
             data[i].normal_(0.0, 1.0, generator=gen)
@@ -375,33 +446,44 @@ class ApiStep:
         self.opt = GPUResidentAdam(batch_size=16, block_size=B, capacity_blocks=SLOTS,
                                    device=device)
         act = self.db.active_buffer
-        order = sorted(sched.slot_block.tolist())
+        order = [int(b) for b in sched.slot_block]
         self.db._allocate_target_tensors(act, SLOTS * B)
-        gen_d = torch.Generator(device=device).manual_seed(5)
-        fill_params(act.components(), gen_d)
-        from tidegs_b200 import _ops
-
+        fill_params(act.components(), torch.Generator(device=device).manual_seed(5))
         _ops.fill_global_ids(act.local_to_global_idx, 0, _ops.i64_to_device(order, device),
                              SLOTS * B, B)
         act.loaded_blocks = list(order)
         act.block_to_local_slice = {b: slice(i * B, (i + 1) * B) for i, b in enumerate(order)}
         act.num_gaussians = SLOTS * B
-        act._block_starts = None
-        self.columns_lr = torch.tensor([LRS[n] for n in NAMES], dtype=torch.float32)
         self.gaussians = types.SimpleNamespace(
             gpu_working_set_manager=self.ws,
-            optimizer=types.SimpleNamespace(columns_lr=self.columns_lr,
-                                            param_groups=[{"betas": (0.9, 0.999), "eps": 1e-15}]))
+            optimizer=types.SimpleNamespace(
+                columns_lr=torch.tensor([LRS[n] for n in NAMES], dtype=torch.float32),
+                param_groups=[{"betas": (0.9, 0.999), "eps": 1e-15}]))
         self._activate()
         self.opt.set_resident_blocks(order)
+        # visible rows of each camera set, page-locked (world == 1)
         self.ids_pinned = []
         for s_ in range(sched.n_sets):
             pos = sched.visible_positions(s_)
-            ids_np = (pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)
-            self.ids_pinned.append(torch.from_numpy(ids_np).pin_memory())
+            self.ids_pinned.append(
+                torch.from_numpy((pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)).pin_memory())
         max_rows = max(t.numel() for t in self.ids_pinned)
         self.grads = {n: torch.empty((max_rows, w), device=device).normal_(0, 1e-3)
                       for n, w in WIDTHS.items()}
+        if world > 1:
+            from tidegs_b200.sharded import BlockGradExchange
+
+            self.exchange = BlockGradExchange(B, device=device)
+            send_max = recv_max = 0
+            for s_ in range(sched.n_sets):
+                send_max = max(send_max, sum(rank_visible_positions(o, s_, world, rank).size
+                                             for o in scheds))
+                recv_max = max(recv_max, sum(rank_visible_positions(sched, s_, world, r).size
+                                             for r in range(world)))
+            self.rank_grads = {n: torch.empty((send_max * B, w), device=device).normal_(0, 1e-3)
+                               for n, w in WIDTHS.items()}
+            self.send_buf = torch.empty((send_max * B, 59), device=device)
+            self.recv_buf = torch.empty((recv_max * B, 59), device=device)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         torch.cuda.synchronize()
@@ -420,33 +502,50 @@ class ApiStep:
         g._xyz, g._opacity, g._scaling = act.xyz, act.opacity, act.scaling
         g._rotation, g._features_dc, g._features_rest = act.rotation, act.features_dc, act.features_rest
 
+    def _grads_and_ids(self, k: int):
+        """(sparse_grad_local_ids, sparse_grad_components) of this owner."""
+        if self.world == 1:
+            ids_host = self.ids_pinned[k % self.sched.n_sets]
+            n = ids_host.numel()
+            self.h2d_bytes += n * 8
+            return ids_host.to(self.device, non_blocking=True), {
+                name: g[:n] for name, g in self.grads.items()}
+        from tidegs_b200.sharded import make_plan
+
+        W, me = self.world, self.rank
+        vis = [np.concatenate([o.slot_block[rank_visible_positions(o, k, W, r)] for o in self.scheds])
+               for r in range(W)]
+        slices = self.db.active_buffer.block_to_local_slice
+        plan = make_plan(vis, W, me, B, out_order={b: s.start for b, s in slices.items()})
+        order = np.unique(vis[me])
+        send = self.exchange.pack(plan, self.rank_grads, {int(b): i * B for i, b in enumerate(order)},
+                                  out=self.send_buf)
+        recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
+        grads = self.exchange.reduce(plan, recv, out=self.grads)
+        starts = np.asarray([slices[int(b)].start for b in plan.out_blocks], np.int64)
+        ids_host = torch.from_numpy((starts[:, None] + np.arange(B)[None, :]).reshape(-1))
+        self.h2d_bytes += ids_host.numel() * 8
+        return ids_host.pin_memory().to(self.device, non_blocking=True), grads
+
     def step(self, k: int) -> int:
         """One iteration in the engine's order: the resident plan for k+1 is
         known up front and its N+1 prefetch (H2D of the incoming blocks) runs
         on the worker thread / prefetch stream while the optimizer step and
         the write-back of iteration k run."""
-        db, ws = self.db, self.ws
+        db, ws, sched = self.db, self.ws, self.sched
         t = time.perf_counter()
-        loaded = list(db.active_buffer.loaded_blocks)
-        # turnover: evict 512 of the loaded blocks, stream 512 new ones
-        rng = np.random.default_rng(30_000 + k)
-        evict_idx = rng.choice(len(loaded), TURNOVER, replace=False)
-        evicted = sorted(loaded[i] for i in evict_idx)
-        resident = set(loaded)
-        cand = [b for b in self.sched.pool_ids.tolist() if b not in resident]
-        incoming = sorted(rng.choice(cand, TURNOVER, replace=False).tolist())
-        keep = sorted(resident - set(evicted))
+        evict_pos, incoming_arr, _ = sched.turnover(k)
+        loaded = [int(b) for b in sched.slot_block]
+        evicted = sorted(int(b) for b in sched.slot_block[evict_pos])
+        incoming = [int(b) for b in incoming_arr]
+        keep = sorted(set(loaded) - set(evicted))
         t = self._mark("plan", t)
         db.start_prefetch(iteration=k + 1, visible_block_ids=keep + incoming,
                           resident_block_ids=keep, evicted_block_ids=evicted,
                           block_reader=self.pool, defer_resident_copy=True)
         t = self._mark("start_prefetch", t)
-        # visible rows: the blocks at visible slice positions of the active
-        # buffer, uploaded from page-locked host memory every step
-        ids_host = self.ids_pinned[k % self.sched.n_sets]
-        ids = ids_host.to(self.device, non_blocking=True)
-        n = ids_host.numel()
-        grads = {name: g[:n] for name, g in self.grads.items()}
+        ids, grads = self._grads_and_ids(k)
+        t = self._mark("exchange", t)
         stats = self.opt.step(k, self.gaussians, ids, grads)
         t = self._mark("adam_step", t)
         updated = stats["updated_block_ids"]
@@ -472,11 +571,14 @@ class ApiStep:
         t = self._mark("wait_prefetch", t)
         db.swap_buffers()
         t = self._mark("swap", t)
+        for o in self.scheds:
+            ev, inc, _ = o.turnover(k)
+            o.slot_block[ev] = inc
         self._activate()
         self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
         self._mark("activate", t)
-        self.h2d_bytes += TURNOVER * B * 59 * 4 + ids_host.numel() * 8
-        return n
+        self.h2d_bytes += TURNOVER * B * 59 * 4
+        return int(ids.numel())
 
 
 # ---------------------------------------------------------------------------
@@ -579,8 +681,9 @@ def main(argv=None):
     from tidegs_b200 import _lib
 
     device = torch.device("cuda", torch.cuda.current_device())
-    sched = Schedule(rank, world)
-    dev = DeviceStep(device, sched)
+    scheds = [Schedule(o, world) for o in range(world)]
+    sched = scheds[rank]
+    dev = DeviceStep(device, sched, scheds=scheds, world=world)
     for k in range(args.warmup):
         dev.step(k)
     torch.cuda.synchronize()
@@ -616,7 +719,8 @@ def main(argv=None):
     try:
         if args.no_e2e:
             raise _Skipped("--no-e2e")
-        api = ApiStep(device, sched, args.pool_blocks)
+        api = ApiStep(device, [Schedule(o, world) for o in range(world)], rank, world,
+                      args.pool_blocks)
         for k in range(args.e2e_warmup):
             api.step(k)
         torch.cuda.synchronize()

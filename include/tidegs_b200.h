@@ -344,6 +344,29 @@ TGS_API int tgs_pack_rows(const TgsPackArgs* args, void* stream);
 TGS_API int tgs_block_bounds(const float* xyz, const int64_t* start, const int64_t* count,
                      int32_t n_plans, float* bounds, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Multi-GPU gradient exchange (no counterpart in the reference, which is    */
+/* single-GPU). Blocks are owned by rank block_id mod world; each rank packs */
+/* the gradient tiles of the blocks it rendered by owner (tgs_pack_rows,     */
+/* UNIFIED order), one all-to-all moves them to their owners, and the owner  */
+/* sums the tiles of each block here.                                        */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  const float* recv;              /* [n_recv_blocks * block_size, 59] tiles, UNIFIED order */
+  int64_t n_recv_blocks;
+  const int64_t* contrib_offsets; /* [n_out + 1] CSR offsets into contrib_blocks */
+  const int64_t* contrib_blocks;  /* recv tile index of each contribution, sender order */
+  int32_t n_out;                  /* output blocks (the owner's visible blocks, row order) */
+  int64_t block_size;
+  float* out[TGS_NUM_COMPONENTS]; /* [n_out * block_size, W_c] compact gradients */
+  int32_t* err;                   /* [4] device error word (may be NULL) */
+} TgsBlockSumArgs;
+
+/* out block k = sum of its contributions, added in listed (sender) order with
+ * one rounding per addition, written as the six SoA gradient components. */
+TGS_API int tgs_block_grad_sum(const TgsBlockSumArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

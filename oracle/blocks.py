@@ -103,6 +103,21 @@ def block_bounds(xyz: np.ndarray, starts, counts) -> np.ndarray:
     return out
 
 
+def block_grad_sum(recv: np.ndarray, offsets, contrib, block_size: int) -> Dict[str, np.ndarray]:
+    """Owner-side sum of exchanged [block_size, 59] UNIFIED tiles, added in
+    listed (sender) order one fp32 addition at a time, returned as SoA
+    components (rows of output block k at k*block_size)."""
+    n_out = len(offsets) - 1
+    acc = np.empty((n_out * block_size, 59), np.float32)
+    for k in range(n_out):
+        tiles = [recv[j * block_size:(j + 1) * block_size] for j in contrib[offsets[k]:offsets[k + 1]]]
+        s = tiles[0].copy()
+        for t in tiles[1:]:
+            s = (s + t).astype(np.float32)
+        acc[k * block_size:(k + 1) * block_size] = s
+    return {n: acc[:, UNIFIED[n]:UNIFIED[n] + w].copy() for n, w in WIDTHS.items()}
+
+
 class DirtyBitmap:
     """Reference semantics of the dirty-block bitmap."""
 

@@ -93,3 +93,37 @@ def test_sophia_matches_oracle_with_hessian_refresh(wd):
         np.testing.assert_array_equal(param.detach().cpu().numpy(), p)
         np.testing.assert_array_equal(opt.state[param]["exp_avg"].cpu().numpy(), m)
         np.testing.assert_array_equal(opt.state[param]["hessian"].cpu().numpy(), h)
+
+
+def test_selective_adam_matches_reference_cuda_kernel():
+    """Against the reference's own submodules/clm_kernels/adam.cu, compiled
+    for sm_100a into oracle/_ref by oracle/build_ref.py. The reference is
+    built with nvcc's default FMA contraction, ours rounds every operation:
+    |a-b| <= 1e-6*|b| + 1e-9."""
+    from oracle import build_ref
+    from tidegs_b200 import SelectiveAdam
+
+    ref = build_ref.load_prebuilt()
+    if ref is None:
+        pytest.skip("reference kernel not built (oracle/_ref)")
+    N = 200_003
+    widths = (3, 45, 1, 4)
+    lrs = (1.6e-4, 1.25e-4, 0.05, 1e-3)
+    groups = _groups(N, widths, 11, lrs)
+    mirror = []
+    for g in groups:
+        p = g["params"][0]
+        mirror.append((p.detach().clone(), p.grad.clone(), torch.zeros_like(p), torch.zeros_like(p)))
+    opt = SelectiveAdam(groups, eps=1e-15, betas=(0.9, 0.999))
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    for step in range(4):
+        vis = torch.rand(N, generator=gen, device="cuda") < 0.3
+        opt.step(vis)
+        for (p, g, m, v), lr, w in zip(mirror, lrs, widths):
+            ref.selective_adam_update(p, g, m, v, vis, lr, 0.9, 0.999, 1e-15, N, w)
+    torch.cuda.synchronize()
+    for grp, (p, _, m, v) in zip(groups, mirror):
+        param = grp["params"][0]
+        torch.testing.assert_close(param.detach(), p, rtol=1e-6, atol=1e-9)
+        torch.testing.assert_close(opt.state[param]["exp_avg"], m, rtol=1e-6, atol=1e-9)
+        torch.testing.assert_close(opt.state[param]["exp_avg_sq"], v, rtol=1e-6, atol=1e-9)

@@ -98,6 +98,14 @@ class PackArgs(C.Structure):
     ]
 
 
+class BlockSumArgs(C.Structure):
+    _fields_ = [
+        ("recv", _vp), ("n_recv_blocks", _i64), ("contrib_offsets", _vp),
+        ("contrib_blocks", _vp), ("n_out", _i32), ("block_size", _i64),
+        ("out", _vp * NUM_COMPONENTS), ("err", _vp),
+    ]
+
+
 # name -> (restype, argtypes). Keep in sync with include/tidegs_b200.h.
 SIGNATURES = {
     "tgs_version": (C.c_int, []),
@@ -120,6 +128,7 @@ SIGNATURES = {
     "tgs_dirty_list": (C.c_int, [_vp, _i64, _vp, _vp, _vp]),
     "tgs_pack_rows": (C.c_int, [C.POINTER(PackArgs), _vp]),
     "tgs_block_bounds": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp]),
+    "tgs_block_grad_sum": (C.c_int, [C.POINTER(BlockSumArgs), _vp]),
 }
 
 _lock = threading.Lock()
@@ -166,7 +175,7 @@ KERNELS_PER_CALL = {
     "tgs_build_block_starts": 1, "tgs_global_to_local": 1, "tgs_global_to_local_compact": 3,
     "tgs_global_to_local_compact_noalloc": 3,
     "tgs_dirty_mark": 1, "tgs_dirty_select": 1, "tgs_dirty_list": 1, "tgs_pack_rows": 1,
-    "tgs_block_bounds": 1,
+    "tgs_block_bounds": 1, "tgs_block_grad_sum": 1,
 }
 launch_counter = {"kernels": 0}
 

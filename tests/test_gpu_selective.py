@@ -95,11 +95,20 @@ def test_sophia_matches_oracle_with_hessian_refresh(wd):
         np.testing.assert_array_equal(opt.state[param]["hessian"].cpu().numpy(), h)
 
 
+def _close_1e6(actual, expected, what):
+    """|a-b| <= 1e-6*|b| + 1e-6*max|b|: 1e-6 relative per element, and 1e-6
+    of the tensor's scale where a value lands near zero by cancellation
+    (p - step with p ~ step), where per-element relative error is
+    meaningless."""
+    scale = float(expected.abs().max())
+    torch.testing.assert_close(actual, expected, rtol=1e-6, atol=1e-6 * scale, msg=what)
+
+
 def test_selective_adam_matches_reference_cuda_kernel():
     """Against the reference's own submodules/clm_kernels/adam.cu, compiled
     for sm_100a into oracle/_ref by oracle/build_ref.py. The reference is
-    built with nvcc's default FMA contraction, ours rounds every operation:
-    |a-b| <= 1e-6*|b| + 1e-9."""
+    built with nvcc's default FMA contraction, ours rounds every operation,
+    so results differ by a few ulps; tolerance as in _close_1e6."""
     from oracle import build_ref
     from tidegs_b200 import SelectiveAdam
 
@@ -124,6 +133,6 @@ def test_selective_adam_matches_reference_cuda_kernel():
     torch.cuda.synchronize()
     for grp, (p, _, m, v) in zip(groups, mirror):
         param = grp["params"][0]
-        torch.testing.assert_close(param.detach(), p, rtol=1e-6, atol=1e-9)
-        torch.testing.assert_close(opt.state[param]["exp_avg"], m, rtol=1e-6, atol=1e-9)
-        torch.testing.assert_close(opt.state[param]["exp_avg_sq"], v, rtol=1e-6, atol=1e-9)
+        _close_1e6(param.detach(), p, "param")
+        _close_1e6(opt.state[param]["exp_avg"], m, "exp_avg")
+        _close_1e6(opt.state[param]["exp_avg_sq"], v, "exp_avg_sq")

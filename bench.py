@@ -310,9 +310,13 @@ class DeviceStep:
         recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
         self.exchange.reduce(plan, recv, out=self.grads, err=self.err)
         pos = np.asarray([slot_of[int(b)] for b in plan.out_blocks], np.int64)
-        ids = (pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)
         self.exchange_rows += int(send.shape[0])
-        return pos, self._ops.i64_to_device(ids, self.device)
+        # the owner's visible slots are its camera set's positions: reuse the
+        # device row ids prepared for that set
+        set_pos, set_ids = self.vis_sets[k % self.sched.n_sets]
+        if not np.array_equal(pos, set_pos):
+            raise RuntimeError("exchange plan and owner visibility disagree")
+        return pos, set_ids
 
     def adam(self, ids: torch.Tensor, timed: bool):
         _lib = self._lib
@@ -350,21 +354,43 @@ class DeviceStep:
             e1.record()
             self.adam_ms.append((e0, e1, n))
 
+    phase_ms = None  # {phase: [ms, ...]} when per-phase timing is on
+
+    def _phase(self, name):
+        if self.phase_ms is None:
+            return
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self._events.append((name, ev))
+
+    def collect_phases(self):
+        if self.phase_ms is None:
+            return
+        torch.cuda.synchronize()
+        for (_, e0), (name, e1) in zip(self._events, self._events[1:]):
+            self.phase_ms.setdefault(name, []).append(e0.elapsed_time(e1))
+        self._events = []
+
     def step(self, k: int, timed: bool = False) -> int:
         _ops = self._ops
         sched = self.sched
+        self._events = []
+        self._phase("start")
         if self.world > 1:
             # 0. gradients of blocks rendered on other ranks reach their owners
             pos, ids = self.exchange_grads(k)
+            self._phase("exchange")
         else:
             pos, ids = self.vis_sets[k % sched.n_sets]
         # 1. optimizer over the visible rows
         self.adam(ids, timed)
+        self._phase("adam")
         # 2. updated blocks are dirty; refresh their bounds
         updated = sched.slot_block[pos]
         _ops.dirty_mark(self.bitmap, updated.tolist(), True)
         _ops.block_bounds(self.arena["xyz"], (pos * B).tolist(), [B] * pos.size,
                           self.bounds[: pos.size])
+        self._phase("dirty_bounds")
         # 3. evict 512 slots: write back the dirty ones
         evict_pos, incoming, dirty = sched.turnover(k)
         # half of the evicted blocks were never touched before: mark a random
@@ -378,14 +404,17 @@ class DeviceStep:
         _ops.pack_rows(self.arena, [p * B for p in wb_pos], [B] * len(wb_pos),
                        self.wb_staging[: len(wb_pos) * B], self._lib.LAYOUT_CACHE)
         _ops.dirty_mark(self.bitmap, wb_ids, False)
+        self._phase("writeback")
         # 4. materialize the incoming blocks into the freed slots
         src = self.incoming_pool[(k % 2) * TURNOVER * B:(k % 2 + 1) * TURNOVER * B]
         ids_dev = _ops.i64_to_device(incoming, self.device)
         _ops.unpack_rows(src, self._lib.LAYOUT_CACHE, self.loading, 0,
                          global_ids=self.loading_gids, block_ids=ids_dev, block_size=B)
+        self._phase("unpack")
         _ops.copy_blocks(self.loading, self.loading_gids, self.arena, self.gids,
                          (np.arange(TURNOVER) * B).tolist(), (evict_pos * B).tolist(),
                          [B] * TURNOVER, self.device)
+        self._phase("slot_copy")
         sched.slot_block[evict_pos] = incoming
         for other in self.scheds:  # replicas of the other owners' schedules
             if other is not sched:
@@ -395,6 +424,7 @@ class DeviceStep:
         self.slot_stamp.copy_(torch.from_numpy(self.stamp_host.view(np.int32)).pin_memory(),
                               non_blocking=True)
         self.slot_step[torch.from_numpy(evict_pos).to(self.device)] = 0
+        self._phase("tables")
         return int(ids.numel())
 
     def adam_stats(self):
@@ -484,6 +514,11 @@ class ApiStep:
                                for n, w in WIDTHS.items()}
             self.send_buf = torch.empty((send_max * B, 59), device=device)
             self.recv_buf = torch.empty((recv_max * B, 59), device=device)
+        # page-lock the write-back staging once, at its largest size (every
+        # evicted block dirty), instead of growing it inside timed steps
+        for _ in range(2):
+            _, _, ready = self.ws._acquire_writeback_staging(TURNOVER * B)
+            ready.set()
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         torch.cuda.synchronize()
@@ -523,9 +558,11 @@ class ApiStep:
         recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
         grads = self.exchange.reduce(plan, recv, out=self.grads)
         starts = np.asarray([slices[int(b)].start for b in plan.out_blocks], np.int64)
-        ids_host = torch.from_numpy((starts[:, None] + np.arange(B)[None, :]).reshape(-1))
+        ids_host = self.ids_pinned[k % self.sched.n_sets]
+        if not np.array_equal(starts, ids_host[::B].numpy()):
+            raise RuntimeError("exchange plan and owner slices disagree")
         self.h2d_bytes += ids_host.numel() * 8
-        return ids_host.pin_memory().to(self.device, non_blocking=True), grads
+        return ids_host.to(self.device, non_blocking=True), grads
 
     def step(self, k: int) -> int:
         """One iteration in the engine's order: the resident plan for k+1 is
@@ -670,6 +707,9 @@ def main(argv=None):
                     help="resident slots per GPU (default: the configs[3] value; smaller "
                          "values make small profiling cases of the same step)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--phase-times", action="store_true",
+                    help="print a per-phase CUDA-event breakdown of the device step to stderr "
+                         "(extra events; not used for the reported value)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
@@ -699,6 +739,16 @@ def main(argv=None):
         rows += dev.step(k, timed=True)
     end.record()
     torch.cuda.synchronize()
+    if args.phase_times:
+        # separate, untimed pass: per-phase CUDA events around each stage
+        dev.phase_ms = {}
+        for k in range(args.warmup + args.steps, args.warmup + args.steps + 3):
+            dev.step(k)
+            dev.collect_phases()
+        print(f"rank {rank} device phase ms/step: " + json.dumps(
+            {n: round(sum(v) / len(v), 3) for n, v in dev.phase_ms.items()}),
+            file=sys.stderr, flush=True)
+        dev.phase_ms = None
     barrier(world)
     clock_info = clocks.stop()
     launches = _lib.launch_counter["kernels"] - launches0

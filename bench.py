@@ -421,8 +421,7 @@ class DeviceStep:
                 ev, inc, _ = other.turnover(k)
                 other.slot_block[ev] = inc
         self.stamp_host[evict_pos] += 1
-        self.slot_stamp.copy_(torch.from_numpy(self.stamp_host.view(np.int32)).pin_memory(),
-                              non_blocking=True)
+        _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
         self.slot_step[torch.from_numpy(evict_pos).to(self.device)] = 0
         self._phase("tables")
         return int(ids.numel())
@@ -543,8 +542,7 @@ class ApiStep:
             ids_host = self.ids_pinned[k % self.sched.n_sets]
             n = ids_host.numel()
             self.h2d_bytes += n * 8
-            return ids_host.to(self.device, non_blocking=True), {
-                name: g[:n] for name, g in self.grads.items()}
+            return self._upload_ids(ids_host), {name: g[:n] for name, g in self.grads.items()}
         from tidegs_b200.sharded import make_plan
 
         W, me = self.world, self.rank
@@ -562,7 +560,17 @@ class ApiStep:
         if not np.array_equal(starts, ids_host[::B].numpy()):
             raise RuntimeError("exchange plan and owner slices disagree")
         self.h2d_bytes += ids_host.numel() * 8
-        return ids_host.to(self.device, non_blocking=True), grads
+        return self._upload_ids(ids_host), grads
+
+    def _upload_ids(self, ids_host: torch.Tensor) -> torch.Tensor:
+        """Row ids from page-locked memory, read by a kernel (not queued
+        behind the prefetch's block DMA on the copy engine)."""
+        from tidegs_b200 import _lib
+
+        out = torch.empty(ids_host.numel(), dtype=torch.int64, device=self.device)
+        _lib.call("tgs_copy_small", out.data_ptr(), ids_host.data_ptr(), ids_host.numel() * 8,
+                  torch.cuda.current_stream(self.device).cuda_stream)
+        return out
 
     def step(self, k: int) -> int:
         """One iteration in the engine's order: the resident plan for k+1 is

@@ -293,6 +293,16 @@ TGS_API int tgs_global_to_local_compact_noalloc(int64_t* out, int64_t* dev_count
                                                 const int64_t* block_starts, int64_t num_blocks,
                                                 int64_t block_size, void* stream);
 
+/* Copies `bytes` from src to dst with a kernel on `stream` (src/dst: device
+ * memory or page-locked host memory, which the device reads directly). Used
+ * for the small per-step tables (row ids, plans, layouts): as kernels they are
+ * ordered on the compute stream and never wait behind multi-GB block DMA
+ * queued on the copy engines by the prefetch stream. Addresses must be
+ * 4-byte aligned (16-byte aligned pairs take 16-byte accesses). No reference
+ * counterpart (the reference uploads such tables with torch.tensor(...,
+ * device=...) copies). */
+TGS_API int tgs_copy_small(void* dst, const void* src, int64_t bytes, void* stream);
+
 /* Issues one cudaMemcpyAsync per block (host -> device) so pinned host blocks
  * reach the device staging buffer without a CPU-side pack. host_src[k] is a
  * host pointer, dev_dst[k] a device pointer, bytes[k] the size (all host

@@ -129,6 +129,7 @@ SIGNATURES = {
     "tgs_pack_rows": (C.c_int, [C.POINTER(PackArgs), _vp]),
     "tgs_block_bounds": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp]),
     "tgs_block_grad_sum": (C.c_int, [C.POINTER(BlockSumArgs), _vp]),
+    "tgs_copy_small": (C.c_int, [_vp, _vp, _i64, _vp]),
 }
 
 _lock = threading.Lock()
@@ -175,7 +176,7 @@ KERNELS_PER_CALL = {
     "tgs_build_block_starts": 1, "tgs_global_to_local": 1, "tgs_global_to_local_compact": 3,
     "tgs_global_to_local_compact_noalloc": 3,
     "tgs_dirty_mark": 1, "tgs_dirty_select": 1, "tgs_dirty_list": 1, "tgs_pack_rows": 1,
-    "tgs_block_bounds": 1, "tgs_block_grad_sum": 1,
+    "tgs_block_bounds": 1, "tgs_block_grad_sum": 1, "tgs_copy_small": 1,
 }
 launch_counter = {"kernels": 0}
 

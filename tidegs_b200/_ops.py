@@ -3,6 +3,8 @@ libtidegs_b200.so, shared by the working-set classes. Every function enqueues
 on the current CUDA stream of the tensors' device and raises on failure."""
 from __future__ import annotations
 
+import collections
+import threading
 from typing import Dict, Iterable, List, Mapping, Optional, Sequence
 
 import numpy as np
@@ -20,13 +22,55 @@ def _stream(device: torch.device) -> int:
     return _lib.stream_handle(device)
 
 
+class _HostTables:
+    """Page-locked host copies of small per-step tables, read on the device by
+    tgs_copy_small. A table stays referenced until an event recorded after
+    the kernel that reads it has completed (the caching host allocator only
+    tracks copies it issued itself)."""
+
+    def __init__(self):
+        self._lock = threading.Lock()
+        self._inflight = collections.deque()
+
+    def stage(self, arr: np.ndarray) -> torch.Tensor:
+        with self._lock:
+            while self._inflight and self._inflight[0][1].query():
+                self._inflight.popleft()
+        return torch.from_numpy(arr).pin_memory()
+
+    def retire(self, host: torch.Tensor, stream: torch.cuda.Stream) -> None:
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        with self._lock:
+            self._inflight.append((host, ev))
+
+
+_TABLES = _HostTables()
+
+
+def upload_into(dst: torch.Tensor, values) -> torch.Tensor:
+    """Writes host `values` (numpy-compatible, dst's dtype) into the contiguous
+    device tensor dst with a kernel on the current stream, so the upload is
+    ordered with the compute work and never waits behind bulk DMA."""
+    arr = np.ascontiguousarray(np.asarray(values).reshape(-1))
+    if arr.size == 0:
+        return dst
+    if arr.nbytes != dst.numel() * dst.element_size() or not dst.is_contiguous():
+        raise RuntimeError("upload_into: size or layout mismatch")
+    host = _TABLES.stage(arr)
+    stream = torch.cuda.current_stream(dst.device)
+    _lib.call("tgs_copy_small", dst.data_ptr(), host.data_ptr(), arr.nbytes, stream.cuda_stream)
+    _TABLES.retire(host, stream)
+    return dst
+
+
 def i64_to_device(values, device: torch.device) -> torch.Tensor:
-    """Host ints -> device int64 via a page-locked staging copy."""
+    """Host ints -> device int64 (kernel upload from a page-locked copy)."""
     arr = np.ascontiguousarray(np.asarray(values, dtype=np.int64).reshape(-1))
-    host = torch.from_numpy(arr)
-    if host.numel() == 0:
-        return torch.empty(0, dtype=torch.int64, device=device)
-    return host.pin_memory().to(device, non_blocking=True)
+    out = torch.empty(arr.size, dtype=torch.int64, device=device)
+    if arr.size:
+        upload_into(out, arr)
+    return out
 
 
 def _comp_ptrs(components: Mapping[str, torch.Tensor], who: str) -> List[int]:

@@ -46,6 +46,50 @@ extern "C" int tgs_last_error(char* buf, size_t len) {
   return static_cast<int>(n);
 }
 
+namespace tgs {
+namespace {
+
+__global__ void copy_words_kernel(uint32_t* __restrict__ dst, const uint32_t* __restrict__ src,
+                                  int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+
+__global__ void copy_vec4_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                 int64_t n) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = src[i];
+}
+
+}  // namespace
+}  // namespace tgs
+
+extern "C" int tgs_copy_small(void* dst, const void* src, int64_t bytes, void* stream) {
+  TGS_CHECK_ARG(bytes >= 0, "tgs_copy_small: bytes < 0");
+  if (bytes == 0) return TGS_OK;
+  TGS_CHECK_ARG(dst && src, "tgs_copy_small: NULL pointer");
+  TGS_CHECK_ARG((bytes & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 3) == 0 &&
+                    (reinterpret_cast<uintptr_t>(src) & 3) == 0,
+                "tgs_copy_small: addresses and size must be 4-byte aligned");
+  cudaStream_t s = tgs::as_stream(stream);
+  const int64_t cap = static_cast<int64_t>(tgs::sm_count()) * 4;
+  if ((bytes & 15) == 0 && tgs::aligned16(dst) && tgs::aligned16(src)) {
+    const int64_t n = bytes / 16;
+    const int grid = static_cast<int>(std::min<int64_t>(tgs::ceil_div<int64_t>(n, 256), cap));
+    tgs::copy_vec4_kernel<<<grid, 256, 0, s>>>(static_cast<uint4*>(dst),
+                                               static_cast<const uint4*>(src), n);
+  } else {
+    const int64_t n = bytes / 4;
+    const int grid = static_cast<int>(std::min<int64_t>(tgs::ceil_div<int64_t>(n, 256), cap));
+    tgs::copy_words_kernel<<<grid, 256, 0, s>>>(static_cast<uint32_t*>(dst),
+                                                static_cast<const uint32_t*>(src), n);
+  }
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
 extern "C" int tgs_h2d_blocks(void* const* dev_dst, const void* const* host_src,
                               const int64_t* bytes, int32_t n, void* stream) {
   TGS_CHECK_ARG(n >= 0, "tgs_h2d_blocks: n=%d < 0", n);

@@ -24,7 +24,7 @@ from typing import Any, Dict, List, Optional, Tuple
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, _ops
 
 # Float index of the admission stamp inside a 128-float state row (the first
 # word of the float4 owned by lane 31 in the update kernel).
@@ -92,12 +92,8 @@ class GPUResidentAdam:
         self._step_tables: Dict[Tuple[float, float], Tuple[torch.Tensor, int, bool]] = {}
         self._slot_tables_dirty = False
 
-        # Reusable pinned buffers for layout uploads / count read-back.
-        self._pin_layout: Optional[torch.Tensor] = None
-        self._pin_slots: Optional[torch.Tensor] = None
+        # Reusable buffers for the per-position count read-back.
         self._pin_counts: Optional[torch.Tensor] = None
-        self._dev_layout: Optional[torch.Tensor] = None
-        self._dev_slots: Optional[torch.Tensor] = None
         self._dev_counts: Optional[torch.Tensor] = None
 
         self._logical_state_blocks = 0
@@ -190,10 +186,8 @@ class GPUResidentAdam:
         """Publishes host step / stamp mirrors after (re)admissions."""
         if not self._slot_tables_dirty:
             return
-        steps = torch.from_numpy(self._slot_steps.astype(np.int32)).pin_memory()
-        stamps = torch.from_numpy(self._slot_stamp.view(np.int32).copy()).pin_memory()
-        self._slot_step_dev.copy_(steps, non_blocking=True)
-        self._slot_stamp_dev.copy_(stamps, non_blocking=True)
+        _ops.upload_into(self._slot_step_dev, self._slot_steps.astype(np.int32))
+        _ops.upload_into(self._slot_stamp_dev, self._slot_stamp.view(np.int32))
         self._slot_tables_dirty = False
 
     def set_resident_blocks(self, block_ids: List[int]) -> None:
@@ -296,22 +290,17 @@ class GPUResidentAdam:
         return starts, ends, arr[:, 2], arr[:, 3]
 
     def _stage_layout(self, starts, ends, slots) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Device copies of the layout tables, uploaded by kernels on the
+        current stream (never queued behind bulk DMA on the copy engines)."""
         P = int(starts.shape[0])
-        if self._pin_layout is None or self._pin_layout.shape[1] < P:
+        if self._pin_counts is None or self._pin_counts.numel() < P + 4:
             cap = max(P, 64)
-            self._pin_layout = torch.empty((2, cap), dtype=torch.int64, pin_memory=True)
-            self._pin_slots = torch.empty(cap, dtype=torch.int32, pin_memory=True)
             self._pin_counts = torch.empty(cap + 4, dtype=torch.int32, pin_memory=True)
-            self._dev_layout = torch.empty((2, cap), dtype=torch.int64, device=self.device)
-            self._dev_slots = torch.empty(cap, dtype=torch.int32, device=self.device)
             self._dev_counts = torch.empty(cap, dtype=torch.int32, device=self.device)
-        pl = self._pin_layout.numpy()
-        pl[0, :P] = starts
-        pl[1, :P] = ends
-        self._pin_slots.numpy()[:P] = slots
-        self._dev_layout[:, :P].copy_(self._pin_layout[:, :P], non_blocking=True)
-        self._dev_slots[:P].copy_(self._pin_slots[:P], non_blocking=True)
-        return self._dev_layout[0], self._dev_layout[1], self._dev_slots
+        bounds = _ops.i64_to_device(np.concatenate([starts, ends]), self.device)
+        dev_slots = torch.empty(P, dtype=torch.int32, device=self.device)
+        _ops.upload_into(dev_slots, np.asarray(slots, dtype=np.int32))
+        return bounds[:P], bounds[P:], dev_slots
 
     def step(
         self,

@@ -170,8 +170,15 @@ class Schedule:
         self.slot_block = self.rng.choice(self.pool_ids, SLOTS, replace=False)
         self.n_sets = n_cameras_sets
 
+    _vis_cache: dict = {}
+
     def visible_positions(self, step: int) -> np.ndarray:
-        """Union over 16 cameras of contiguous runs of slots, ~30 % visible."""
+        """Union over 16 cameras of contiguous runs of slots, ~30 % visible
+        (the same runs for every owner; cached per camera set)."""
+        key = (SLOTS, step % self.n_sets)
+        hit = Schedule._vis_cache.get(key)
+        if hit is not None:
+            return hit
         rng = np.random.default_rng(10_000 + step % self.n_sets)
         vis = np.zeros(SLOTS, bool)
         scale = SLOTS / 2048.0
@@ -179,15 +186,27 @@ class Schedule:
             length = max(1, int(rng.integers(24, 56) * scale))
             start = int(rng.integers(0, max(1, SLOTS - length)))
             vis[start:start + length] = True
-        return np.nonzero(vis)[0]
+        out = np.nonzero(vis)[0]
+        out.setflags(write=False)
+        Schedule._vis_cache[key] = out
+        return out
 
     def turnover(self, step: int):
         rng = np.random.default_rng(20_000 + step)
         evict_pos = np.sort(rng.choice(SLOTS, TURNOVER, replace=False))
-        candidates = np.setdiff1d(self.pool_ids, self.slot_block, assume_unique=True)
+        # pool blocks not resident, ascending (pool_ids is ascending)
+        resident = np.zeros(self.pool_ids.size, bool)
+        resident[(self.slot_block - self.rank) // self.world] = True
+        candidates = self.pool_ids[~resident]
         incoming = np.sort(rng.choice(candidates, TURNOVER, replace=False))
         dirty = rng.random(TURNOVER) < 0.5
         return evict_pos, incoming, dirty
+
+    def slot_table(self) -> np.ndarray:
+        """Dense block id -> slot position table (-1: not resident)."""
+        table = np.full(int(self.pool_ids[-1]) + 1, -1, np.int64)
+        table[self.slot_block] = np.arange(SLOTS, dtype=np.int64)
+        return table
 
 
 def fill_params(comps, gen):
@@ -220,8 +239,27 @@ def rank_visible_positions(sched: "Schedule", step: int, world: int, rank: int) 
     return pos[lo:hi]
 
 
+def rendered_blocks(scheds, step: int, world: int):
+    """Block ids whose gradients each rank renders at `step` (every owner's
+    share for that rank)."""
+    return [np.concatenate([o.slot_block[rank_visible_positions(o, step, world, r)]
+                            for o in scheds]) for r in range(world)]
+
+
+def exchange_capacity(sched: "Schedule", scheds, world: int):
+    """(blocks a rank renders, tiles an owner receives): the largest over the
+    periodic camera sets."""
+    send_max = recv_max = 0
+    for s_ in range(sched.n_sets):
+        mine = sum(rank_visible_positions(o, s_, world, sched.rank).size for o in scheds)
+        theirs = sum(rank_visible_positions(sched, s_, world, r).size for r in range(world))
+        send_max, recv_max = max(send_max, mine), max(recv_max, theirs)
+    return send_max, recv_max
+
+
 class DeviceStep:
-    def __init__(self, device, sched: Schedule, scheds=None, world: int = 1):
+    def __init__(self, device, sched: Schedule, scheds=None, world: int = 1,
+                 exchange: str = "pull"):
         from tidegs_b200 import _lib, _ops
 
         self._lib, self._ops = _lib, _ops
@@ -270,21 +308,30 @@ class DeviceStep:
             max_rows = max(max_rows, ids.size)
         self.grads = {n: torch.empty((max_rows, w), device=device).normal_(0, 1e-3, generator=gen)
                       for n, w in WIDTHS.items()}
+        self.exchange_mode = exchange if world > 1 else None
+        self.peer = None
+        self.pull = None
+        self.plan = None
         if world > 1:
             # gradients this rank renders for blocks of every owner, and the
             # exchange buffers (sizes: the largest of the periodic camera sets)
-            from tidegs_b200.sharded import BlockGradExchange
-
-            self.exchange = BlockGradExchange(B, device=device)
-            send_max = recv_max = 0
-            for s_ in range(sched.n_sets):
-                mine = sum(rank_visible_positions(o, s_, world, sched.rank).size for o in self.scheds)
-                theirs = sum(rank_visible_positions(sched, s_, world, r).size for r in range(world))
-                send_max, recv_max = max(send_max, mine), max(recv_max, theirs)
+            send_max, recv_max = exchange_capacity(sched, self.scheds, world)
             self.rank_grads = {n: torch.empty((send_max * B, w), device=device).normal_(
                 0, 1e-3, generator=gen) for n, w in WIDTHS.items()}
-            self.send_buf = torch.empty((send_max * B, 59), device=device)
-            self.recv_buf = torch.empty((recv_max * B, 59), device=device)
+            if exchange == "pull":
+                from tidegs_b200.sharded import PeerGradPull
+
+                self.pull = PeerGradPull(self.rank_grads, B, device)
+            elif exchange == "push":
+                from tidegs_b200.sharded import PeerGradExchange
+
+                self.peer = PeerGradExchange(B, capacity_blocks=recv_max, device=device)
+            else:
+                from tidegs_b200.sharded import BlockGradExchange
+
+                self.exchange = BlockGradExchange(B, device=device)
+                self.send_buf = torch.empty((send_max * B, 59), device=device)
+                self.recv_buf = torch.empty((recv_max * B, 59), device=device)
             self.exchange_rows = 0
         self.adam_ms = []
         self.updated_rows = []
@@ -297,20 +344,29 @@ class DeviceStep:
         from tidegs_b200.sharded import make_plan
 
         W, me = self.world, self.sched.rank
-        vis = []
-        for r in range(W):
-            vis.append(np.concatenate([o.slot_block[rank_visible_positions(o, k, W, r)]
-                                       for o in self.scheds]))
-        own = self.sched
-        slot_of = {int(b): i for i, b in enumerate(own.slot_block)}
+        vis = rendered_blocks(self.scheds, k, W)
+        slot_of = self.sched.slot_table()
         plan = make_plan(vis, W, me, B, out_order=slot_of)
-        order = np.unique(vis[me])
-        start = {int(b): i * B for i, b in enumerate(order)}
-        send = self.exchange.pack(plan, self.rank_grads, start, out=self.send_buf)
-        recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
-        self.exchange.reduce(plan, recv, out=self.grads, err=self.err)
-        pos = np.asarray([slot_of[int(b)] for b in plan.out_blocks], np.int64)
-        self.exchange_rows += int(send.shape[0])
+        # the rank's rendered gradients: its blocks in ascending id, B rows each
+        starts = np.searchsorted(np.unique(vis[me]), plan.send_blocks).astype(np.int64) * B
+        self._phase("plan")
+        if self.pull is not None:
+            # the owner's update kernel sums the senders' gradients itself
+            self.plan = plan
+            self.exchange_rows += int(plan.send_blocks.size) * B
+        elif self.peer is not None:
+            self.exchange_rows += self.peer.push(plan, self.rank_grads, starts, parity=k)
+            self._phase("push")
+            self.peer.barrier()
+            self._phase("barrier")
+            self.peer.reduce(plan, parity=k, out=self.grads, err=self.err)
+            self._phase("owner_sum")
+        else:
+            send = self.exchange.pack(plan, self.rank_grads, starts, out=self.send_buf)
+            recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
+            self.exchange.reduce(plan, recv, out=self.grads, err=self.err)
+            self.exchange_rows += int(send.shape[0])
+        pos = slot_of[plan.out_blocks]
         # the owner's visible slots are its camera set's positions: reuse the
         # device row ids prepared for that set
         set_pos, set_ids = self.vis_sets[k % self.sched.n_sets]
@@ -345,14 +401,21 @@ class DeviceStep:
         a.local_ids, a.n_rows = ids.data_ptr(), n
         a.state, a.slot_stamp = self.state.data_ptr(), self.slot_stamp.data_ptr()
         a.slot_bias, a.err = self.slot_bias.data_ptr(), self.err.data_ptr()
+        if self.pull is not None:
+            self.pull.barrier()  # every rank's gradients of this step are written
         if timed:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-        _lib.call("tgs_resident_adam_apply", a, stream)
+        if self.pull is not None:
+            self.pull.launch(a, self.plan, stream)
+        else:
+            _lib.call("tgs_resident_adam_apply", a, stream)
         if timed:
             e1.record()
             self.adam_ms.append((e0, e1, n))
+        if self.pull is not None:
+            self.pull.barrier()  # no owner still reads this step's gradients
 
     phase_ms = None  # {phase: [ms, ...]} when per-phase timing is on
 
@@ -426,6 +489,14 @@ class DeviceStep:
         self._phase("tables")
         return int(ids.numel())
 
+    def close(self):
+        """Releases the peer mappings (collective over the ranks)."""
+        for attr in ("peer", "pull"):
+            obj = getattr(self, attr)
+            if obj is not None:
+                obj.close()
+                setattr(self, attr, None)
+
     def adam_stats(self):
         ms = [e0.elapsed_time(e1) for e0, e1, _ in self.adam_ms]
         rows = [n for _, _, n in self.adam_ms]
@@ -454,7 +525,8 @@ class ApiStep:
             return now
         return t
 
-    def __init__(self, device, scheds, rank: int, world: int, pool_blocks: int):
+    def __init__(self, device, scheds, rank: int, world: int, pool_blocks: int,
+                 exchange: str = "pull"):
         import types
 
         from tidegs_b200 import (BlockLayout, DoubleBufferGPUWorkingSet, GPUResidentAdam,
@@ -499,20 +571,26 @@ class ApiStep:
         max_rows = max(t.numel() for t in self.ids_pinned)
         self.grads = {n: torch.empty((max_rows, w), device=device).normal_(0, 1e-3)
                       for n, w in WIDTHS.items()}
+        self.peer = None
+        self.pull = None
         if world > 1:
-            from tidegs_b200.sharded import BlockGradExchange
-
-            self.exchange = BlockGradExchange(B, device=device)
-            send_max = recv_max = 0
-            for s_ in range(sched.n_sets):
-                send_max = max(send_max, sum(rank_visible_positions(o, s_, world, rank).size
-                                             for o in scheds))
-                recv_max = max(recv_max, sum(rank_visible_positions(sched, s_, world, r).size
-                                             for r in range(world)))
+            send_max, recv_max = exchange_capacity(sched, scheds, world)
             self.rank_grads = {n: torch.empty((send_max * B, w), device=device).normal_(0, 1e-3)
                                for n, w in WIDTHS.items()}
-            self.send_buf = torch.empty((send_max * B, 59), device=device)
-            self.recv_buf = torch.empty((recv_max * B, 59), device=device)
+            if exchange == "pull":
+                from tidegs_b200.sharded import PeerGradPull
+
+                self.pull = PeerGradPull(self.rank_grads, B, device)
+            elif exchange == "push":
+                from tidegs_b200.sharded import PeerGradExchange
+
+                self.peer = PeerGradExchange(B, capacity_blocks=recv_max, device=device)
+            else:
+                from tidegs_b200.sharded import BlockGradExchange
+
+                self.exchange = BlockGradExchange(B, device=device)
+                self.send_buf = torch.empty((send_max * B, 59), device=device)
+                self.recv_buf = torch.empty((recv_max * B, 59), device=device)
         # page-lock the write-back staging once, at its largest size (every
         # evicted block dirty), instead of growing it inside timed steps
         for _ in range(2):
@@ -537,7 +615,8 @@ class ApiStep:
         g._rotation, g._features_dc, g._features_rest = act.rotation, act.features_dc, act.features_rest
 
     def _grads_and_ids(self, k: int):
-        """(sparse_grad_local_ids, sparse_grad_components) of this owner."""
+        """(sparse_grad_local_ids, sparse_grad_components or (pull, plan)) of
+        this owner."""
         if self.world == 1:
             ids_host = self.ids_pinned[k % self.sched.n_sets]
             n = ids_host.numel()
@@ -546,21 +625,38 @@ class ApiStep:
         from tidegs_b200.sharded import make_plan
 
         W, me = self.world, self.rank
-        vis = [np.concatenate([o.slot_block[rank_visible_positions(o, k, W, r)] for o in self.scheds])
-               for r in range(W)]
-        slices = self.db.active_buffer.block_to_local_slice
-        plan = make_plan(vis, W, me, B, out_order={b: s.start for b, s in slices.items()})
-        order = np.unique(vis[me])
-        send = self.exchange.pack(plan, self.rank_grads, {int(b): i * B for i, b in enumerate(order)},
-                                  out=self.send_buf)
-        recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
-        grads = self.exchange.reduce(plan, recv, out=self.grads)
-        starts = np.asarray([slices[int(b)].start for b in plan.out_blocks], np.int64)
+        vis = rendered_blocks(self.scheds, k, W)
+        # slice position i of the active buffer holds sched.slot_block[i]
+        slot_of = self.sched.slot_table()
+        plan = make_plan(vis, W, me, B, out_order=slot_of)
+        starts = np.searchsorted(np.unique(vis[me]), plan.send_blocks).astype(np.int64) * B
+        if self.pull is not None:
+            grads = (self.pull, plan)
+        elif self.peer is not None:
+            self.peer.push(plan, self.rank_grads, starts, parity=k)
+            self.peer.barrier()
+            grads = self.peer.reduce(plan, parity=k, out=self.grads)
+        else:
+            send = self.exchange.pack(plan, self.rank_grads, starts, out=self.send_buf)
+            recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
+            grads = self.exchange.reduce(plan, recv, out=self.grads)
+        rows = slot_of[plan.out_blocks] * B
         ids_host = self.ids_pinned[k % self.sched.n_sets]
-        if not np.array_equal(starts, ids_host[::B].numpy()):
+        slices = self.db.active_buffer.block_to_local_slice
+        probe = plan.out_blocks[:: max(1, plan.n_out // 16)]
+        if (not np.array_equal(rows, ids_host[::B].numpy())
+                or any(slices[int(b)].start != slot_of[int(b)] * B for b in probe)):
             raise RuntimeError("exchange plan and owner slices disagree")
         self.h2d_bytes += ids_host.numel() * 8
         return self._upload_ids(ids_host), grads
+
+    def close(self):
+        """Releases the peer mappings (collective over the ranks)."""
+        for attr in ("peer", "pull"):
+            obj = getattr(self, attr)
+            if obj is not None:
+                obj.close()
+                setattr(self, attr, None)
 
     def _upload_ids(self, ids_host: torch.Tensor) -> torch.Tensor:
         """Row ids from page-locked memory, read by a kernel (not queued
@@ -591,7 +687,10 @@ class ApiStep:
         t = self._mark("start_prefetch", t)
         ids, grads = self._grads_and_ids(k)
         t = self._mark("exchange", t)
-        stats = self.opt.step(k, self.gaussians, ids, grads)
+        if isinstance(grads, tuple):
+            stats = self.opt.step_pulled(k, self.gaussians, ids, *grads)
+        else:
+            stats = self.opt.step(k, self.gaussians, ids, grads)
         t = self._mark("adam_step", t)
         updated = stats["updated_block_ids"]
         db.mark_dirty_blocks(updated)
@@ -719,6 +818,10 @@ def main(argv=None):
                     help="print a per-phase CUDA-event breakdown of the device step to stderr "
                          "(extra events; not used for the reported value)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="pull", choices=["pull", "push", "nccl"],
+                    help="N>1 gradient exchange: the owner's update kernel sums the senders' "
+                         "gradients over NVLink (pull, default); a push kernel into receive "
+                         "buffers + owner sum (push); or pack + NCCL all-to-all + owner sum")
     args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     set_slots(args.slots)
@@ -731,7 +834,7 @@ def main(argv=None):
     device = torch.device("cuda", torch.cuda.current_device())
     scheds = [Schedule(o, world) for o in range(world)]
     sched = scheds[rank]
-    dev = DeviceStep(device, sched, scheds=scheds, world=world)
+    dev = DeviceStep(device, sched, scheds=scheds, world=world, exchange=args.exchange)
     for k in range(args.warmup):
         dev.step(k)
     torch.cuda.synchronize()
@@ -769,6 +872,8 @@ def main(argv=None):
     adam_bytes = ADAM_BYTES_PER_ROW * (sum(adam_rows) / len(adam_rows))
     achieved = adam_bytes / (adam_avg_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
+    exchange_rows = getattr(dev, "exchange_rows", 0)
+    dev.close()
     del dev
     torch.cuda.empty_cache()
 
@@ -778,7 +883,7 @@ def main(argv=None):
         if args.no_e2e:
             raise _Skipped("--no-e2e")
         api = ApiStep(device, [Schedule(o, world) for o in range(world)], rank, world,
-                      args.pool_blocks)
+                      args.pool_blocks, exchange=args.exchange)
         for k in range(args.e2e_warmup):
             api.step(k)
         torch.cuda.synchronize()
@@ -805,6 +910,7 @@ def main(argv=None):
                 + " writeback staging bytes: "
                 + str(api.ws.writeback_stats["pinned_staging_bytes"]),
                 file=sys.stderr, flush=True)
+        api.close()
         del api
     except _Skipped as why:
         e2e = {"value": None, "unit": UNIT, "skipped": str(why)}
@@ -827,6 +933,13 @@ def main(argv=None):
                        "slots_per_gpu": SLOTS, "block_size": B, "turnover_blocks": TURNOVER,
                        "rows_updated_per_step": rows / args.steps,
                        "parallelism": f"block ownership, rank = block_id mod {world}",
+                       "exchange_rows_per_step": exchange_rows / (args.warmup + args.steps),
+                       "exchange": (None if world == 1 else
+                                    "owner update kernel sums senders' gradients over NVLink "
+                                    "(tgs_resident_adam_apply_sum)" if args.exchange == "pull"
+                                    else "direct NVLink push (tgs_grad_push) + ordered owner sum"
+                                    if args.exchange == "push" else
+                                    "pack + NCCL all-to-all + ordered owner sum"),
                        "l2": "every input larger than L2 (126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None,

@@ -7,7 +7,9 @@
  *     struct is a DEVICE pointer unless its comment says "host".
  *   - The library allocates nothing and keeps no per-call state: every buffer,
  *     including scratch words, is owned by the caller. Calls are re-entrant and
- *     may come from several host threads on different streams.
+ *     may come from several host threads on different streams. The one
+ *     exception is tgs_peer_buffer_alloc, which allocates the exportable
+ *     buffer its caller asks for and hands its ownership to that caller.
  *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream).
  *     All work is enqueued on it; no entry point synchronizes the device.
  *   - Return value: 0 (TGS_OK) or a TGS_ERR_* code. The message of the last
@@ -376,6 +378,83 @@ typedef struct {
 /* out block k = sum of its contributions, added in listed (sender) order with
  * one rounding per addition, written as the six SoA gradient components. */
 TGS_API int tgs_block_grad_sum(const TgsBlockSumArgs* args, void* stream);
+
+/* Direct push over peer memory: the pack and the all-to-all above in one
+ * kernel. Each rank writes its UNIFIED tiles straight into the owners'
+ * receive buffers (NVLink stores through CUDA IPC mappings), at the rows an
+ * all-to-all would have put them, so tgs_block_grad_sum runs unchanged on the
+ * owner. The caller orders the push before the owners' sums with a barrier
+ * across ranks (a collective on the same stream) and double-buffers the
+ * receive buffers, so that a push never overwrites tiles an owner still sums. */
+
+#define TGS_MAX_PEERS 64
+#define TGS_PEER_HANDLE_BYTES 64
+
+typedef struct {
+  unsigned char bytes[TGS_PEER_HANDLE_BYTES]; /* a cudaIpcMemHandle_t */
+} TgsPeerHandle;
+
+/* Device buffer of `bytes` (cudaMalloc, so that it can be exported) and its
+ * IPC handle. Free with tgs_peer_buffer_free after every peer closed it. */
+TGS_API int tgs_peer_buffer_alloc(int64_t bytes, void** dev_ptr, TgsPeerHandle* handle);
+TGS_API int tgs_peer_buffer_free(void* dev_ptr);
+/* Maps another process's buffer into the current device's address space
+ * (peer access enabled on first use). Unmap with tgs_peer_buffer_close. */
+TGS_API int tgs_peer_buffer_open(const TgsPeerHandle* handle, void** dev_ptr);
+TGS_API int tgs_peer_buffer_close(void* dev_ptr);
+
+typedef struct {
+  const float* comp[TGS_NUM_COMPONENTS]; /* this rank's gradients, SoA components */
+  const int64_t* src_start;       /* [n_tiles] first source row of each sent block */
+  const int64_t* row_count;       /* [n_tiles] rows of each sent block */
+  const int32_t* dst_rank;        /* [n_tiles] owner rank of each sent block */
+  const int64_t* dst_row;         /* [n_tiles] first row in the owner's receive buffer */
+  int32_t n_tiles;
+  int64_t max_rows;               /* max(row_count) */
+  float* recv[TGS_MAX_PEERS];     /* each rank's receive buffer as mapped here (own included) */
+  int64_t recv_rows[TGS_MAX_PEERS]; /* capacity of each receive buffer, rows */
+  int32_t n_ranks;
+  int32_t* err;                   /* [4] device error word (may be NULL) */
+} TgsGradPushArgs;
+
+/* recv[dst_rank[k]][dst_row[k] + i] = UNIFIED row src_start[k] + i of comp,
+ * i < row_count[k]. A tile that would land outside its receive buffer is
+ * skipped and reported in err (TGS_DEV_BAD_SLICE). */
+TGS_API int tgs_grad_push(const TgsGradPushArgs* args, void* stream);
+
+/* IPC handle of the allocation that contains dev_ptr (any device pointer,
+ * for example a tensor inside a caching allocator's segment) and dev_ptr's
+ * byte offset from that allocation's base. A peer maps the allocation with
+ * tgs_peer_buffer_open and adds the offset. */
+TGS_API int tgs_peer_export(const void* dev_ptr, TgsPeerHandle* handle, int64_t* offset);
+
+/* Owner-side reduction fused into the resident Adam step ("pull"): the
+ * gradient of compact row i is read from the senders' own gradient buffers
+ * (this rank's and peers' through IPC mappings, plain loads over NVLink) and
+ * summed in listed (rank) order, one rounding per addition, then the update
+ * of tgs_resident_adam_apply runs on it. Equal, bit for bit, to
+ * tgs_grad_push / all-to-all + tgs_block_grad_sum + tgs_resident_adam_apply,
+ * without the receive buffers, the push and the sum pass.
+ * Compact rows are split into segments (normally one per visible block);
+ * row i of segment s (seg_begin[s] <= i < seg_begin[s+1]) receives, for each
+ * contribution j of s, row contrib_row[j] + (i - seg_begin[s]) of rank
+ * contrib_rank[j]'s gradient components. The caller orders the senders'
+ * gradient writes before this kernel and this kernel before the senders'
+ * next writes (barriers across ranks on the stream). */
+typedef struct {
+  TgsResidentAdamArgs adam;         /* grad[] is not read (may be NULL) */
+  const float* const* grad_src;     /* [n_ranks * 6] rank r's component c at r*6+c, as mapped here */
+  const int64_t* grad_rows;         /* [n_ranks] rows of each rank's gradient components */
+  int32_t n_ranks;
+  const int64_t* seg_begin;         /* [n_segments + 1] ascending, 0 .. adam.n_rows */
+  int32_t n_segments;
+  const int64_t* contrib_offsets;   /* [n_segments + 1] CSR into contrib_rank / contrib_row */
+  const int32_t* contrib_rank;      /* [n_contrib] summation order inside a segment */
+  const int64_t* contrib_row;       /* [n_contrib] source row of the segment's first row */
+  int32_t* err;                     /* [4] the error word of adam.err, writable */
+} TgsResidentAdamSumArgs;
+
+TGS_API int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* args, void* stream);
 
 #ifdef __cplusplus
 }

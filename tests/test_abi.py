@@ -63,6 +63,39 @@ def test_struct_layouts_match_the_header_sizes():
     assert _lib.ResidentAdamArgs.batch_size.offset == 96 + 24 + 5 * 4
 
 
+def test_struct_offsets_match_the_c_compiler(tmp_path):
+    """Every field offset and struct size of the ctypes mirrors equals what a
+    C compiler computes from include/tidegs_b200.h."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    structs = {name: getattr(_lib, name) for name in (
+        "ResidentCountArgs", "ResidentAdamArgs", "DenseGroup", "DenseArgs", "UnpackArgs",
+        "CopyBlocksArgs", "PackArgs", "BlockSumArgs", "GradPushArgs", "PeerHandle")}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "tidegs_b200.h"',
+             'int main(void) {']
+    expect = []
+    for name, cls in structs.items():
+        c_name = "Tgs" + name
+        lines.append(f'  printf("%zu\\n", sizeof({c_name}));')
+        expect.append(ctypes.sizeof(cls))
+        for field, _ in cls._fields_:
+            lines.append(f'  printf("%zu\\n", offsetof({c_name}, {field}));')
+            expect.append(getattr(cls, field).offset)
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "offsets.c"
+    src.write_text("\n".join(lines))
+    include = Path(__file__).resolve().parents[1] / "include"
+    exe = tmp_path / "offsets"
+    subprocess.run(["gcc", "-std=c11", f"-I{include}", str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True,
+                                          text=True).stdout.split()]
+    assert got == expect
+
+
 def test_no_cpu_fallback_without_cuda():
     import torch
 

@@ -5,7 +5,13 @@ Adam update after pack -> all-to-all -> ordered sum equal the single-GPU
 result on the same per-rank gradients summed in rank order, bit for bit.
 Ranks are emulated inside one process here (the all-to-all's delivery order
 is reproduced by concatenation); test_two_gpu_nccl_exchange runs the real
-NCCL exchange when the box has two GPUs."""
+NCCL exchange when the box has two GPUs. The direct push (tgs_grad_push,
+PeerGradExchange) must put every tile exactly where the all-to-all puts it:
+emulated here with every "peer" buffer on one GPU, and over CUDA IPC between
+two GPUs in test_two_gpu_peer_push. The pull path (PeerGradPull +
+GPUResidentAdam.step_pulled: the owner's update kernel sums the senders'
+gradients itself) must equal exchange + sum + plain update bit for bit:
+emulated ranks here, two GPUs in test_two_gpu_pull_sum_adam."""
 import os
 import socket
 
@@ -15,7 +21,9 @@ import torch
 import torch.multiprocessing as mp
 
 from oracle import blocks as ob
-from tidegs_b200.sharded import BlockGradExchange, make_plan
+from tidegs_b200 import _lib, _ops
+from tidegs_b200.sharded import (BlockGradExchange, PeerGradExchange, PeerGradPull, make_plan,
+                                 owner_of)
 
 pytestmark = pytest.mark.gpu
 
@@ -122,6 +130,171 @@ def test_owner_adam_after_exchange_equals_single_gpu():
         assert torch.equal(a[n], b[n]), n
 
 
+def _push_emulated(plans, soas, starts, recv_bufs, err=None):
+    """Runs tgs_grad_push for every emulated rank, 'peer' buffers all local."""
+    W = len(plans)
+    for r, plan in enumerate(plans):
+        n = int(plan.send_blocks.size)
+        if n == 0:
+            continue
+        B = plan.block_size
+        tab = torch.from_numpy(np.concatenate([starts[r], np.full(n, B, np.int64),
+                                               plan.send_dst_tiles * B])).cuda()
+        ranks = torch.from_numpy(owner_of(plan.send_blocks, W).astype(np.int32)).cuda()
+        a = _lib.GradPushArgs()
+        for c, n_ in enumerate(NAMES):
+            a.comp[c] = soas[r][n_].data_ptr()
+        a.src_start, a.row_count = tab[:n].data_ptr(), tab[n:2 * n].data_ptr()
+        a.dst_row, a.dst_rank = tab[2 * n:].data_ptr(), ranks.data_ptr()
+        a.n_tiles, a.max_rows, a.n_ranks = n, B, W
+        for o in range(W):
+            a.recv[o] = recv_bufs[o].data_ptr()
+            a.recv_rows[o] = recv_bufs[o].shape[0]
+        a.err = _lib.ptr(err)
+        _lib.call("tgs_grad_push", a, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("W,B", [(4, 64), (3, 16384), (2, 100)])
+def test_push_lands_where_all_to_all_delivers(W, B):
+    rng = np.random.default_rng(11 + W)
+    nb = 80 if B != 16384 else 12
+    vis = [sorted(set(rng.integers(0, nb, nb // 2).tolist())) for _ in range(W)]
+    ex, plans, recvs = _emulate(vis, W, B)
+    soas, starts = [], []
+    for r, plan in enumerate(plans):
+        order = sorted(int(b) for b in plan.send_blocks)
+        soas.append(_compact_grads(r, order, B)[1])
+        starts.append(np.searchsorted(order, plan.send_blocks).astype(np.int64) * B)
+    cap = [max(1, sum(pl.recv_counts)) * B + 3 for pl in plans]  # slack rows stay untouched
+    bufs = [torch.full((c, 59), -7.0, device="cuda") for c in cap]
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    _push_emulated(plans, soas, starts, bufs, err)
+    assert err.cpu().tolist() == [0, 0, 0, 0]
+    for o in range(W):
+        n = recvs[o].shape[0]
+        assert torch.equal(bufs[o][:n], recvs[o]), o
+        assert bool((bufs[o][n:] == -7.0).all())
+        got = ex.reduce(plans[o], bufs[o][:n])
+        want = ob.block_grad_sum(recvs[o].cpu().numpy(), plans[o].contrib_offsets,
+                                 plans[o].contrib_blocks, B)
+        for n_ in NAMES:
+            np.testing.assert_array_equal(got[n_].cpu().numpy(), want[n_], err_msg=n_)
+
+
+def test_push_reports_tile_outside_receive_buffer():
+    W, B = 2, 64
+    vis = [[0, 1, 2, 3], [1, 2]]
+    plans = [make_plan(vis, W, r, B) for r in range(W)]
+    soas, starts = [], []
+    for r, plan in enumerate(plans):
+        order = sorted(int(b) for b in plan.send_blocks)
+        soas.append(_compact_grads(r, order, B)[1])
+        starts.append(np.searchsorted(order, plan.send_blocks).astype(np.int64) * B)
+    # owner 1 receives 3 tiles (blocks 1, 3 from rank 0, block 1 from rank 1);
+    # give it room for 2: rank 1's tile (its send tile 1, destination tile 2)
+    # must be skipped and reported, the two that fit written
+    assert plans[1].recv_counts == [2, 1]
+    bufs = [torch.zeros((sum(pl.recv_counts) * B, 59), device="cuda") for pl in plans]
+    bufs[1] = torch.zeros((2 * B, 59), device="cuda")
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    _push_emulated(plans, soas, starts, bufs, err)
+    code, idx_lo, _, aux = err.cpu().tolist()
+    assert (code, idx_lo, aux) == (5, 1, 1)  # TGS_DEV_BAD_SLICE, tile 1, owner 1
+    want = np.concatenate([_compact_grads(0, [1], B)[0], _compact_grads(0, [3], B)[0]])
+    np.testing.assert_array_equal(bufs[1].cpu().numpy(), want)
+
+
+def test_peer_exchange_single_rank_equals_all_to_all_path():
+    W, B = 1, 256
+    vis = [[3, 5, 8, 9]]
+    plan = make_plan(vis, W, 0, B)
+    order = sorted(int(b) for b in plan.send_blocks)
+    _, soa = _compact_grads(0, order, B)
+    starts = {b: i * B for i, b in enumerate(order)}
+    ex = BlockGradExchange(B)
+    want = ex.reduce(plan, ex.all_to_all(plan, ex.pack(plan, soa, starts)))
+    peer = PeerGradExchange(B, capacity_blocks=8, device="cuda")
+    try:
+        for parity in (0, 1):
+            assert peer.push(plan, soa, starts, parity) == 4 * B
+            peer.barrier()
+            got = peer.reduce(plan, parity)
+            for n in NAMES:
+                assert torch.equal(got[n], want[n]), n
+    finally:
+        peer.close()
+
+
+LR6 = [1e-3, 5e-2, 5e-3, 1e-3, 2.5e-3, 1e-4]
+
+
+def _owner(owned, B, params):
+    """A GPUResidentAdam whose working set is `owned` (slice i = block i)."""
+    import types
+
+    from tidegs_b200 import GPUResidentAdam
+
+    rows = len(owned) * B
+    ids = torch.arange(rows, device="cuda")
+
+    class M:
+        loaded_blocks = list(owned)
+        block_to_gpu_slice = {b: slice(i * B, (i + 1) * B) for i, b in enumerate(owned)}
+        local_to_global_idx = ids
+
+    g = types.SimpleNamespace(gpu_working_set_manager=M(), optimizer=types.SimpleNamespace(
+        columns_lr=torch.tensor(LR6), param_groups=[{"betas": (0.9, 0.999), "eps": 1e-15}]))
+    for n in NAMES:
+        setattr(g, "_" + n, params[n].clone())
+    opt = GPUResidentAdam(batch_size=16, block_size=B, capacity_blocks=len(owned), device="cuda")
+    opt.set_resident_blocks(list(owned))
+    return opt, g
+
+
+@pytest.mark.parametrize("W,B", [(3, 64), (2, 16384), (5, 32)])
+def test_pull_sum_adam_equals_exchange_then_adam(W, B):
+    rng = np.random.default_rng(40 + W)
+    nb = 70 if B != 16384 else 10
+    vis = [sorted(set(rng.integers(0, nb, nb // 2).tolist())) for _ in range(W)]
+    ex, plans, recvs = _emulate(vis, W, B)
+    # each rank's gradients: its rendered blocks in ascending id, B rows each
+    grads = [_compact_grads(r, sorted(int(b) for b in plans[r].send_blocks), B)[1]
+             for r in range(W)]
+    for o in range(W):
+        plan = plans[o]
+        owned = plan.out_blocks.tolist()
+        if not owned:
+            continue
+        params = {n: torch.randn((len(owned) * B, w), device="cuda") for n, w in ob.WIDTHS.items()}
+        summed = ex.reduce(plan, recvs[o])
+        opt_a, g_a = _owner(owned, B, params)
+        opt_b, g_b = _owner(owned, B, params)
+        pull = PeerGradPull.in_process(grads, o, B, "cuda")
+        ids = torch.arange(len(owned) * B, device="cuda")
+        for step in (1, 2, 3):
+            sa = opt_a.step(step, g_a, ids, summed)
+            sb = opt_b.step_pulled(step, g_b, ids, pull, plan)
+            assert sa == sb
+        for n in NAMES:
+            assert torch.equal(getattr(g_a, "_" + n), getattr(g_b, "_" + n)), (o, n)
+        assert torch.equal(opt_a._state, opt_b._state)
+
+
+def test_pull_rejects_rows_that_do_not_match_the_plan():
+    W, B = 2, 32
+    vis = [[0, 1], [1]]
+    plans = [make_plan(vis, W, r, B) for r in range(W)]
+    grads = [_compact_grads(r, sorted(int(b) for b in plans[r].send_blocks), B)[1]
+             for r in range(W)]
+    owned = plans[1].out_blocks.tolist()
+    params = {n: torch.randn((len(owned) * B, w), device="cuda") for n, w in ob.WIDTHS.items()}
+    opt, g = _owner(owned, B, params)
+    pull = PeerGradPull.in_process(grads, 1, B, "cuda")
+    with pytest.raises(ValueError):
+        opt.step_pulled(1, g, torch.arange(B - 1, device="cuda"), pull, plans[1])
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
@@ -175,6 +348,146 @@ def test_two_gpu_nccl_exchange():
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, vis, B, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert results == {0: True, 1: True}
+
+
+def _peer_worker(rank, world, port, vis_steps, B, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    peer = None
+    try:
+        cap = max(sum(make_plan(v, world, rank, B).recv_counts) for v in vis_steps)
+        peer = PeerGradExchange(B, capacity_blocks=cap, device=torch.device("cuda", rank))
+        ok = True
+        for step, vis in enumerate(vis_steps):
+            plan = make_plan(vis, world, rank, B)
+            order = sorted(int(b) for b in plan.send_blocks)
+            _, soa = _compact_grads(rank + 10 * step, order, B)
+            peer.push(plan, soa, {b: i * B for i, b in enumerate(order)}, parity=step)
+            peer.barrier()
+            got = peer.reduce(plan, parity=step)
+            expect = []
+            for s in range(world):
+                for b in (b for b in np.unique(vis[s]) if b % world == rank):
+                    expect.append(_compact_grads(s + 10 * step, [int(b)], B)[0])
+            recv = np.concatenate(expect) if expect else np.zeros((0, 59), np.float32)
+            want = ob.block_grad_sum(recv, plan.contrib_offsets, plan.contrib_blocks, B)
+            ok = ok and all(np.array_equal(got[n].cpu().numpy(), want[n]) for n in NAMES)
+        torch.cuda.synchronize()
+        q.put((rank, bool(ok)))
+    finally:
+        if peer is not None:
+            peer.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_peer_push():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, B = 2, 256
+    rng = np.random.default_rng(6)
+    vis_steps = [[sorted(set(rng.integers(0, 64, 30).tolist())) for _ in range(world)]
+                 for _ in range(3)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, vis_steps, B, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert results == {0: True, 1: True}
+
+
+def _pull_worker(rank, world, port, vis_steps, B, nb, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    pull = None
+    try:
+        cap = max(len(set(v[rank])) for v in vis_steps)
+        grads = {n: torch.zeros((cap * B, w), device="cuda") for n, w in ob.WIDTHS.items()}
+        pull = PeerGradPull(grads, B, torch.device("cuda", rank))
+        owned = [b for b in range(nb) if b % world == rank]  # every block this rank owns
+        table = np.full(nb, -1, np.int64)
+        table[owned] = np.arange(len(owned))
+        gen = torch.Generator(device="cuda").manual_seed(77 + rank)
+        params = {n: torch.randn((len(owned) * B, w), device="cuda", generator=gen)
+                  for n, w in ob.WIDTHS.items()}
+        opt_a, g_a = _owner(owned, B, params)   # fused pull
+        opt_b, g_b = _owner(owned, B, params)   # rank-order sum computed here, plain update
+        ok = True
+        for step, vis in enumerate(vis_steps, start=1):
+            plan = make_plan(vis, world, rank, B, out_order=table)
+            mine = sorted(int(b) for b in plan.send_blocks)
+            _, soa = _compact_grads(rank + 10 * step, mine, B)
+            for n in NAMES:
+                grads[n][:len(mine) * B].copy_(soa[n])
+            ids = torch.from_numpy((table[plan.out_blocks][:, None] * B
+                                    + np.arange(B)[None, :]).reshape(-1)).cuda()
+            sa = opt_a.step_pulled(step, g_a, ids, pull, plan)
+            summed = {n: torch.empty((plan.n_out * B, w), device="cuda")
+                      for n, w in ob.WIDTHS.items()}
+            for k, b in enumerate(plan.out_blocks.tolist()):
+                acc = None
+                for r in range(world):
+                    if b in vis[r]:
+                        t = _compact_grads(r + 10 * step, [b], B)[0]
+                        acc = t.copy() if acc is None else (acc + t).astype(np.float32)
+                for n, w in ob.WIDTHS.items():
+                    summed[n][k * B:(k + 1) * B] = torch.from_numpy(
+                        acc[:, ob.UNIFIED[n]:ob.UNIFIED[n] + w].copy())
+            sb = opt_b.step(step, g_b, ids, summed)
+            ok = ok and sa == sb
+        for n in NAMES:
+            ok = ok and torch.equal(getattr(g_a, "_" + n), getattr(g_b, "_" + n))
+        ok = ok and torch.equal(opt_a._state, opt_b._state)
+        torch.cuda.synchronize()
+        q.put((rank, bool(ok)))
+    finally:
+        if pull is not None:
+            pull.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_pull_sum_adam():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, B, nb = 2, 256, 40
+    rng = np.random.default_rng(8)
+    vis_steps = [[sorted(set(rng.integers(0, nb, 18).tolist())) for _ in range(world)]
+                 for _ in range(3)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pull_worker, args=(r, world, port, vis_steps, B, nb, q))
              for r in range(world)]
     for p in procs:
         p.start()

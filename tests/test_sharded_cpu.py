@@ -43,6 +43,39 @@ def test_plan_output_order_follows_owner_rows():
         make_plan(vis, 2, 0, block_size=1, out_order={0: 1})
 
 
+@pytest.mark.parametrize("W", [2, 3, 5, 8])
+def test_push_destinations_match_all_to_all_delivery(W):
+    """send_dst_tiles puts every tile where all_to_all_single delivers it
+    (sender-major, ascending block ids inside a sender)."""
+    rng = np.random.default_rng(W)
+    vis = [np.unique(rng.choice(300, 70, replace=False)) for _ in range(W)]
+    vis[W - 1] = np.zeros(0, np.int64)  # a rank that rendered nothing
+    plans = [make_plan(vis, W, r, block_size=1) for r in range(W)]
+    for o in range(W):
+        delivered = []
+        for pl in plans:
+            off = np.concatenate([[0], np.cumsum(pl.send_counts)])
+            delivered += pl.send_blocks[off[o]:off[o + 1]].tolist()
+        assert delivered == plans[o].recv_blocks.tolist()
+        pushed = np.full(len(delivered), -1)
+        for pl in plans:
+            mine = owner_of(pl.send_blocks, W) == o
+            assert np.all(pushed[pl.send_dst_tiles[mine]] == -1)  # no tile written twice
+            pushed[pl.send_dst_tiles[mine]] = pl.send_blocks[mine]
+        assert pushed.tolist() == delivered
+
+
+def test_plan_accepts_dense_order_table():
+    vis = [[2, 6, 4], [4, 0]]
+    table = np.full(10, -1, np.int64)
+    table[[0, 2, 4, 6]] = [30, 10, 20, 0]
+    plan = make_plan(vis, 2, 0, block_size=1, out_order=table)
+    assert plan.out_blocks.tolist() == [6, 2, 4, 0]
+    table[0] = -1
+    with pytest.raises(KeyError):
+        make_plan(vis, 2, 0, block_size=1, out_order=table)
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))

@@ -20,6 +20,8 @@ NUM_COMPONENTS = 6
 ROW_WIDTH = 59
 STATE_ROW_FLOATS = 128
 MAX_GROUPS = 16
+MAX_PEERS = 64
+PEER_HANDLE_BYTES = 64
 
 LAYOUT_CACHE = 0
 LAYOUT_UNIFIED = 1
@@ -106,6 +108,27 @@ class BlockSumArgs(C.Structure):
     ]
 
 
+class PeerHandle(C.Structure):
+    _fields_ = [("bytes", C.c_ubyte * PEER_HANDLE_BYTES)]
+
+
+class GradPushArgs(C.Structure):
+    _fields_ = [
+        ("comp", _vp * NUM_COMPONENTS), ("src_start", _vp), ("row_count", _vp),
+        ("dst_rank", _vp), ("dst_row", _vp), ("n_tiles", _i32), ("max_rows", _i64),
+        ("recv", _vp * MAX_PEERS), ("recv_rows", _i64 * MAX_PEERS), ("n_ranks", _i32),
+        ("err", _vp),
+    ]
+
+
+class ResidentAdamSumArgs(C.Structure):
+    _fields_ = [
+        ("adam", ResidentAdamArgs), ("grad_src", _vp), ("grad_rows", _vp), ("n_ranks", _i32),
+        ("seg_begin", _vp), ("n_segments", _i32), ("contrib_offsets", _vp),
+        ("contrib_rank", _vp), ("contrib_row", _vp), ("err", _vp),
+    ]
+
+
 # name -> (restype, argtypes). Keep in sync with include/tidegs_b200.h.
 SIGNATURES = {
     "tgs_version": (C.c_int, []),
@@ -130,6 +153,13 @@ SIGNATURES = {
     "tgs_block_bounds": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _vp]),
     "tgs_block_grad_sum": (C.c_int, [C.POINTER(BlockSumArgs), _vp]),
     "tgs_copy_small": (C.c_int, [_vp, _vp, _i64, _vp]),
+    "tgs_grad_push": (C.c_int, [C.POINTER(GradPushArgs), _vp]),
+    "tgs_peer_buffer_alloc": (C.c_int, [_i64, C.POINTER(_vp), C.POINTER(PeerHandle)]),
+    "tgs_peer_buffer_free": (C.c_int, [_vp]),
+    "tgs_peer_buffer_open": (C.c_int, [C.POINTER(PeerHandle), C.POINTER(_vp)]),
+    "tgs_peer_buffer_close": (C.c_int, [_vp]),
+    "tgs_peer_export": (C.c_int, [_vp, C.POINTER(PeerHandle), C.POINTER(_i64)]),
+    "tgs_resident_adam_apply_sum": (C.c_int, [C.POINTER(ResidentAdamSumArgs), _vp]),
 }
 
 _lock = threading.Lock()
@@ -176,7 +206,8 @@ KERNELS_PER_CALL = {
     "tgs_build_block_starts": 1, "tgs_global_to_local": 1, "tgs_global_to_local_compact": 3,
     "tgs_global_to_local_compact_noalloc": 3,
     "tgs_dirty_mark": 1, "tgs_dirty_select": 1, "tgs_dirty_list": 1, "tgs_pack_rows": 1,
-    "tgs_block_bounds": 1, "tgs_block_grad_sum": 1, "tgs_copy_small": 1,
+    "tgs_block_bounds": 1, "tgs_block_grad_sum": 1, "tgs_copy_small": 1, "tgs_grad_push": 1,
+    "tgs_resident_adam_apply_sum": 1,
 }
 launch_counter = {"kernels": 0}
 

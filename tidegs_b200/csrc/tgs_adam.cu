@@ -264,6 +264,176 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
 }
 
 // ---------------------------------------------------------------------------
+// Kernel C': the same update with the owner-side gradient reduction fused in
+// ("pull"). A row's gradient is the sum, in listed (rank) order, of its
+// contributions read straight from the senders' gradient components (peer
+// memory through IPC mappings for other ranks): plain loads, issued together
+// with the row's state and parameter loads, so the NVLink reads overlap the
+// HBM traffic of the update. The first two contributions of the U rows in
+// flight load in one round; further ones (rare) follow one by one.
+// ---------------------------------------------------------------------------
+struct ResidentSumParams {
+  ResidentApplyParams a;            // a.grad unused
+  const float* const* grad_src;     // [n_ranks * kNumComp]
+  const int64_t* grad_rows;         // [n_ranks]
+  int n_ranks;
+  const int64_t* seg_begin;         // [n_seg + 1]
+  int n_seg;
+  const int64_t* contrib_offsets;   // [n_seg + 1]
+  const int32_t* contrib_rank;
+  const int64_t* contrib_row;
+  int32_t* err;
+};
+
+struct __align__(16) RowSeg {
+  int64_t off;  // row offset inside its segment
+  int32_t cb;   // first contribution
+  int32_t cn;   // contributions
+};
+
+struct LaneCols {
+  int comp[2];
+  int col[2];
+  int width[2];
+};
+
+__device__ __forceinline__ void load_contrib(const ResidentSumParams& q, const LaneCols& lc, int j,
+                                             int64_t off, float& x0, float& x1) {
+  const int r = __ldg(q.contrib_rank + j);
+  const int64_t srow = __ldg(q.contrib_row + j) + off;
+  if (r < 0 || r >= q.n_ranks || srow < 0 || srow >= __ldg(q.grad_rows + r)) {
+    report_error(q.err, TGS_DEV_BAD_SLICE, j, r);
+    x0 = x1 = 0.f;
+    return;
+  }
+  const float* b0 = q.grad_src[r * kNumComp + lc.comp[0]];
+  const float* b1 = q.grad_src[r * kNumComp + lc.comp[1]];
+  x0 = b0[srow * lc.width[0] + lc.col[0]];
+  x1 = b1[srow * lc.width[1] + lc.col[1]];
+}
+
+template <bool kPow2Batch>
+__global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks)
+    resident_adam_sum_kernel(const ResidentSumParams q) {
+  __shared__ RowAddr s_addr[kApplyWarps][32];
+  __shared__ RowScale s_scale[kApplyWarps][32];
+  __shared__ RowSeg s_seg[kApplyWarps][32];
+  const ResidentApplyParams& a = q.a;
+  if (load_error(a.err) != 0) return;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const unsigned full = 0xffffffffu;
+  const AdamScalars hp = {a.beta1, a.beta2, a.omb1, a.omb2, a.eps, a.batch_size, a.inv_batch_size};
+
+  LaneCols lc;
+  float* pbase[2];
+  int width[2];
+  float lr[2];
+  bool act[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int j = 2 * lane + e;
+    act[e] = j < kRowWidth;
+    const int c = act[e] ? unified_comp_of(j) : 0;
+    const int k = act[e] ? j - unified_offset(c) : 0;
+    lc.comp[e] = c;
+    lc.col[e] = k;
+    lc.width[e] = comp_width(c);
+    pbase[e] = pick6(a.param, c) + k;
+    width[e] = comp_width(c);
+    lr[e] = pick6(a.lr, c);
+  }
+  const bool keep_lo = lane < 30;
+  const bool keep_hi = lane < 29;
+  const bool stamp_lane = lane == 31;
+
+  const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * kApplyWarps + warp;
+  const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kApplyWarps;
+
+  for (int64_t chunk = warp_id; chunk * 32 < a.n; chunk += warp_stride) {
+    const int64_t row0 = chunk * 32;
+    const int nr = static_cast<int>(min64(32, a.n - row0));
+
+    if (lane < nr) {
+      const int64_t row = row0 + lane;
+      const int64_t id = a.ids[row];
+      const int p = upper_bound_i64(a.pos_end, a.n_pos, id);
+      const int s = __ldg(a.pos_slot + p);
+      const float2 bb = a.slot_bias[s];
+      s_addr[warp][lane] = {id, static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p))};
+      s_scale[warp][lane] = {bb.x, bb.y, __ldg(a.slot_stamp + s), 0u};
+      // segment of the row: first s with seg_begin[s + 1] > row
+      const int sg = upper_bound_i64(q.seg_begin + 1, q.n_seg, row);
+      RowSeg rs = {0, 0, 0};
+      if (sg < q.n_seg && __ldg(q.seg_begin + sg) <= row) {
+        rs.cb = static_cast<int32_t>(__ldg(q.contrib_offsets + sg));
+        rs.cn = static_cast<int32_t>(__ldg(q.contrib_offsets + sg + 1)) - rs.cb;
+        rs.off = row - __ldg(q.seg_begin + sg);
+      } else {
+        report_error(q.err, TGS_DEV_BAD_SLICE, row);
+      }
+      s_seg[warp][lane] = rs;
+    }
+    __syncwarp();
+
+    for (int r = 0; r < nr; r += kApplyUnroll) {
+      float4 st[kApplyUnroll];
+      float g0[kApplyUnroll], g1[kApplyUnroll], h0[kApplyUnroll], h1[kApplyUnroll];
+      float p0[kApplyUnroll], p1[kApplyUnroll];
+#pragma unroll
+      for (int u = 0; u < kApplyUnroll; ++u) {
+        const int rr = r + u;  // warp-uniform
+        st[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        g0[u] = g1[u] = h0[u] = h1[u] = p0[u] = p1[u] = 0.f;
+        if (rr < nr) {
+          const RowAddr ra = s_addr[warp][rr];
+          const RowSeg sg = s_seg[warp][rr];
+          st[u] = a.state[ra.sr * 32 + lane];
+          if (sg.cn > 0) load_contrib(q, lc, sg.cb, sg.off, g0[u], g1[u]);
+          if (sg.cn > 1) load_contrib(q, lc, sg.cb + 1, sg.off, h0[u], h1[u]);
+          p0[u] = pbase[0][ra.id * width[0]];
+          p1[u] = pbase[1][ra.id * width[1]];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kApplyUnroll; ++u) {
+        const int rr = r + u;
+        if (rr >= nr) break;  // warp-uniform
+        const RowAddr ra = s_addr[warp][rr];
+        const RowScale rs = s_scale[warp][rr];
+        const RowSeg sg = s_seg[warp][rr];
+        if (sg.cn > 1) {
+          g0[u] = fadd(g0[u], h0[u]);
+          g1[u] = fadd(g1[u], h1[u]);
+        }
+#pragma unroll 1
+        for (int j = 2; j < sg.cn; ++j) {
+          float x0, x1;
+          load_contrib(q, lc, sg.cb + j, sg.off, x0, x1);
+          g0[u] = fadd(g0[u], x0);
+          g1[u] = fadd(g1[u], x1);
+        }
+        const bool fresh =
+            __shfl_sync(full, __float_as_uint(st[u].x) == rs.stamp ? 1 : 0, 31) != 0;
+        float m0 = fresh ? st[u].x : 0.f, v0 = fresh ? st[u].y : 0.f;
+        float m1 = fresh ? st[u].z : 0.f, v1 = fresh ? st[u].w : 0.f;
+        adam_elem<kPow2Batch>(p0[u], m0, v0, g0[u], hp, fmul(rs.rb1, lr[0]), rs.ds);
+        adam_elem<kPow2Batch>(p1[u], m1, v1, g1[u], hp, fmul(rs.rb1, lr[1]), rs.ds);
+        float4 out;
+        out.x = stamp_lane ? __uint_as_float(rs.stamp) : (keep_lo ? m0 : 0.f);
+        out.y = keep_lo ? v0 : 0.f;
+        out.z = keep_hi ? m1 : 0.f;
+        out.w = keep_hi ? v1 : 0.f;
+        a.state[ra.sr * 32 + lane] = out;
+        if (act[0]) pbase[0][ra.id * width[0]] = p0[u];
+        if (act[1]) pbase[1][ra.id * width[1]] = p1[u];
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Dense masked optimizers (SelectiveAdam, SelectiveSophia). All groups run in
 // one launch: CTAs [cta_begin[g], cta_begin[g+1]) serve group g. A thread
 // handles 4 consecutive elements (one float4 when the group is 16-byte
@@ -487,52 +657,99 @@ extern "C" int tgs_resident_adam_count(const TgsResidentCountArgs* a, void* stre
   return TGS_OK;
 }
 
-extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* stream) {
-  TGS_CHECK_ARG(a != nullptr, "tgs_resident_adam_apply: args is NULL");
-  if (a->n_rows == 0) return TGS_OK;
-  TGS_CHECK_ARG(a->n_rows > 0 && a->n_positions >= 1 && a->block_size >= 1,
-                "tgs_resident_adam_apply: bad sizes");
+namespace {
+
+// Checks the update arguments shared by both apply entry points and fills the
+// kernel parameters; *pow2 tells whether the batch divide is a multiply.
+int fill_apply_params(const TgsResidentAdamArgs* a, bool need_grad, const char* who,
+                      ResidentApplyParams* p, bool* pow2) {
+  TGS_CHECK_ARG(a->n_rows > 0 && a->n_positions >= 1 && a->block_size >= 1, "%s: bad sizes", who);
   TGS_CHECK_ARG(a->local_ids && a->pos_start && a->pos_end && a->pos_slot && a->state &&
                     a->slot_stamp && a->slot_bias && a->err,
-                "tgs_resident_adam_apply: NULL pointer");
-  TGS_CHECK_ARG(aligned16(a->state), "tgs_resident_adam_apply: state must be 16-byte aligned");
-  TGS_CHECK_ARG(a->batch_size != 0.0f, "tgs_resident_adam_apply: batch_size is 0");
-  ResidentApplyParams p;
+                "%s: NULL pointer", who);
+  TGS_CHECK_ARG(aligned16(a->state), "%s: state must be 16-byte aligned", who);
+  TGS_CHECK_ARG(a->batch_size != 0.0f, "%s: batch_size is 0", who);
   for (int c = 0; c < kNumComp; ++c) {
-    TGS_CHECK_ARG(a->param[c] && a->grad[c], "tgs_resident_adam_apply: component %d is NULL", c);
-    p.param[c] = a->param[c];
-    p.grad[c] = a->grad[c];
-    p.lr[c] = a->lr[c];
+    TGS_CHECK_ARG(a->param[c] && (a->grad[c] || !need_grad), "%s: component %d is NULL", who, c);
+    p->param[c] = a->param[c];
+    p->grad[c] = a->grad[c];
+    p->lr[c] = a->lr[c];
   }
-  p.beta1 = a->beta1;
-  p.beta2 = a->beta2;
-  p.omb1 = a->one_minus_beta1;
-  p.omb2 = a->one_minus_beta2;
-  p.eps = a->eps;
-  p.batch_size = a->batch_size;
+  p->beta1 = a->beta1;
+  p->beta2 = a->beta2;
+  p->omb1 = a->one_minus_beta1;
+  p->omb2 = a->one_minus_beta2;
+  p->eps = a->eps;
+  p->batch_size = a->batch_size;
   // A power-of-two batch size with a normal reciprocal divides exactly by a
   // multiply (same exactly rounded result as the division).
   int exp2 = 0;
   const float mant = frexpf(a->batch_size, &exp2);
-  const bool pow2 = mant == 0.5f && exp2 > -125 && exp2 < 126;
-  p.inv_batch_size = pow2 ? 1.0f / a->batch_size : 0.0f;
-  p.pos_start = a->pos_start;
-  p.pos_end = a->pos_end;
-  p.pos_slot = a->pos_slot;
-  p.n_pos = a->n_positions;
-  p.block_size = a->block_size;
-  p.ids = a->local_ids;
-  p.n = a->n_rows;
-  p.state = reinterpret_cast<float4*>(a->state);
-  p.slot_stamp = a->slot_stamp;
-  p.slot_bias = reinterpret_cast<const float2*>(a->slot_bias);
-  p.err = a->err;
-  const int64_t warps_needed = ceil_div<int64_t>(a->n_rows, 32);
+  *pow2 = mant == 0.5f && exp2 > -125 && exp2 < 126;
+  p->inv_batch_size = *pow2 ? 1.0f / a->batch_size : 0.0f;
+  p->pos_start = a->pos_start;
+  p->pos_end = a->pos_end;
+  p->pos_slot = a->pos_slot;
+  p->n_pos = a->n_positions;
+  p->block_size = a->block_size;
+  p->ids = a->local_ids;
+  p->n = a->n_rows;
+  p->state = reinterpret_cast<float4*>(a->state);
+  p->slot_stamp = a->slot_stamp;
+  p->slot_bias = reinterpret_cast<const float2*>(a->slot_bias);
+  p->err = a->err;
+  return TGS_OK;
+}
+
+int apply_grid(int64_t n_rows) {
+  const int64_t warps_needed = ceil_div<int64_t>(n_rows, 32);
   const int64_t ctas_needed = ceil_div<int64_t>(warps_needed, kApplyThreads / 32);
   const int64_t cap = static_cast<int64_t>(sm_count()) * kApplyMinBlocks;
-  const int grid = static_cast<int>(std::min<int64_t>(ctas_needed, cap));
+  return static_cast<int>(std::min<int64_t>(ctas_needed, cap));
+}
+
+}  // namespace
+
+extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* stream) {
+  TGS_CHECK_ARG(a != nullptr, "tgs_resident_adam_apply: args is NULL");
+  if (a->n_rows == 0) return TGS_OK;
+  ResidentApplyParams p;
+  bool pow2 = false;
+  const int rc = fill_apply_params(a, true, "tgs_resident_adam_apply", &p, &pow2);
+  if (rc != TGS_OK) return rc;
+  const int grid = apply_grid(a->n_rows);
   if (pow2) resident_adam_kernel<true><<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
   else resident_adam_kernel<false><<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void* stream) {
+  TGS_CHECK_ARG(a != nullptr, "tgs_resident_adam_apply_sum: args is NULL");
+  if (a->adam.n_rows == 0) return TGS_OK;
+  ResidentSumParams q;
+  bool pow2 = false;
+  const int rc = fill_apply_params(&a->adam, false, "tgs_resident_adam_apply_sum", &q.a, &pow2);
+  if (rc != TGS_OK) return rc;
+  TGS_CHECK_ARG(a->n_ranks >= 1 && a->n_segments >= 1,
+                "tgs_resident_adam_apply_sum: n_ranks=%d n_segments=%d", a->n_ranks,
+                a->n_segments);
+  TGS_CHECK_ARG(a->grad_src && a->grad_rows && a->seg_begin && a->contrib_offsets &&
+                    a->contrib_rank && a->contrib_row && a->err,
+                "tgs_resident_adam_apply_sum: NULL table");
+  TGS_CHECK_ARG(a->err == a->adam.err, "tgs_resident_adam_apply_sum: err must be adam.err");
+  q.grad_src = a->grad_src;
+  q.grad_rows = a->grad_rows;
+  q.n_ranks = a->n_ranks;
+  q.seg_begin = a->seg_begin;
+  q.n_seg = a->n_segments;
+  q.contrib_offsets = a->contrib_offsets;
+  q.contrib_rank = a->contrib_rank;
+  q.contrib_row = a->contrib_row;
+  q.err = a->err;
+  const int grid = apply_grid(a->adam.n_rows);
+  if (pow2) resident_adam_sum_kernel<true><<<grid, kApplyThreads, 0, as_stream(stream)>>>(q);
+  else resident_adam_sum_kernel<false><<<grid, kApplyThreads, 0, as_stream(stream)>>>(q);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

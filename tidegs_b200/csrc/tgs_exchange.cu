@@ -7,6 +7,14 @@
 // Adam step consumes, in the owner's row order. The summation order is fixed
 // (sender 0 first), so the result equals a single-GPU sum in rank order bit for
 // bit. No counterpart in the reference (it is single-GPU).
+//
+// The tiles reach the owners either through an all-to-all (after
+// tgs_pack_rows) or through tgs_grad_push below, which gathers each tile and
+// stores it straight into the owner's receive buffer over NVLink (a CUDA IPC
+// mapping of the owner's buffer), so the pack pass, the send buffer and the
+// collective's own copy disappear.
+#include <cuda.h>
+
 #include "tgs_common.cuh"
 
 namespace tgs {
@@ -67,6 +75,79 @@ __global__ void __launch_bounds__(kSumThreads) block_sum_kernel(const BlockSumPa
   }
 }
 
+// ---------------------------------------------------------------------------
+// Direct push: grid (64-row tile, sent block). The CTA gathers its tile of
+// the sender's SoA gradient components into an AoS UNIFIED tile in shared
+// memory (coalesced component reads), then stores the tile into the owner's
+// receive buffer with 16-byte stores when the destination rows allow it.
+// Remote stores are plain st.global through the peer mapping: no TMA or bulk
+// copy touches another GPU's memory.
+// ---------------------------------------------------------------------------
+constexpr int kPushThreads = 256;
+constexpr int kPushTileRows = 64;
+
+struct PushParams {
+  const float* comp[kNumComp];
+  const int64_t* src_start;
+  const int64_t* row_count;
+  const int32_t* dst_rank;
+  const int64_t* dst_row;
+  int n_tiles;
+  float* recv[TGS_MAX_PEERS];
+  int64_t recv_rows[TGS_MAX_PEERS];
+  int n_ranks;
+  int32_t* err;
+};
+
+__global__ void __launch_bounds__(kPushThreads) grad_push_kernel(const PushParams a) {
+  __shared__ __align__(16) float tile[kPushTileRows * kRowWidth];
+  __shared__ float* s_dst;
+  for (int k = blockIdx.y; k < a.n_tiles; k += gridDim.y) {
+    const int64_t rows_total = a.row_count[k];
+    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kPushTileRows;
+    if (r0 >= rows_total) continue;
+    const int rows = static_cast<int>(min64(kPushTileRows, rows_total - r0));
+    if (threadIdx.x == 0) {
+      const int d = a.dst_rank[k];
+      const int64_t row = a.dst_row[k];
+      float* dst = nullptr;
+      if (d >= 0 && d < a.n_ranks && row >= 0 && rows_total <= a.recv_rows[d] &&
+          row <= a.recv_rows[d] - rows_total && a.recv[d] != nullptr)
+        dst = a.recv[d] + (row + r0) * kRowWidth;
+      else if (blockIdx.x == 0)
+        report_error(a.err, TGS_DEV_BAD_SLICE, k, d);
+      s_dst = dst;
+    }
+    const int64_t src = a.src_start[k] + r0;
+#pragma unroll
+    for (int c = 0; c < kNumComp; ++c) {
+      const int w = comp_width(c);
+      const int col = unified_offset(c);
+      const float* __restrict__ s = a.comp[c] + src * w;
+      for (int e = threadIdx.x; e < rows * w; e += kPushThreads) {
+        const int r = e / w;
+        tile[r * kRowWidth + col + (e - r * w)] = s[e];
+      }
+    }
+    __syncthreads();
+    float* dst = s_dst;
+    if (dst != nullptr) {
+      const int n = rows * kRowWidth;
+      if (aligned16(dst) && (n & 3) == 0) {
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        const float4* t4 = reinterpret_cast<const float4*>(tile);
+        for (int e = threadIdx.x; e < (n >> 2); e += kPushThreads) d4[e] = t4[e];
+      } else {
+        for (int e = threadIdx.x; e < n; e += kPushThreads) dst[e] = tile[e];
+      }
+    }
+    __syncthreads();
+  }
+  // Order this thread's remote stores before anything the owner is told
+  // later (the barrier collective that follows on the stream).
+  __threadfence_system();
+}
+
 }  // namespace
 }  // namespace tgs
 
@@ -96,5 +177,110 @@ extern "C" int tgs_block_grad_sum(const TgsBlockSumArgs* a, void* stream) {
   dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(std::min(a->n_out, 65535)));
   block_sum_kernel<<<grid, kSumThreads, 0, as_stream(stream)>>>(p);
   TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+extern "C" int tgs_grad_push(const TgsGradPushArgs* a, void* stream) {
+  TGS_CHECK_ARG(a != nullptr, "tgs_grad_push: args is NULL");
+  TGS_CHECK_ARG(a->n_tiles >= 0 && a->max_rows >= 0, "tgs_grad_push: bad sizes");
+  TGS_CHECK_ARG(a->n_ranks >= 1 && a->n_ranks <= TGS_MAX_PEERS,
+                "tgs_grad_push: n_ranks=%d outside [1, %d]", a->n_ranks, TGS_MAX_PEERS);
+  if (a->n_tiles == 0 || a->max_rows == 0) return TGS_OK;
+  TGS_CHECK_ARG(a->src_start && a->row_count && a->dst_rank && a->dst_row,
+                "tgs_grad_push: NULL plan");
+  PushParams p;
+  for (int c = 0; c < kNumComp; ++c) {
+    TGS_CHECK_ARG(a->comp[c] != nullptr, "tgs_grad_push: component %d is NULL", c);
+    p.comp[c] = a->comp[c];
+  }
+  for (int r = 0; r < TGS_MAX_PEERS; ++r) {
+    const bool used = r < a->n_ranks;
+    TGS_CHECK_ARG(!used || (a->recv[r] != nullptr && a->recv_rows[r] >= 0),
+                  "tgs_grad_push: receive buffer of rank %d is missing", r);
+    p.recv[r] = used ? a->recv[r] : nullptr;
+    p.recv_rows[r] = used ? a->recv_rows[r] : 0;
+  }
+  p.src_start = a->src_start;
+  p.row_count = a->row_count;
+  p.dst_rank = a->dst_rank;
+  p.dst_row = a->dst_row;
+  p.n_tiles = a->n_tiles;
+  p.n_ranks = a->n_ranks;
+  p.err = a->err;
+  const int64_t tiles = ceil_div<int64_t>(a->max_rows, kPushTileRows);
+  TGS_CHECK_ARG(tiles < (1ll << 31), "tgs_grad_push: max_rows too large");
+  dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(std::min(a->n_tiles, 65535)));
+  grad_push_kernel<<<grid, kPushThreads, 0, as_stream(stream)>>>(p);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+static_assert(sizeof(cudaIpcMemHandle_t) == TGS_PEER_HANDLE_BYTES,
+              "TgsPeerHandle must hold a cudaIpcMemHandle_t");
+
+extern "C" int tgs_peer_buffer_alloc(int64_t bytes, void** dev_ptr, TgsPeerHandle* handle) {
+  TGS_CHECK_ARG(bytes > 0 && dev_ptr != nullptr && handle != nullptr,
+                "tgs_peer_buffer_alloc: bad arguments (bytes=%lld)", (long long)bytes);
+  void* p = nullptr;
+  TGS_CUDA(cudaMalloc(&p, static_cast<size_t>(bytes)));
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    set_error("cudaIpcGetMemHandle failed: %s", cudaGetErrorString(e));
+    return TGS_ERR_CUDA;
+  }
+  memcpy(handle->bytes, &h, sizeof(h));
+  *dev_ptr = p;
+  return TGS_OK;
+}
+
+extern "C" int tgs_peer_buffer_free(void* dev_ptr) {
+  if (dev_ptr == nullptr) return TGS_OK;
+  TGS_CUDA(cudaFree(dev_ptr));
+  return TGS_OK;
+}
+
+extern "C" int tgs_peer_buffer_open(const TgsPeerHandle* handle, void** dev_ptr) {
+  TGS_CHECK_ARG(handle != nullptr && dev_ptr != nullptr, "tgs_peer_buffer_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle->bytes, sizeof(h));
+  void* p = nullptr;
+  TGS_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *dev_ptr = p;
+  return TGS_OK;
+}
+
+extern "C" int tgs_peer_buffer_close(void* dev_ptr) {
+  if (dev_ptr == nullptr) return TGS_OK;
+  TGS_CUDA(cudaIpcCloseMemHandle(dev_ptr));
+  return TGS_OK;
+}
+
+extern "C" int tgs_peer_export(const void* dev_ptr, TgsPeerHandle* handle, int64_t* offset) {
+  TGS_CHECK_ARG(dev_ptr != nullptr && handle != nullptr && offset != nullptr,
+                "tgs_peer_export: NULL argument");
+  // The allocation base comes from the driver (no libcuda link: the entry
+  // point is resolved through the runtime).
+  using GetRange = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static GetRange get_range = nullptr;
+  if (get_range == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    TGS_CUDA(cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &fn, 12000,
+                                              cudaEnableDefault, &q));
+    TGS_CHECK_ARG(q == cudaDriverEntryPointSuccess && fn != nullptr,
+                  "tgs_peer_export: cuMemGetAddressRange not available");
+    get_range = reinterpret_cast<GetRange>(fn);
+  }
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  const CUresult r = get_range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr));
+  TGS_CHECK_ARG(r == CUDA_SUCCESS, "tgs_peer_export: %p is not device memory (driver error %d)",
+                dev_ptr, static_cast<int>(r));
+  cudaIpcMemHandle_t h;
+  TGS_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  memcpy(handle->bytes, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
   return TGS_OK;
 }

@@ -309,8 +309,35 @@ class GPUResidentAdam:
         sparse_grad_local_ids: torch.Tensor,
         sparse_grad_components: Dict[str, torch.Tensor],
     ) -> Dict[str, Any]:
-        empty = {"updated_blocks": 0, "updated_block_ids": [], "touched_rows": 0, "cold_rows": 0}
-        if sparse_grad_local_ids is None or sparse_grad_components is None:
+        if sparse_grad_components is None:
+            return self._empty()
+        return self._step(iteration, gaussians, sparse_grad_local_ids, sparse_grad_components,
+                          None)
+
+    def step_pulled(self, iteration: int, gaussians, sparse_grad_local_ids: torch.Tensor,
+                    pull, plan) -> Dict[str, Any]:
+        """Multi-GPU step of a block owner (no counterpart in the single-GPU
+        reference): the gradient of each row is summed, in rank order, from
+        the gradient buffers of the ranks that rendered its block, inside the
+        update kernel (sharded.PeerGradPull; plan = the step's ExchangePlan,
+        sparse_grad_local_ids = the rows of plan.out_blocks, block_size rows
+        each, ascending). Same result and return value as step() given the
+        rank-order sum of the contributions."""
+        if sparse_grad_local_ids is not None and sparse_grad_local_ids.numel() != (
+                plan.n_out * self.block_size):
+            raise ValueError(
+                f"[GPUResidentAdam] {sparse_grad_local_ids.numel()} rows for "
+                f"{plan.n_out} exchanged blocks of {self.block_size}")
+        return self._step(iteration, gaussians, sparse_grad_local_ids, None, (pull, plan))
+
+    @staticmethod
+    def _empty() -> Dict[str, Any]:
+        return {"updated_blocks": 0, "updated_block_ids": [], "touched_rows": 0, "cold_rows": 0}
+
+    def _step(self, iteration, gaussians, sparse_grad_local_ids, sparse_grad_components,
+              pulled) -> Dict[str, Any]:
+        empty = self._empty()
+        if sparse_grad_local_ids is None:
             return empty
         if sparse_grad_local_ids.numel() == 0:
             return empty
@@ -336,26 +363,29 @@ class GPUResidentAdam:
         grads: List[torch.Tensor] = []
         param_rows = None
         for name, attr_name, width, _ in self.COMPONENT_SPECS:
-            if name not in sparse_grad_components:
+            if pulled is None and name not in sparse_grad_components:
                 raise KeyError(
                     f"[GPUResidentAdam] Missing sparse_grad_components[{name!r}] "
                     f"at iter={iteration}"
                 )
             param = getattr(gaussians, attr_name).data
-            grad = sparse_grad_components[name]
-            if not param.is_contiguous() or not grad.is_contiguous():
+            # a pulled step reads the senders' gradients inside the kernel
+            grad = None if pulled is not None else sparse_grad_components[name]
+            tensors = (param,) if grad is None else (param, grad)
+            if not all(t.is_contiguous() for t in tensors):
                 raise RuntimeError(
                     f"[GPUResidentAdam] {name} parameter and gradient must be contiguous"
                 )
-            if param.dtype != torch.float32 or grad.dtype != torch.float32:
+            if any(t.dtype != torch.float32 for t in tensors):
                 raise RuntimeError(f"[GPUResidentAdam] {name} must be float32")
-            if param.device != self.device or grad.device != self.device:
+            if any(t.device != self.device for t in tensors):
                 raise RuntimeError(f"[GPUResidentAdam] {name} must live on {self.device}")
             rows = param.numel() // width
-            if param.numel() != rows * width or grad.numel() != n * width:
+            if param.numel() != rows * width or (grad is not None and grad.numel() != n * width):
                 raise RuntimeError(
                     f"[GPUResidentAdam] {name} has shape {tuple(param.shape)} / gradient "
-                    f"{tuple(grad.shape)}; expected [M, {width}] / [{n}, {width}]"
+                    f"{None if grad is None else tuple(grad.shape)}; "
+                    f"expected [M, {width}] / [{n}, {width}]"
                 )
             if param_rows is None:
                 param_rows = rows
@@ -391,7 +421,7 @@ class GPUResidentAdam:
         aargs = _lib.ResidentAdamArgs()
         for c, (p, g) in enumerate(zip(params, grads)):
             aargs.param[c] = p.data_ptr()
-            aargs.grad[c] = g.data_ptr()
+            aargs.grad[c] = None if g is None else g.data_ptr()
         for c, (name, _, _, _) in enumerate(self.COMPONENT_SPECS):
             aargs.lr[c] = component_lrs[name]
         aargs.beta1, aargs.beta2, aargs.eps = beta1, beta2, eps
@@ -405,7 +435,11 @@ class GPUResidentAdam:
         aargs.slot_stamp = self._slot_stamp_dev.data_ptr()
         aargs.slot_bias = self._slot_bias_dev.data_ptr()
         aargs.err = self._err.data_ptr()
-        _lib.call("tgs_resident_adam_apply", aargs, stream)
+        if pulled is None:
+            _lib.call("tgs_resident_adam_apply", aargs, stream)
+        else:
+            pull, plan = pulled
+            pull.apply(aargs, plan, stream)
         counts_ready.synchronize()
         host = pin.numpy()
         problem = _lib.decode_device_error(host[P:P + 4])

@@ -257,14 +257,32 @@ def exchange_capacity(sched: "Schedule", scheds, world: int):
     return send_max, recv_max
 
 
+class ScheduleTrace:
+    """Every owner's synthetic schedule simulated ahead of the timed region
+    (workload generation, not the measured path): for step k, the blocks
+    each rank renders (vis[k], world > 1) and this rank's slot turnover
+    (turn[k] = evicted slot positions, incoming block ids, dirty pattern)."""
+
+    def __init__(self, world: int, rank: int, n_steps: int):
+        scheds = [Schedule(o, world) for o in range(world)]
+        self.vis, self.turn = [], []
+        for k in range(n_steps):
+            self.vis.append(rendered_blocks(scheds, k, world) if world > 1 else None)
+            turns = [o.turnover(k) for o in scheds]
+            self.turn.append(turns[rank])
+            for o, (ev, inc, _) in zip(scheds, turns):
+                o.slot_block[ev] = inc
+
+
 class DeviceStep:
-    def __init__(self, device, sched: Schedule, scheds=None, world: int = 1,
+    def __init__(self, device, sched: Schedule, trace: ScheduleTrace, scheds=None, world: int = 1,
                  exchange: str = "pull"):
         from tidegs_b200 import _lib, _ops
 
         self._lib, self._ops = _lib, _ops
         self.device = device
         self.sched = sched
+        self.trace = trace
         self.world = world
         self.scheds = scheds if scheds is not None else [sched]
         gen = torch.Generator(device=device).manual_seed(1234 + sched.rank)
@@ -344,7 +362,7 @@ class DeviceStep:
         from tidegs_b200.sharded import make_plan
 
         W, me = self.world, self.sched.rank
-        vis = rendered_blocks(self.scheds, k, W)
+        vis = self.trace.vis[k]
         slot_of = self.sched.slot_table()
         plan = make_plan(vis, W, me, B, out_order=slot_of)
         # the rank's rendered gradients: its blocks in ascending id, B rows each
@@ -386,7 +404,9 @@ class DeviceStep:
             slot_bias=self.slot_bias.data_ptr(), step_table=self.table.data_ptr(),
             step_table_len=self.table.shape[0], n_slots=SLOTS,
             pos_count=self.pos_count.data_ptr(), err=self.err.data_ptr())
+        tables = self.pull.tables(self.plan) if self.pull is not None else None
         _lib.call("tgs_resident_adam_count", c, stream)
+        self._phase("count")
         a = _lib.ResidentAdamArgs()
         for i, name in enumerate(NAMES):
             a.param[i] = self.arena[name].data_ptr()
@@ -403,35 +423,40 @@ class DeviceStep:
         a.slot_bias, a.err = self.slot_bias.data_ptr(), self.err.data_ptr()
         if self.pull is not None:
             self.pull.barrier()  # every rank's gradients of this step are written
+            self._phase("acquire")
         if timed:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
         if self.pull is not None:
-            self.pull.launch(a, self.plan, stream)
+            self.pull.launch(a, self.plan, stream, tables=tables)
         else:
             _lib.call("tgs_resident_adam_apply", a, stream)
         if timed:
             e1.record()
             self.adam_ms.append((e0, e1, n))
+        self._phase("adam")
         if self.pull is not None:
             self.pull.barrier()  # no owner still reads this step's gradients
+            self._phase("release")
 
     phase_ms = None  # {phase: [ms, ...]} when per-phase timing is on
+    host_ms = None   # host time between the same marks
 
     def _phase(self, name):
         if self.phase_ms is None:
             return
         ev = torch.cuda.Event(enable_timing=True)
         ev.record()
-        self._events.append((name, ev))
+        self._events.append((name, ev, time.perf_counter()))
 
     def collect_phases(self):
         if self.phase_ms is None:
             return
         torch.cuda.synchronize()
-        for (_, e0), (name, e1) in zip(self._events, self._events[1:]):
+        for (_, e0, h0), (name, e1, h1) in zip(self._events, self._events[1:]):
             self.phase_ms.setdefault(name, []).append(e0.elapsed_time(e1))
+            self.host_ms.setdefault(name, []).append((h1 - h0) * 1e3)
         self._events = []
 
     def step(self, k: int, timed: bool = False) -> int:
@@ -447,7 +472,6 @@ class DeviceStep:
             pos, ids = self.vis_sets[k % sched.n_sets]
         # 1. optimizer over the visible rows
         self.adam(ids, timed)
-        self._phase("adam")
         # 2. updated blocks are dirty; refresh their bounds
         updated = sched.slot_block[pos]
         _ops.dirty_mark(self.bitmap, updated.tolist(), True)
@@ -455,7 +479,7 @@ class DeviceStep:
                           self.bounds[: pos.size])
         self._phase("dirty_bounds")
         # 3. evict 512 slots: write back the dirty ones
-        evict_pos, incoming, dirty = sched.turnover(k)
+        evict_pos, incoming, dirty = self.trace.turn[k]
         # half of the evicted blocks were never touched before: mark a random
         # dirty pattern so that the compaction has work of the configured mix
         evicted_blocks = sched.slot_block[evict_pos]
@@ -479,10 +503,6 @@ class DeviceStep:
                          [B] * TURNOVER, self.device)
         self._phase("slot_copy")
         sched.slot_block[evict_pos] = incoming
-        for other in self.scheds:  # replicas of the other owners' schedules
-            if other is not sched:
-                ev, inc, _ = other.turnover(k)
-                other.slot_block[ev] = inc
         self.stamp_host[evict_pos] += 1
         _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
         self.slot_step[torch.from_numpy(evict_pos).to(self.device)] = 0
@@ -525,8 +545,8 @@ class ApiStep:
             return now
         return t
 
-    def __init__(self, device, scheds, rank: int, world: int, pool_blocks: int,
-                 exchange: str = "pull"):
+    def __init__(self, device, scheds, trace: ScheduleTrace, rank: int, world: int,
+                 pool_blocks: int, exchange: str = "pull"):
         import types
 
         from tidegs_b200 import (BlockLayout, DoubleBufferGPUWorkingSet, GPUResidentAdam,
@@ -534,6 +554,7 @@ class ApiStep:
 
         self.device = device
         self.scheds = scheds
+        self.trace = trace
         self.sched = sched = scheds[rank]
         self.rank, self.world = rank, world
         num_total = int(max(int(o.pool_ids.max()) for o in scheds) + 1) * B
@@ -625,7 +646,7 @@ class ApiStep:
         from tidegs_b200.sharded import make_plan
 
         W, me = self.world, self.rank
-        vis = rendered_blocks(self.scheds, k, W)
+        vis = self.trace.vis[k]
         # slice position i of the active buffer holds sched.slot_block[i]
         slot_of = self.sched.slot_table()
         plan = make_plan(vis, W, me, B, out_order=slot_of)
@@ -675,7 +696,7 @@ class ApiStep:
         the write-back of iteration k run."""
         db, ws, sched = self.db, self.ws, self.sched
         t = time.perf_counter()
-        evict_pos, incoming_arr, _ = sched.turnover(k)
+        evict_pos, incoming_arr, _ = self.trace.turn[k]
         loaded = [int(b) for b in sched.slot_block]
         evicted = sorted(int(b) for b in sched.slot_block[evict_pos])
         incoming = [int(b) for b in incoming_arr]
@@ -715,9 +736,7 @@ class ApiStep:
         t = self._mark("wait_prefetch", t)
         db.swap_buffers()
         t = self._mark("swap", t)
-        for o in self.scheds:
-            ev, inc, _ = o.turnover(k)
-            o.slot_block[ev] = inc
+        sched.slot_block[evict_pos] = incoming_arr
         self._activate()
         self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
         self._mark("activate", t)
@@ -832,9 +851,11 @@ def main(argv=None):
     from tidegs_b200 import _lib
 
     device = torch.device("cuda", torch.cuda.current_device())
+    n_trace = max(args.warmup + args.steps + 3, args.e2e_warmup + args.e2e_steps + 1)
+    trace = ScheduleTrace(world, rank, n_trace)
     scheds = [Schedule(o, world) for o in range(world)]
     sched = scheds[rank]
-    dev = DeviceStep(device, sched, scheds=scheds, world=world, exchange=args.exchange)
+    dev = DeviceStep(device, sched, trace, scheds=scheds, world=world, exchange=args.exchange)
     for k in range(args.warmup):
         dev.step(k)
     torch.cuda.synchronize()
@@ -852,14 +873,16 @@ def main(argv=None):
     torch.cuda.synchronize()
     if args.phase_times:
         # separate, untimed pass: per-phase CUDA events around each stage
-        dev.phase_ms = {}
+        dev.phase_ms, dev.host_ms = {}, {}
         for k in range(args.warmup + args.steps, args.warmup + args.steps + 3):
             dev.step(k)
             dev.collect_phases()
         print(f"rank {rank} device phase ms/step: " + json.dumps(
-            {n: round(sum(v) / len(v), 3) for n, v in dev.phase_ms.items()}),
+            {n: round(sum(v) / len(v), 3) for n, v in dev.phase_ms.items()})
+            + " host ms/step: " + json.dumps(
+            {n: round(sum(v) / len(v), 3) for n, v in dev.host_ms.items()}),
             file=sys.stderr, flush=True)
-        dev.phase_ms = None
+        dev.phase_ms = dev.host_ms = None
     barrier(world)
     clock_info = clocks.stop()
     launches = _lib.launch_counter["kernels"] - launches0
@@ -869,6 +892,7 @@ def main(argv=None):
     value = total_rows / (ms_max / 1e3)
     adam_ms, adam_rows = dev.adam_stats()
     adam_avg_ms = sum(adam_ms) / len(adam_ms)
+    adam_max_ms = allreduce_max(adam_avg_ms, world)
     adam_bytes = ADAM_BYTES_PER_ROW * (sum(adam_rows) / len(adam_rows))
     achieved = adam_bytes / (adam_avg_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
@@ -882,7 +906,7 @@ def main(argv=None):
     try:
         if args.no_e2e:
             raise _Skipped("--no-e2e")
-        api = ApiStep(device, [Schedule(o, world) for o in range(world)], rank, world,
+        api = ApiStep(device, [Schedule(o, world) for o in range(world)], trace, rank, world,
                       args.pool_blocks, exchange=args.exchange)
         for k in range(args.e2e_warmup):
             api.step(k)
@@ -945,7 +969,8 @@ def main(argv=None):
                          "frac": achieved / peak, "traffic": None,
                          "kernel": "resident_adam_kernel",
                          "algorithmic_bytes_per_row": ADAM_BYTES_PER_ROW,
-                         "avg_launch_ms": adam_avg_ms, "peak_source": peak_kind},
+                         "avg_launch_ms": adam_avg_ms, "peak_source": peak_kind,
+                         "avg_launch_ms_max_over_ranks": adam_max_ms},
             "clocks": clock_info,
             "gpu_launches": launches,
             "e2e": e2e,

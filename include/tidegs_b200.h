@@ -451,6 +451,10 @@ typedef struct {
   const int64_t* contrib_offsets;   /* [n_segments + 1] CSR into contrib_rank / contrib_row */
   const int32_t* contrib_rank;      /* [n_contrib] summation order inside a segment */
   const int64_t* contrib_row;       /* [n_contrib] source row of the segment's first row */
+  /* The kernel walks the compact rows starting at this one (wrapping around).
+   * Owners that start at different senders' rows read from every sender at
+   * once instead of all reading the same sender first; 0 = natural order. */
+  int64_t rotate_rows;
   int32_t* err;                     /* [4] the error word of adam.err, writable */
 } TgsResidentAdamSumArgs;
 

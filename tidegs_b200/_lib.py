@@ -125,7 +125,7 @@ class ResidentAdamSumArgs(C.Structure):
     _fields_ = [
         ("adam", ResidentAdamArgs), ("grad_src", _vp), ("grad_rows", _vp), ("n_ranks", _i32),
         ("seg_begin", _vp), ("n_segments", _i32), ("contrib_offsets", _vp),
-        ("contrib_rank", _vp), ("contrib_row", _vp), ("err", _vp),
+        ("contrib_rank", _vp), ("contrib_row", _vp), ("rotate_rows", _i64), ("err", _vp),
     ]
 
 

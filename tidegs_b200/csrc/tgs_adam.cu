@@ -282,6 +282,7 @@ struct ResidentSumParams {
   const int64_t* contrib_offsets;   // [n_seg + 1]
   const int32_t* contrib_rank;
   const int64_t* contrib_row;
+  int64_t rotate_chunks;            // first 32-row chunk walked
   int32_t* err;
 };
 
@@ -350,7 +351,10 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks)
   const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * kApplyWarps + warp;
   const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kApplyWarps;
 
-  for (int64_t chunk = warp_id; chunk * 32 < a.n; chunk += warp_stride) {
+  const int64_t n_chunks = (a.n + 31) / 32;
+  for (int64_t c = warp_id; c < n_chunks; c += warp_stride) {
+    int64_t chunk = c + q.rotate_chunks;
+    if (chunk >= n_chunks) chunk -= n_chunks;
     const int64_t row0 = chunk * 32;
     const int nr = static_cast<int>(min64(32, a.n - row0));
 
@@ -746,6 +750,9 @@ extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void
   q.contrib_offsets = a->contrib_offsets;
   q.contrib_rank = a->contrib_rank;
   q.contrib_row = a->contrib_row;
+  const int64_t n_chunks = ceil_div<int64_t>(a->adam.n_rows, 32);
+  TGS_CHECK_ARG(a->rotate_rows >= 0, "tgs_resident_adam_apply_sum: rotate_rows < 0");
+  q.rotate_chunks = (a->rotate_rows / 32) % n_chunks;
   q.err = a->err;
   const int grid = apply_grid(a->adam.n_rows);
   if (pow2) resident_adam_sum_kernel<true><<<grid, kApplyThreads, 0, as_stream(stream)>>>(q);

@@ -508,12 +508,13 @@ class PeerGradPull:
         self.launch(adam_args, plan, stream)
         self.barrier()
 
-    def launch(self, adam_args, plan: ExchangePlan, stream: int) -> None:
-        """The fused update alone; the caller provides both barriers."""
+    def launch(self, adam_args, plan: ExchangePlan, stream: int, tables=None) -> None:
+        """The fused update alone; the caller provides both barriers.
+        tables: the result of tables(plan), when the caller built it earlier."""
         S = plan.n_out
         if int(adam_args.n_rows) != S * plan.block_size:
             raise ValueError("PeerGradPull: rows to update do not match the plan's blocks")
-        i64, i32 = self.tables(plan)
+        i64, i32 = tables if tables is not None else self.tables(plan)
         args = _lib.ResidentAdamSumArgs()
         args.adam = adam_args
         args.grad_src = self._src_dev.data_ptr()
@@ -524,6 +525,9 @@ class PeerGradPull:
         args.contrib_offsets = i64[S + 1:2 * S + 2].data_ptr()
         args.contrib_row = i64[2 * S + 2:].data_ptr()
         args.contrib_rank = i32.data_ptr()
+        # start at this rank's share of the rows, so that at any moment the
+        # owners pull from different senders
+        args.rotate_rows = (self.rank * S // max(1, self.world)) * plan.block_size
         args.err = adam_args.err
         _lib.call("tgs_resident_adam_apply_sum", args, stream)
         cur = torch.cuda.current_stream(self.device)

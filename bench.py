@@ -359,12 +359,13 @@ class DeviceStep:
         """Owner-sharded gradient exchange of step k (world > 1): returns the
         owner's visible slot positions and local row ids; the reduced
         gradients land in self.grads."""
-        from tidegs_b200.sharded import make_plan
-
         W, me = self.world, self.sched.rank
         vis = self.trace.vis[k]
-        slot_of = self.sched.slot_table()
-        plan = make_plan(vis, W, me, B, out_order=slot_of)
+        if self._ahead is not None and self._ahead[0] == k:
+            _, plan, slot_of, self.pull_tables = self._ahead  # built during step k-1
+        else:
+            plan, slot_of, self.pull_tables = self._make_plan(k, self.sched.slot_block)
+        self._ahead = None
         # the rank's rendered gradients: its blocks in ascending id, B rows each
         starts = np.searchsorted(np.unique(vis[me]), plan.send_blocks).astype(np.int64) * B
         self._phase("plan")
@@ -392,6 +393,30 @@ class DeviceStep:
             raise RuntimeError("exchange plan and owner visibility disagree")
         return pos, set_ids
 
+    def _make_plan(self, k: int, slot_block: np.ndarray):
+        """Exchange plan of step k for the slot map `slot_block` (and, for the
+        pull exchange, its device tables)."""
+        from tidegs_b200.sharded import make_plan
+
+        table = np.full(int(self.sched.pool_ids[-1]) + 1, -1, np.int64)
+        table[slot_block] = np.arange(slot_block.size, dtype=np.int64)
+        plan = make_plan(self.trace.vis[k], self.world, self.sched.rank, B, out_order=table)
+        tables = self.pull.tables(plan) if self.pull is not None else None
+        return plan, table, tables
+
+    def plan_ahead(self, k: int):
+        """Builds step k+1's plan on the host while the GPU runs step k (the
+        slot map after step k's turnover is known from the schedule)."""
+        if self.world == 1 or k + 1 >= len(self.trace.turn):
+            return
+        ev, inc, _ = self.trace.turn[k]
+        nxt = self.sched.slot_block.copy()
+        nxt[ev] = inc
+        self._ahead = (k + 1,) + self._make_plan(k + 1, nxt)
+
+    _ahead = None
+    pull_tables = None
+
     def adam(self, ids: torch.Tensor, timed: bool):
         _lib = self._lib
         n = ids.numel()
@@ -404,7 +429,7 @@ class DeviceStep:
             slot_bias=self.slot_bias.data_ptr(), step_table=self.table.data_ptr(),
             step_table_len=self.table.shape[0], n_slots=SLOTS,
             pos_count=self.pos_count.data_ptr(), err=self.err.data_ptr())
-        tables = self.pull.tables(self.plan) if self.pull is not None else None
+        tables = self.pull_tables
         _lib.call("tgs_resident_adam_count", c, stream)
         self._phase("count")
         a = _lib.ResidentAdamArgs()
@@ -472,6 +497,7 @@ class DeviceStep:
             pos, ids = self.vis_sets[k % sched.n_sets]
         # 1. optimizer over the visible rows
         self.adam(ids, timed)
+        self.plan_ahead(k)
         # 2. updated blocks are dirty; refresh their bounds
         updated = sched.slot_block[pos]
         _ops.dirty_mark(self.bitmap, updated.tolist(), True)
@@ -505,7 +531,7 @@ class DeviceStep:
         sched.slot_block[evict_pos] = incoming
         self.stamp_host[evict_pos] += 1
         _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
-        self.slot_step[torch.from_numpy(evict_pos).to(self.device)] = 0
+        self.slot_step.index_fill_(0, _ops.i64_to_device(evict_pos, self.device), 0)
         self._phase("tables")
         return int(ids.numel())
 

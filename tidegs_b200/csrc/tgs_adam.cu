@@ -119,6 +119,20 @@ constexpr int kApplyThreads = 256;
 constexpr int kApplyWarps = kApplyThreads / 32;
 constexpr int kApplyUnroll = TGS_APPLY_UNROLL;
 constexpr int kApplyMinBlocks = TGS_APPLY_MIN_BLOCKS;
+// The pulling variant (kernel C') waits on remote reads: its own knobs.
+#ifndef TGS_SUM_MIN_BLOCKS
+#define TGS_SUM_MIN_BLOCKS 3
+#endif
+#ifndef TGS_SUM_UNROLL
+#define TGS_SUM_UNROLL 4
+#endif
+#ifndef TGS_SUM_FAST_UNROLL
+#define TGS_SUM_FAST_UNROLL 2
+#endif
+constexpr int kSumUnroll = TGS_SUM_UNROLL;
+constexpr int kSumFastUnroll = TGS_SUM_FAST_UNROLL;  // rows per batch, one-segment chunks
+constexpr int kStagedContribs = 2;  // contributions loaded with the batch (more: per row)
+constexpr int kSumMinBlocks = TGS_SUM_MIN_BLOCKS;
 
 struct AdamScalars {
   float beta1, beta2, omb1, omb2, eps, batch_size, inv_batch_size;
@@ -314,7 +328,7 @@ __device__ __forceinline__ void load_contrib(const ResidentSumParams& q, const L
 }
 
 template <bool kPow2Batch>
-__global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks)
+__global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
     resident_adam_sum_kernel(const ResidentSumParams q) {
   __shared__ RowAddr s_addr[kApplyWarps][32];
   __shared__ RowScale s_scale[kApplyWarps][32];
@@ -359,14 +373,133 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks)
     const int nr = static_cast<int>(min64(32, a.n - row0));
 
     if (lane < nr) {
-      const int64_t row = row0 + lane;
-      const int64_t id = a.ids[row];
+      const int64_t id = a.ids[row0 + lane];
       const int p = upper_bound_i64(a.pos_end, a.n_pos, id);
       const int s = __ldg(a.pos_slot + p);
       const float2 bb = a.slot_bias[s];
       s_addr[warp][lane] = {id, static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p))};
       s_scale[warp][lane] = {bb.x, bb.y, __ldg(a.slot_stamp + s), 0u};
-      // segment of the row: first s with seg_begin[s + 1] > row
+    }
+    // Segment of the chunk's first row (first s with seg_begin[s + 1] > row0),
+    // resolved by lane 0; the chunk takes the fast path when its last row is
+    // in the same segment.
+    int sg_cb = 0, sg_cn = 0, uniform = 0;
+    int64_t sg_off = 0;
+    if (lane == 0) {
+      const int sg = upper_bound_i64(q.seg_begin + 1, q.n_seg, row0);
+      if (sg < q.n_seg && __ldg(q.seg_begin + sg) <= row0) {
+        sg_cb = static_cast<int>(__ldg(q.contrib_offsets + sg));
+        sg_cn = static_cast<int>(__ldg(q.contrib_offsets + sg + 1)) - sg_cb;
+        sg_off = row0 - __ldg(q.seg_begin + sg);
+        uniform = row0 + nr <= __ldg(q.seg_begin + sg + 1) ? 1 : 0;
+      }
+    }
+    uniform = __shfl_sync(full, uniform, 0);
+    __syncwarp();
+
+    if (uniform) {
+      sg_cb = __shfl_sync(full, sg_cb, 0);
+      sg_cn = __shfl_sync(full, sg_cn, 0);
+      sg_off = __shfl_sync(full, sg_off, 0);
+      // This lane's columns of the first two contributions at the chunk's
+      // first row: a row's gradient is then one load per contribution, as
+      // in the single-GPU kernel. Out-of-range contributions read as zero.
+      const int ns = sg_cn < kStagedContribs ? sg_cn : kStagedContribs;
+      const float* gb[kStagedContribs][2] = {{nullptr, nullptr}, {nullptr, nullptr}};
+#pragma unroll
+      for (int jj = 0; jj < kStagedContribs; ++jj) {
+        if (jj < ns) {
+          const int r = __ldg(q.contrib_rank + sg_cb + jj);
+          const int64_t srow = __ldg(q.contrib_row + sg_cb + jj) + sg_off;
+          if (r >= 0 && r < q.n_ranks && srow >= 0 && srow + nr <= __ldg(q.grad_rows + r)) {
+#pragma unroll
+            for (int e = 0; e < 2; ++e)
+              gb[jj][e] = q.grad_src[r * kNumComp + lc.comp[e]] + srow * lc.width[e] + lc.col[e];
+          } else if (lane == 0) {
+            report_error(q.err, TGS_DEV_BAD_SLICE, sg_cb + jj, r);
+          }
+        }
+      }
+      auto load_grads = [&](int rr, float& x0, float& x1, float& y0, float& y1) {
+        x0 = x1 = y0 = y1 = 0.f;
+        if (rr < nr) {
+          if (gb[0][0] != nullptr) {
+            x0 = gb[0][0][rr * width[0]];
+            x1 = gb[0][1][rr * width[1]];
+          }
+          if (gb[1][0] != nullptr) {
+            y0 = gb[1][0][rr * width[0]];
+            y1 = gb[1][1][rr * width[1]];
+          }
+        }
+      };
+      // gradients of the next batch load while the current one updates
+      float n0[kSumFastUnroll], n1[kSumFastUnroll], m0n[kSumFastUnroll], m1n[kSumFastUnroll];
+#pragma unroll
+      for (int u = 0; u < kSumFastUnroll; ++u) load_grads(u, n0[u], n1[u], m0n[u], m1n[u]);
+      for (int r = 0; r < nr; r += kSumFastUnroll) {
+        float4 st[kSumFastUnroll];
+        float g0[kSumFastUnroll], g1[kSumFastUnroll], h0[kSumFastUnroll], h1[kSumFastUnroll];
+        float p0[kSumFastUnroll], p1[kSumFastUnroll];
+#pragma unroll
+        for (int u = 0; u < kSumFastUnroll; ++u) {
+          const int rr = r + u;  // warp-uniform
+          g0[u] = n0[u];
+          g1[u] = n1[u];
+          h0[u] = m0n[u];
+          h1[u] = m1n[u];
+          st[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          p0[u] = p1[u] = 0.f;
+          if (rr < nr) {
+            const RowAddr ra = s_addr[warp][rr];
+            st[u] = a.state[ra.sr * 32 + lane];
+            p0[u] = pbase[0][ra.id * width[0]];
+            p1[u] = pbase[1][ra.id * width[1]];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kSumFastUnroll; ++u)
+          load_grads(r + kSumFastUnroll + u, n0[u], n1[u], m0n[u], m1n[u]);
+#pragma unroll
+        for (int u = 0; u < kSumFastUnroll; ++u) {
+          const int rr = r + u;
+          if (rr >= nr) break;  // warp-uniform
+          const RowAddr ra = s_addr[warp][rr];
+          const RowScale rs = s_scale[warp][rr];
+          if (ns > 1) {
+            g0[u] = fadd(g0[u], h0[u]);
+            g1[u] = fadd(g1[u], h1[u]);
+          }
+#pragma unroll 1
+          for (int jj = kStagedContribs; jj < sg_cn; ++jj) {
+            float x0, x1;
+            load_contrib(q, lc, sg_cb + jj, sg_off + rr, x0, x1);
+            g0[u] = fadd(g0[u], x0);
+            g1[u] = fadd(g1[u], x1);
+          }
+          const bool fresh =
+              __shfl_sync(full, __float_as_uint(st[u].x) == rs.stamp ? 1 : 0, 31) != 0;
+          float m0 = fresh ? st[u].x : 0.f, v0 = fresh ? st[u].y : 0.f;
+          float m1 = fresh ? st[u].z : 0.f, v1 = fresh ? st[u].w : 0.f;
+          adam_elem<kPow2Batch>(p0[u], m0, v0, g0[u], hp, fmul(rs.rb1, lr[0]), rs.ds);
+          adam_elem<kPow2Batch>(p1[u], m1, v1, g1[u], hp, fmul(rs.rb1, lr[1]), rs.ds);
+          float4 out;
+          out.x = stamp_lane ? __uint_as_float(rs.stamp) : (keep_lo ? m0 : 0.f);
+          out.y = keep_lo ? v0 : 0.f;
+          out.z = keep_hi ? m1 : 0.f;
+          out.w = keep_hi ? v1 : 0.f;
+          a.state[ra.sr * 32 + lane] = out;
+          if (act[0]) pbase[0][ra.id * width[0]] = p0[u];
+          if (act[1]) pbase[1][ra.id * width[1]] = p1[u];
+        }
+      }
+      __syncwarp();
+      continue;
+    }
+
+    // Chunk straddling segments: each row resolves its own segment.
+    if (lane < nr) {
+      const int64_t row = row0 + lane;
       const int sg = upper_bound_i64(q.seg_begin + 1, q.n_seg, row);
       RowSeg rs = {0, 0, 0};
       if (sg < q.n_seg && __ldg(q.seg_begin + sg) <= row) {
@@ -380,12 +513,12 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks)
     }
     __syncwarp();
 
-    for (int r = 0; r < nr; r += kApplyUnroll) {
-      float4 st[kApplyUnroll];
-      float g0[kApplyUnroll], g1[kApplyUnroll], h0[kApplyUnroll], h1[kApplyUnroll];
-      float p0[kApplyUnroll], p1[kApplyUnroll];
+    for (int r = 0; r < nr; r += kSumUnroll) {
+      float4 st[kSumUnroll];
+      float g0[kSumUnroll], g1[kSumUnroll], h0[kSumUnroll], h1[kSumUnroll];
+      float p0[kSumUnroll], p1[kSumUnroll];
 #pragma unroll
-      for (int u = 0; u < kApplyUnroll; ++u) {
+      for (int u = 0; u < kSumUnroll; ++u) {
         const int rr = r + u;  // warp-uniform
         st[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         g0[u] = g1[u] = h0[u] = h1[u] = p0[u] = p1[u] = 0.f;
@@ -400,7 +533,7 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks)
         }
       }
 #pragma unroll
-      for (int u = 0; u < kApplyUnroll; ++u) {
+      for (int u = 0; u < kSumUnroll; ++u) {
         const int rr = r + u;
         if (rr >= nr) break;  // warp-uniform
         const RowAddr ra = s_addr[warp][rr];
@@ -411,9 +544,9 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks)
           g1[u] = fadd(g1[u], h1[u]);
         }
 #pragma unroll 1
-        for (int j = 2; j < sg.cn; ++j) {
+        for (int jj = 2; jj < sg.cn; ++jj) {
           float x0, x1;
-          load_contrib(q, lc, sg.cb + j, sg.off, x0, x1);
+          load_contrib(q, lc, sg.cb + jj, sg.off, x0, x1);
           g0[u] = fadd(g0[u], x0);
           g1[u] = fadd(g1[u], x1);
         }
@@ -705,10 +838,10 @@ int fill_apply_params(const TgsResidentAdamArgs* a, bool need_grad, const char* 
   return TGS_OK;
 }
 
-int apply_grid(int64_t n_rows) {
+int apply_grid(int64_t n_rows, int ctas_per_sm = kApplyMinBlocks) {
   const int64_t warps_needed = ceil_div<int64_t>(n_rows, 32);
   const int64_t ctas_needed = ceil_div<int64_t>(warps_needed, kApplyThreads / 32);
-  const int64_t cap = static_cast<int64_t>(sm_count()) * kApplyMinBlocks;
+  const int64_t cap = static_cast<int64_t>(sm_count()) * ctas_per_sm;
   return static_cast<int>(std::min<int64_t>(ctas_needed, cap));
 }
 
@@ -754,7 +887,7 @@ extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void
   TGS_CHECK_ARG(a->rotate_rows >= 0, "tgs_resident_adam_apply_sum: rotate_rows < 0");
   q.rotate_chunks = (a->rotate_rows / 32) % n_chunks;
   q.err = a->err;
-  const int grid = apply_grid(a->adam.n_rows);
+  const int grid = apply_grid(a->adam.n_rows, kSumMinBlocks);
   if (pow2) resident_adam_sum_kernel<true><<<grid, kApplyThreads, 0, as_stream(stream)>>>(q);
   else resident_adam_sum_kernel<false><<<grid, kApplyThreads, 0, as_stream(stream)>>>(q);
   TGS_LAUNCH_CHECK();

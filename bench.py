@@ -771,6 +771,45 @@ class ApiStep:
 
 
 # ---------------------------------------------------------------------------
+# Diagnostic: the pull kernel with a remote sender, in one process
+# ---------------------------------------------------------------------------
+def pull_probe(args, modes):
+    """Not the bench line. One owner (GPU 0) of a two-rank schedule updates
+    its visible rows with the pull kernel while the other rank's gradients
+    live on GPU 1 ("remote", read over NVLink) or on GPU 0 ("local"), next to
+    the single-GPU kernel ("plain"). One JSON line per mode (CUDA events)."""
+    from tidegs_b200.sharded import PeerGradPull, make_plan
+
+    W = 2
+    torch.cuda.set_device(0)
+    d0 = torch.device("cuda", 0)
+    scheds = [Schedule(r, W) for r in range(W)]
+    ds = DeviceStep(d0, scheds[0], None, scheds=scheds, world=1)
+    caps = [exchange_capacity(scheds[r], scheds, W)[0] for r in range(W)]
+    plan = make_plan(rendered_blocks(scheds, 0, W), W, 0, B, out_order=scheds[0].slot_table())
+    pos, ids = ds.vis_sets[0]
+    if not np.array_equal(scheds[0].slot_table()[plan.out_blocks], pos):
+        raise RuntimeError("probe plan and owner visibility disagree")
+    for mode in modes:
+        ds.pull = ds.pull_tables = None
+        if mode != "plain":
+            where = [d0, torch.device("cuda", 1) if mode == "remote" else d0]
+            grads = [{n: torch.empty((caps[r] * B, w), device=where[r]).normal_(0, 1e-3)
+                      for n, w in WIDTHS.items()} for r in range(W)]
+            ds.pull = PeerGradPull.in_process(grads, 0, B, d0)
+            ds.plan, ds.pull_tables = plan, ds.pull.tables(plan)
+        ds.adam_ms = []
+        for k in range(args.warmup + args.steps):
+            ds.adam(ids, timed=k >= args.warmup)
+        torch.cuda.synchronize()
+        ms = sorted(ms for ms, _ in zip(*ds.adam_stats()))
+        print(json.dumps({"probe": mode, "rows": int(ids.numel()), "median_ms": ms[len(ms) // 2],
+                          "contributions": int(plan.contrib_offsets[-1]), "blocks": plan.n_out,
+                          "remote_blocks": int(sum(plan.recv_counts[1:]))}), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline: the reference's torch CPU path (oracle port), bounded sample
 # ---------------------------------------------------------------------------
 def cpu_baseline(seconds_budget: float = 12.0):
@@ -863,6 +902,9 @@ def main(argv=None):
                     help="print a per-phase CUDA-event breakdown of the device step to stderr "
                          "(extra events; not used for the reported value)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--pull-probe", default=None, metavar="MODES",
+                    help="diagnostic instead of the bench: comma list of remote,local,plain "
+                         "(needs two GPUs for remote)")
     ap.add_argument("--exchange", default="pull", choices=["pull", "push", "nccl"],
                     help="N>1 gradient exchange: the owner's update kernel sums the senders' "
                          "gradients over NVLink (pull, default); a push kernel into receive "
@@ -873,6 +915,8 @@ def main(argv=None):
     world, rank, local = dist_setup()
     if args.impl == "reference":
         return run_reference_arm(args, world, rank)
+    if args.pull_probe:
+        return pull_probe(args, args.pull_probe.split(","))
 
     from tidegs_b200 import _lib
 

@@ -422,6 +422,11 @@ typedef struct {
  * skipped and reported in err (TGS_DEV_BAD_SLICE). */
 TGS_API int tgs_grad_push(const TgsGradPushArgs* args, void* stream);
 
+/* Lets kernels on the current device read and write peer_device's memory
+ * directly (one process driving several GPUs; processes use IPC mappings).
+ * Already enabled counts as success. */
+TGS_API int tgs_peer_access_enable(int32_t peer_device);
+
 /* IPC handle of the allocation that contains dev_ptr (any device pointer,
  * for example a tensor inside a caching allocator's segment) and dev_ptr's
  * byte offset from that allocation's base. A peer maps the allocation with

@@ -281,6 +281,34 @@ def test_pull_sum_adam_equals_exchange_then_adam(W, B):
         assert torch.equal(opt_a._state, opt_b._state)
 
 
+def test_pull_reads_a_sender_on_another_gpu_in_process():
+    """One process, two GPUs: rank 1's gradients on cuda:1 are read over
+    peer access by the owner's kernel on cuda:0; same result as the
+    exchange + sum + plain update."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    W, B = 2, 64
+    rng = np.random.default_rng(12)
+    vis = [sorted(set(rng.integers(0, 40, 20).tolist())) for _ in range(W)]
+    ex, plans, recvs = _emulate(vis, W, B)
+    grads = [_compact_grads(r, sorted(int(b) for b in plans[r].send_blocks), B)[1]
+             for r in range(W)]
+    grads[1] = {n: t.to("cuda:1") for n, t in grads[1].items()}
+    plan = plans[0]
+    owned = plan.out_blocks.tolist()
+    params = {n: torch.randn((len(owned) * B, w), device="cuda:0") for n, w in ob.WIDTHS.items()}
+    summed = ex.reduce(plan, recvs[0])
+    opt_a, g_a = _owner(owned, B, params)
+    opt_b, g_b = _owner(owned, B, params)
+    pull = PeerGradPull.in_process(grads, 0, B, "cuda:0")
+    ids = torch.arange(len(owned) * B, device="cuda:0")
+    for step in (1, 2):
+        assert opt_a.step(step, g_a, ids, summed) == opt_b.step_pulled(step, g_b, ids, pull, plan)
+    for n in NAMES:
+        assert torch.equal(getattr(g_a, "_" + n), getattr(g_b, "_" + n)), n
+    assert torch.equal(opt_a._state, opt_b._state)
+
+
 def test_pull_rejects_rows_that_do_not_match_the_plan():
     W, B = 2, 32
     vis = [[0, 1], [1]]

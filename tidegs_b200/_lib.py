@@ -159,6 +159,7 @@ SIGNATURES = {
     "tgs_peer_buffer_open": (C.c_int, [C.POINTER(PeerHandle), C.POINTER(_vp)]),
     "tgs_peer_buffer_close": (C.c_int, [_vp]),
     "tgs_peer_export": (C.c_int, [_vp, C.POINTER(PeerHandle), C.POINTER(_i64)]),
+    "tgs_peer_access_enable": (C.c_int, [_i32]),
     "tgs_resident_adam_apply_sum": (C.c_int, [C.POINTER(ResidentAdamSumArgs), _vp]),
 }
 

@@ -284,3 +284,20 @@ extern "C" int tgs_peer_export(const void* dev_ptr, TgsPeerHandle* handle, int64
   *offset = static_cast<int64_t>(reinterpret_cast<CUdeviceptr>(dev_ptr) - base);
   return TGS_OK;
 }
+
+extern "C" int tgs_peer_access_enable(int32_t peer_device) {
+  int dev = 0;
+  TGS_CUDA(cudaGetDevice(&dev));
+  if (peer_device == dev) return TGS_OK;
+  int can = 0;
+  TGS_CUDA(cudaDeviceCanAccessPeer(&can, dev, peer_device));
+  TGS_CHECK_ARG(can != 0, "tgs_peer_access_enable: device %d cannot access device %d", dev,
+                peer_device);
+  const cudaError_t e = cudaDeviceEnablePeerAccess(peer_device, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();  // reset the last-error state this call left behind
+    return TGS_OK;
+  }
+  TGS_CUDA(e);
+  return TGS_OK;
+}

@@ -455,9 +455,15 @@ class PeerGradPull:
     def in_process(cls, grads_by_rank: Sequence[Mapping[str, torch.Tensor]], rank: int,
                    block_size: int, device) -> "PeerGradPull":
         """Every rank's gradients live in this process (ranks emulated on one
-        GPU): no IPC mappings and no barriers."""
+        GPU, or one process driving several GPUs): no IPC mappings and no
+        barriers; gradients on other devices are read through peer access."""
         self = cls.__new__(cls)
         self.device = _lib.require_cuda(device, "PeerGradPull")
+        with torch.cuda.device(self.device):
+            for g in grads_by_rank:
+                other = g["xyz"].device
+                if other != self.device:
+                    _lib.call("tgs_peer_access_enable", int(other.index))
         self.block_size = int(block_size)
         self.group = None
         self.world = len(grads_by_rank)

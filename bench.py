@@ -810,6 +810,90 @@ def pull_probe(args, modes):
 
 
 # ---------------------------------------------------------------------------
+# Diagnostic: touched-only gradient accumulation of a camera batch
+# ---------------------------------------------------------------------------
+def accum_probe(args):
+    """Not the bench line. A camera batch of the configs[3] shape (16 cameras,
+    each seeing a contiguous run of 24-56 resident blocks of 16,384 rows out
+    of 2048) accumulated by SparseGradAccumulator, and by the reference's own
+    torch operations on the same GPU (engine.py:1801-1826: mask, nonzero,
+    zeros; :2434-2471: searchsorted + six scatter_add_ per camera). Checks the
+    two results are equal; prints one JSON line (CUDA events, median)."""
+    from tidegs_b200 import SparseGradAccumulator
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    M = SLOTS * B
+    rng = np.random.default_rng(10_000)
+    filters, grads = [], []
+    for _ in range(16):
+        length = max(1, int(rng.integers(24, 56) * SLOTS / 2048))
+        start = int(rng.integers(0, max(1, SLOTS - length)))
+        f = torch.arange(start * B, (start + length) * B, dtype=torch.int64, device=dev)
+        n = f.numel()
+        filters.append(f)
+        grads.append({k: torch.empty((n, w), device=dev).normal_(0, 1e-3) for k, w in
+                      (("xyz", 3), ("opacity", 1), ("scaling", 3), ("rotation", 4), ("shs", 48))})
+    filter_rows = sum(f.numel() for f in filters)
+
+    split = []
+
+    def ours():
+        acc = SparseGradAccumulator(filters, M)
+        mid = torch.cuda.Event(enable_timing=True)
+        mid.record()
+        for f, g in zip(filters, grads):
+            acc.add(f, g["xyz"], g["opacity"], g["scaling"], g["rotation"], g["shs"])
+        split.append(mid)
+        return acc.sparse_grad_local_ids, acc.sparse_grad_components
+
+    def reference():
+        mask = torch.zeros((M,), dtype=torch.bool, device=dev)
+        for f in filters:
+            mask.scatter_(0, f, True)
+        ids = torch.nonzero(mask, as_tuple=False).flatten()
+        n = int(ids.numel())
+        comps = {k: torch.zeros((n, w), device=dev) for k, w in WIDTHS.items()}
+        for f, g in zip(filters, grads):
+            idx = torch.searchsorted(ids, f)
+            for k, w in (("xyz", 3), ("opacity", 1), ("scaling", 3), ("rotation", 4)):
+                comps[k].scatter_add_(0, idx.reshape(-1, 1).expand(-1, w), g[k])
+            comps["features_dc"].scatter_add_(0, idx.reshape(-1, 1).expand(-1, 3), g["shs"][:, :3])
+            comps["features_rest"].scatter_add_(0, idx.reshape(-1, 1).expand(-1, 45),
+                                                g["shs"][:, 3:48])
+        return ids, comps
+
+    out = {}
+    adds = []
+    for name, fn in (("tidegs_b200", ours), ("reference_torch_ops", reference)):
+        times = []
+        for k in range(args.warmup + args.steps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            split.clear()
+            e0.record()
+            res = fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if k >= args.warmup:
+                times.append(e0.elapsed_time(e1))
+                if split:
+                    adds.append(split[0].elapsed_time(e1))
+        out[name] = (sorted(times)[len(times) // 2], res)
+    (ids_a, ca), (ids_b, cb) = out["tidegs_b200"][1], out["reference_torch_ops"][1]
+    equal = bool(torch.equal(ids_a, ids_b)) and all(torch.equal(ca[k], cb[k]) for k in WIDTHS)
+    ms = out["tidegs_b200"][0]
+    print(json.dumps({"probe": "sparse_grad_accumulation", "cameras": len(filters),
+                      "filter_rows": filter_rows, "touched_rows": int(ids_a.numel()),
+                      "ms": ms, "reference_torch_ops_ms": out["reference_torch_ops"][0],
+                      "equal_to_reference_ops": equal,
+                      "accumulate_ms": sorted(adds)[len(adds) // 2],
+                      "accumulate_GBps": filter_rows * 712 / (sorted(adds)[len(adds) // 2] / 1e3)
+                      / 1e9}), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # CPU baseline: the reference's torch CPU path (oracle port), bounded sample
 # ---------------------------------------------------------------------------
 def cpu_baseline(seconds_budget: float = 12.0):
@@ -905,6 +989,9 @@ def main(argv=None):
     ap.add_argument("--pull-probe", default=None, metavar="MODES",
                     help="diagnostic instead of the bench: comma list of remote,local,plain "
                          "(needs two GPUs for remote)")
+    ap.add_argument("--accum-probe", action="store_true",
+                    help="diagnostic instead of the bench: touched-only gradient accumulation "
+                         "of a camera batch against the reference's torch operations")
     ap.add_argument("--exchange", default="pull", choices=["pull", "push", "nccl"],
                     help="N>1 gradient exchange: the owner's update kernel sums the senders' "
                          "gradients over NVLink (pull, default); a push kernel into receive "
@@ -917,6 +1004,8 @@ def main(argv=None):
         return run_reference_arm(args, world, rank)
     if args.pull_probe:
         return pull_probe(args, args.pull_probe.split(","))
+    if args.accum_probe:
+        return accum_probe(args)
 
     from tidegs_b200 import _lib
 

@@ -70,7 +70,8 @@ enum {
   TGS_DEV_ID_NOT_SORTED = 2,     /* local row ids are not strictly ascending */
   TGS_DEV_ID_NOT_RESIDENT = 3,   /* a local row id lies in no resident block */
   TGS_DEV_WAIT_TIMEOUT = 4,      /* a bounded mbarrier wait gave up */
-  TGS_DEV_BAD_SLICE = 5          /* a copy segment/plan is inconsistent */
+  TGS_DEV_BAD_SLICE = 5,         /* a copy segment/plan is inconsistent */
+  TGS_DEV_ID_NOT_TOUCHED = 6     /* a filter id is missing from the touched rows */
 };
 
 enum { TGS_LAYOUT_CACHE = 0, TGS_LAYOUT_UNIFIED = 1 };
@@ -355,6 +356,68 @@ TGS_API int tgs_pack_rows(const TgsPackArgs* args, void* stream);
  * _resident_block_bounds_kernel (:990-1061). */
 TGS_API int tgs_block_bounds(const float* xyz, const int64_t* start, const int64_t* count,
                      int32_t n_plans, float* bounds, void* stream);
+
+/* ------------------------------------------------------------------------ */
+/* Touched-only gradient accumulation of a camera batch                      */
+/* Replaces: strategies/tide_engine/engine.py                                */
+/*   :1801-1826  touched mask (zeros + scatter_ True) -> nonzero ids,        */
+/*               local_to_global gather, zero-filled compact components      */
+/*   :2434-2471  per camera: searchsorted + six scatter_add_                 */
+/* ------------------------------------------------------------------------ */
+
+/* Sets bit ids[i] of a bitmap of num_bits bits for every i; ids outside
+ * [0, num_bits) are skipped and reported in err (TGS_DEV_ID_OUT_OF_RANGE).
+ * The touched-row mask of engine.py:1803-1806 (scatter_ True per filter). */
+TGS_API int tgs_bitmap_set(uint32_t* bitmap, int64_t num_bits, const int64_t* ids, int64_t n,
+                   int32_t* err, void* stream);
+
+/* Scratch words tgs_bitmap_list needs for num_bits bits. */
+TGS_API int64_t tgs_bitmap_list_scratch_words(int64_t num_bits);
+
+/* Ascending positions of the set bits among the first num_bits bits of
+ * bitmap (bit i = word i/32, bit i%32), *dev_count = how many. Multi-CTA,
+ * order preserving (tile counts, one-CTA scan, ranked writes). With
+ * tgs_bitmap_set setting the bits of every camera's filter, this is the
+ * touched-row list (torch.nonzero of the mask, engine.py:1803-1807).
+ * pos_map (optional, [num_bits] int32, filled with -1 by the caller; fewer
+ * than 2^31 set bits): pos_map[b] = rank of set bit b, so that a later
+ * lookup of a row's position is one load instead of a binary search. */
+TGS_API int tgs_bitmap_list(const uint32_t* bitmap, int64_t num_bits, int64_t* out_ids,
+                    int64_t* dev_count, int64_t* scratch, int32_t* pos_map, void* stream);
+
+/* out[i] = src[idx[i]] (int64), e.g. local_to_global[touched ids]
+ * (engine.py:1815). Indices outside [0, n_src) are reported in err. */
+TGS_API int tgs_gather_i64(int64_t* out, const int64_t* src, int64_t n_src, const int64_t* idx,
+                   int64_t n, int32_t* err, void* stream);
+
+typedef struct {
+  const int64_t* touched;   /* [n_touched] ascending touched local ids */
+  int64_t n_touched;
+  /* optional: the pos_map of tgs_bitmap_list for these touched rows; a row's
+   * position is then pos_map[id] (-1: not touched) instead of a binary
+   * search of touched */
+  const int32_t* pos_map;
+  int64_t pos_map_len;
+  const int64_t* filter;    /* [n_filter] this camera's local ids */
+  int64_t n_filter;
+  /* The camera's gradients per component (xyz, opacity, scaling, rotation,
+   * features_dc, features_rest), row r of component c at
+   * src[c] + r * src_stride[c] (floats); a NULL component is skipped (the
+   * reference skips the SH components when they have no gradient). The SH
+   * gradient [n, 48] passes as dc = shs (stride 48), rest = shs + 3. */
+  const float* src[TGS_NUM_COMPONENTS];
+  int64_t src_stride[TGS_NUM_COMPONENTS];
+  float* acc[TGS_NUM_COMPONENTS];  /* [n_touched, W_c] compact gradients */
+  /* 1: no id repeats inside filter (true of projection filters): each sum
+   * is one exactly rounded addition. 0: atomic additions (order of repeated
+   * ids unspecified, as in torch's scatter_add_ on a GPU). */
+  int32_t unique_filter;
+  int32_t* err;             /* [4] TGS_DEV_ID_NOT_TOUCHED for a missing id */
+} TgsSparseAccumArgs;
+
+/* acc[c][searchsorted(touched, filter[r])] += src row r of component c, all
+ * six components in one launch. */
+TGS_API int tgs_sparse_grad_accumulate(const TgsSparseAccumArgs* args, void* stream);
 
 /* ------------------------------------------------------------------------ */
 /* Multi-GPU gradient exchange (no counterpart in the reference, which is    */

@@ -12,6 +12,8 @@ checked against golden vectors produced by running the reference's own CPU
 code paths (tests/golden/make_golden.py). The SelectiveAdam restatement
 follows submodules/clm_kernels/adam.cu and is checked against that kernel
 compiled from the reference sources (oracle/build_ref.py) where a GPU is
-available. The Sophia restatement has no reference implementation in TideGS:
-parity unpinned.
+available. The touched-only gradient accumulation (sparse_grad.py) is
+checked against the reference's own torch operations run on the CPU. The
+Sophia restatement has no reference implementation in TideGS: parity
+unpinned.
 """

@@ -74,7 +74,8 @@ def test_struct_offsets_match_the_c_compiler(tmp_path):
         pytest.skip("gcc not available")
     structs = {name: getattr(_lib, name) for name in (
         "ResidentCountArgs", "ResidentAdamArgs", "DenseGroup", "DenseArgs", "UnpackArgs",
-        "CopyBlocksArgs", "PackArgs", "BlockSumArgs", "GradPushArgs", "PeerHandle")}
+        "CopyBlocksArgs", "PackArgs", "BlockSumArgs", "GradPushArgs", "PeerHandle",
+        "ResidentAdamSumArgs", "SparseAccumArgs")}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "tidegs_b200.h"',
              'int main(void) {']
     expect = []

@@ -6,6 +6,7 @@ Drop-in classes (same names and behaviour as the reference's):
     SelectiveAdam, ResidentAdamContext   optimizer.py
     DoubleBufferGPUWorkingSet, GPUBuffer strategies/tide_engine/double_buffer_gpu.py
     GPUWorkingSet, PendingBlockWriteback strategies/tide_engine/gpu_working_set.py
+    SparseGradAccumulator                strategies/tide_engine/engine.py:1793-1826, 2434-2471
 plus SelectiveSophia (no reference counterpart) and PinnedBlockPool.
 
 All compute runs in libtidegs_b200.so (include/tidegs_b200.h); importing the
@@ -18,10 +19,12 @@ from .double_buffer_gpu import DoubleBufferGPUWorkingSet, GPUBuffer, ResidentHan
 from .gpu_resident_optimizer import GPUResidentAdam
 from .gpu_working_set import GPUWorkingSet, PendingBlockBounds, PendingBlockWriteback
 from .optimizer import ResidentAdamContext, SelectiveAdam, SelectiveSophia
+from .sparse_grad import SparseGradAccumulator
 
 __all__ = [
     "BlockBatch", "BlockLayout", "BlockReader", "PinnedBlockPool", "UnifiedParamsBlockReader",
     "parse_block_row_components", "DoubleBufferGPUWorkingSet", "GPUBuffer",
     "ResidentHandoffResult", "GPUResidentAdam", "GPUWorkingSet", "PendingBlockBounds",
     "PendingBlockWriteback", "ResidentAdamContext", "SelectiveAdam", "SelectiveSophia",
+    "SparseGradAccumulator",
 ]

@@ -32,6 +32,7 @@ DEV_ERRORS = {
     3: "local row id is not inside any resident block",
     4: "bounded device wait timed out",
     5: "inconsistent copy plan",
+    6: "filter id is not among the touched rows",
 }
 
 _vp = C.c_void_p
@@ -129,6 +130,15 @@ class ResidentAdamSumArgs(C.Structure):
     ]
 
 
+class SparseAccumArgs(C.Structure):
+    _fields_ = [
+        ("touched", _vp), ("n_touched", _i64), ("pos_map", _vp), ("pos_map_len", _i64),
+        ("filter", _vp), ("n_filter", _i64),
+        ("src", _vp * NUM_COMPONENTS), ("src_stride", _i64 * NUM_COMPONENTS),
+        ("acc", _vp * NUM_COMPONENTS), ("unique_filter", _i32), ("err", _vp),
+    ]
+
+
 # name -> (restype, argtypes). Keep in sync with include/tidegs_b200.h.
 SIGNATURES = {
     "tgs_version": (C.c_int, []),
@@ -161,6 +171,11 @@ SIGNATURES = {
     "tgs_peer_export": (C.c_int, [_vp, C.POINTER(PeerHandle), C.POINTER(_i64)]),
     "tgs_peer_access_enable": (C.c_int, [_i32]),
     "tgs_resident_adam_apply_sum": (C.c_int, [C.POINTER(ResidentAdamSumArgs), _vp]),
+    "tgs_bitmap_set": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _vp]),
+    "tgs_bitmap_list_scratch_words": (_i64, [_i64]),
+    "tgs_bitmap_list": (C.c_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "tgs_gather_i64": (C.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _vp]),
+    "tgs_sparse_grad_accumulate": (C.c_int, [C.POINTER(SparseAccumArgs), _vp]),
 }
 
 _lock = threading.Lock()
@@ -208,7 +223,8 @@ KERNELS_PER_CALL = {
     "tgs_global_to_local_compact_noalloc": 3,
     "tgs_dirty_mark": 1, "tgs_dirty_select": 1, "tgs_dirty_list": 1, "tgs_pack_rows": 1,
     "tgs_block_bounds": 1, "tgs_block_grad_sum": 1, "tgs_copy_small": 1, "tgs_grad_push": 1,
-    "tgs_resident_adam_apply_sum": 1,
+    "tgs_resident_adam_apply_sum": 1, "tgs_bitmap_list": 3, "tgs_gather_i64": 1, "tgs_bitmap_set": 1,
+    "tgs_sparse_grad_accumulate": 1,
 }
 launch_counter = {"kernels": 0}
 

@@ -24,7 +24,8 @@ BUILD_DIR = REPO_DIR / "_build" / "tidegs_b200"
 LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libtidegs_b200.so"
 
-SOURCES = ("tgs_abi.cu", "tgs_adam.cu", "tgs_blocks.cu", "tgs_dirty.cu", "tgs_exchange.cu")
+SOURCES = ("tgs_abi.cu", "tgs_adam.cu", "tgs_blocks.cu", "tgs_dirty.cu", "tgs_exchange.cu",
+           "tgs_sparse.cu")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

@@ -152,20 +152,6 @@ __device__ __forceinline__ void adam_elem(float& p, float& m, float& v, float gr
   p = fsub(p, fmul(fdiv(m, denom), step_scale));
 }
 
-// Selects entry c of a 6-entry kernel-parameter array with constant offsets
-// (a dynamic index would copy the whole parameter block to local memory).
-template <typename T>
-__device__ __forceinline__ T pick6(const T (&arr)[kNumComp], int c) {
-  switch (c) {
-    case 0: return arr[0];
-    case 1: return arr[1];
-    case 2: return arr[2];
-    case 3: return arr[3];
-    case 4: return arr[4];
-    default: return arr[5];
-  }
-}
-
 // Per-row metadata shared by the lanes of a warp (two 16-byte halves, each
 // read with one broadcast shared-memory load).
 struct __align__(16) RowAddr {

@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "tgs_common.cuh"
+#include "tgs_scan.cuh"
 
 namespace tgs {
 namespace {
@@ -337,33 +338,6 @@ constexpr int kCompactThreads = 256;
 constexpr int kCompactPerThread = 8;
 constexpr int kCompactTile = kCompactThreads * kCompactPerThread;
 
-__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_sums, int& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += y;
-  }
-  if (lane == 31) warp_sums[warp] = x;
-  __syncthreads();
-  if (warp == 0) {
-    const int nw = blockDim.x >> 5;
-    int s = lane < nw ? warp_sums[lane] : 0;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += y;
-    }
-    if (lane < nw) warp_sums[lane] = s;
-  }
-  __syncthreads();
-  total = warp_sums[(blockDim.x >> 5) - 1];
-  const int base = warp == 0 ? 0 : warp_sums[warp - 1];
-  __syncthreads();
-  return base + x - v;
-}
-
 __global__ void __launch_bounds__(kCompactThreads) g2l_count_kernel(
     const int64_t* __restrict__ gids, int64_t n, const int64_t* __restrict__ block_starts,
     int64_t num_blocks, int64_t block_size, int64_t* __restrict__ tile_counts) {
@@ -378,44 +352,6 @@ __global__ void __launch_bounds__(kCompactThreads) g2l_count_kernel(
   int total;
   block_exclusive_scan(cnt, warp_sums, total);
   if (threadIdx.x == 0) tile_counts[blockIdx.x] = total;
-}
-
-__global__ void __launch_bounds__(1024) scan_counts_kernel(int64_t* __restrict__ counts,
-                                                           int64_t n_tiles,
-                                                           int64_t* __restrict__ total_out) {
-  __shared__ int64_t warp_sums[32];
-  __shared__ int64_t carry;
-  if (threadIdx.x == 0) carry = 0;
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int64_t b = 0; b < n_tiles; b += blockDim.x) {
-    const int64_t i = b + threadIdx.x;
-    const int64_t v = i < n_tiles ? counts[i] : 0;
-    int64_t x = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
-    }
-    if (lane == 31) warp_sums[warp] = x;
-    __syncthreads();
-    if (warp == 0) {
-      int64_t s = lane < static_cast<int>(blockDim.x >> 5) ? warp_sums[lane] : 0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int64_t y = __shfl_up_sync(0xffffffffu, s, o);
-        if (lane >= o) s += y;
-      }
-      warp_sums[lane] = s;
-    }
-    __syncthreads();
-    const int64_t wbase = warp == 0 ? 0 : warp_sums[warp - 1];
-    if (i < n_tiles) counts[i] = carry + wbase + x - v;
-    __syncthreads();
-    if (threadIdx.x == 0) carry += warp_sums[(blockDim.x >> 5) - 1];
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) *total_out = carry;
 }
 
 __global__ void __launch_bounds__(kCompactThreads) g2l_write_kernel(

@@ -82,6 +82,20 @@ __host__ __device__ constexpr int layout_comp_of(int layout, int j) {
              : (j < 3 ? 0 : j < 6 ? 2 : j < 10 ? 3 : j < 11 ? 1 : j < 14 ? 4 : 5);
 }
 
+// Selects entry c of a 6-entry kernel-parameter array with constant offsets
+// (a dynamic index would copy the whole parameter block to local memory).
+template <typename T>
+__device__ __forceinline__ T pick6(const T (&arr)[kNumComp], int c) {
+  switch (c) {
+    case 0: return arr[0];
+    case 1: return arr[1];
+    case 2: return arr[2];
+    case 3: return arr[3];
+    case 4: return arr[4];
+    default: return arr[5];
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Device error word helpers.
 // ---------------------------------------------------------------------------

@@ -563,6 +563,7 @@ class ApiStep:
     schedule's turnover, so every rank can replicate every owner's layout."""
 
     profile = None
+    _pending_activate = False
 
     def _mark(self, name, t):
         if self.profile is not None:
@@ -722,6 +723,10 @@ class ApiStep:
         the write-back of iteration k run."""
         db, ws, sched = self.db, self.ws, self.sched
         t = time.perf_counter()
+        if self.profile is not None:
+            step_ev = torch.cuda.Event(enable_timing=True)
+            step_ev.record()
+            db.prefetch_events = {}
         evict_pos, incoming_arr, _ = self.trace.turn[k]
         loaded = [int(b) for b in sched.slot_block]
         evicted = sorted(int(b) for b in sched.slot_block[evict_pos])
@@ -732,6 +737,13 @@ class ApiStep:
                           resident_block_ids=keep, evicted_block_ids=evicted,
                           block_reader=self.pool, defer_resident_copy=True)
         t = self._mark("start_prefetch", t)
+        if self._pending_activate:
+            # the views of the slots swapped in at the end of the previous
+            # step (after the N+1 DMA is queued: it needs only the slot map)
+            self._activate()
+            self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
+            self._pending_activate = False
+            t = self._mark("activate", t)
         ids, grads = self._grads_and_ids(k)
         t = self._mark("exchange", t)
         if isinstance(grads, tuple):
@@ -760,12 +772,22 @@ class ApiStep:
         t = self._mark("bounds_finalize", t)
         db.wait_for_prefetch(k + 1)
         t = self._mark("wait_prefetch", t)
+        if self.profile is not None:
+            # device timeline of the N+1 prefetch, relative to the step start
+            end_ev = torch.cuda.Event(enable_timing=True)
+            end_ev.record()
+            end_ev.synchronize()
+            for name, ev in db.prefetch_events.items():
+                key = "dev_" + name
+                self.profile[key] = self.profile.get(key, 0.0) + step_ev.elapsed_time(ev) / 1e3
+            key = "dev_wait_prefetch_done"
+            self.profile[key] = self.profile.get(key, 0.0) + step_ev.elapsed_time(end_ev) / 1e3
+            db.prefetch_events = None
+            t = time.perf_counter()
         db.swap_buffers()
         t = self._mark("swap", t)
         sched.slot_block[evict_pos] = incoming_arr
-        self._activate()
-        self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
-        self._mark("activate", t)
+        self._pending_activate = True
         self.h2d_bytes += TURNOVER * B * 59 * 4
         return int(ids.numel())
 

@@ -130,6 +130,7 @@ class DoubleBufferGPUWorkingSet:
 
         self.prefetch_stream = torch.cuda.Stream(device=self.device)
         self.resident_refresh_stream = torch.cuda.Stream(device=self.device)
+        self._unpack_stream = torch.cuda.Stream(device=self.device)
         self.prefetch_complete_event = torch.cuda.Event()
         self.resident_refresh_complete_event: Optional[torch.cuda.Event] = None
         self.prefetch_in_progress = False
@@ -173,6 +174,7 @@ class DoubleBufferGPUWorkingSet:
             "persistent_slot_updates": 0,
             "persistent_streamed_blocks": 0,
             "persistent_ab_fallbacks": 0,
+            "inline_prefetches": 0,
             "persistent_omega_reuses": 0,
             "resident_refresh_blocks": 0,
             "resident_plan_jobs": 0,
@@ -322,17 +324,29 @@ class DoubleBufferGPUWorkingSet:
         free_slices = sorted((source.block_to_local_slice[int(b)] for b in evicted),
                              key=lambda s: int(s.start))
         target_slices = {b: s for b, s in zip(incoming, free_slices)}
-        next_slices = {int(b): source.block_to_local_slice[int(b)] for b in keep_set}
-        next_slices.update(target_slices)
-        next_order = [b for b, _ in sorted(next_slices.items(), key=lambda it: int(it[1].start))]
+        # the full next slot map (next_slices / next_order) is only needed at
+        # swap time: persistent_plan_layout() builds it after the DMA is queued
         return {
-            "keep_blocks": sorted(keep_set),
+            "keep_set": keep_set,
             "incoming_blocks": incoming,
             "evicted_blocks": sorted(evicted),
             "target_slices": target_slices,
-            "next_slices": next_slices,
-            "next_order": next_order,
         }
+
+    def _persistent_plan_layout(self, plan) -> None:
+        """Completes a persistent plan with the slot map of the next step:
+        kept blocks stay in their slices, incoming ones take the freed ones,
+        loaded_blocks in slice order (double_buffer_gpu.py:604-649)."""
+        if "next_slices" in plan:
+            return
+        source = self.active_buffer
+        keep_set = plan["keep_set"]
+        next_slices = {int(b): source.block_to_local_slice[int(b)] for b in keep_set}
+        next_slices.update(plan["target_slices"])
+        plan["next_slices"] = next_slices
+        plan["next_order"] = [b for b, _ in sorted(next_slices.items(),
+                                                   key=lambda it: int(it[1].start))]
+        plan["keep_blocks"] = sorted(keep_set)
 
     @property
     def loaded_blocks(self) -> List[int]:
@@ -348,6 +362,7 @@ class DoubleBufferGPUWorkingSet:
         if persistent_plan is not None:
             if self._before_persistent_apply is not None:
                 self._before_persistent_apply()
+            self._persistent_plan_layout(persistent_plan)
             source = self.loading_buffer
             target = self.active_buffer
             incoming_blocks = persistent_plan["incoming_blocks"]
@@ -362,6 +377,8 @@ class DoubleBufferGPUWorkingSet:
             target.num_gaussians = int(target.xyz.shape[0])
             target._block_starts = _build_block_starts(target.block_to_local_slice,
                                                        self.num_blocks, self.device)
+            # the slot copy above reads the staging buffer on this stream
+            self._retire(source, torch.cuda.current_stream(self.device))
             source.clear()
             with self.lock:
                 self._persistent_plan = None
@@ -461,7 +478,7 @@ class DoubleBufferGPUWorkingSet:
         persistent_plan = self._persistent_plan
         if target == "loading" and persistent_plan is not None:
             requested = set(int(b) for b in block_ids)
-            reused = len(requested & set(persistent_plan["keep_blocks"]))
+            reused = len(requested & persistent_plan["keep_set"])
             with self.lock:
                 self._prefetch_finalized = True
                 self._deferred_resident_blocks = []
@@ -547,6 +564,7 @@ class DoubleBufferGPUWorkingSet:
             pointer_reader = getattr(block_reader, "block_host_pointers", None)
             pinned_reader = getattr(block_reader, "read_blocks_pinned", None)
             read_batch = getattr(block_reader, "read_batch", None)
+            self._mark_prefetch("h2d_start")
             if callable(pointer_reader) or callable(pinned_reader):
                 # Page-locked pool: one DMA per block straight into device
                 # staging, no CPU-side concatenation.
@@ -568,9 +586,34 @@ class DoubleBufferGPUWorkingSet:
                             raise ValueError(f"Invalid pinned block {b}: shape {tuple(host.shape)}")
                     src = np.asarray([blocks[b].data_ptr() for b in streamed_blocks], np.int64)
                 nbytes = want * (59 * 4)
-                dst = packed_gpu.data_ptr() + np.concatenate([[0], np.cumsum(nbytes)[:-1]])
-                _ops.h2d_blocks(dst.tolist(), src.tolist(), nbytes.tolist(), self.device)
+                row_off = np.concatenate([[0], np.cumsum(want)[:-1]]).astype(np.int64)
+                dst = packed_gpu.data_ptr() + row_off * (59 * 4)
+                ids_all = _ops.i64_to_device(streamed_blocks, self.device)
+                # DMA in chunks on this stream; each chunk is unpacked on the
+                # unpack stream as soon as its copies have landed, so only
+                # the last chunk's unpack follows the DMA
+                dma_stream = torch.cuda.current_stream(self.device)
+                for c0 in range(0, len(streamed_blocks), self.PREFETCH_CHUNK_BLOCKS):
+                    c1 = min(len(streamed_blocks), c0 + self.PREFETCH_CHUNK_BLOCKS)
+                    _ops.h2d_blocks(dst[c0:c1].tolist(), src[c0:c1].tolist(),
+                                    nbytes[c0:c1].tolist(), self.device)
+                    landed = torch.cuda.Event()
+                    landed.record(dma_stream)
+                    self._unpack_stream.wait_event(landed)
+                    r0 = int(row_off[c0])
+                    r1 = int(row_off[c1 - 1] + want[c1 - 1])
+                    with torch.cuda.stream(self._unpack_stream):
+                        _ops.unpack_rows(packed_gpu[r0:r1], layout_code(block_reader.layout),
+                                         target.components(), resident_rows + r0,
+                                         global_ids=target.local_to_global_idx,
+                                         block_ids=ids_all[c0:c1], block_size=self.block_size,
+                                         err=self._err)
+                self._mark_prefetch("h2d_end")
+                dma_stream.wait_stream(self._unpack_stream)
+                ids_all.record_stream(self._unpack_stream)
+                packed_gpu.record_stream(self._unpack_stream)
                 self.stats["direct_block_dma_calls"] += len(streamed_blocks)
+                self._finish_streamed(target, staging_slot)
             else:
                 if callable(read_batch):
                     staging, packed_gpu, staging_slot = self._acquire_host_staging(streamed_rows)
@@ -596,14 +639,12 @@ class DoubleBufferGPUWorkingSet:
                     packed_cpu, packed_gpu, streamed_rows, staging_slot = self._pack_streamed_blocks(
                         streamed_blocks, block_lengths, reader_blocks, block_reader.layout)
                 packed_gpu.copy_(packed_cpu, non_blocking=packed_cpu.is_pinned())
-            ids = _ops.i64_to_device(streamed_blocks, self.device)
-            _ops.unpack_rows(packed_gpu, layout_code(block_reader.layout), target.components(),
-                             resident_rows, global_ids=target.local_to_global_idx, block_ids=ids,
-                             block_size=self.block_size, err=self._err)
-            staging_event = torch.cuda.Event()
-            staging_event.record(torch.cuda.current_stream(self.device))
-            self._host_staging_events[staging_slot] = staging_event
-            self.stats["batched_h2d_calls"] += 1
+                self._mark_prefetch("h2d_end")
+                ids = _ops.i64_to_device(streamed_blocks, self.device)
+                _ops.unpack_rows(packed_gpu, layout_code(block_reader.layout), target.components(),
+                                 resident_rows, global_ids=target.local_to_global_idx,
+                                 block_ids=ids, block_size=self.block_size, err=self._err)
+                self._finish_streamed(target, staging_slot)
         else:
             streamed_rows = 0
 
@@ -617,6 +658,15 @@ class DoubleBufferGPUWorkingSet:
         self.stats["batched_materializations"] += 1
         self.stats["batched_resident_blocks"] += len(resident_blocks)
         self.stats["batched_streamed_blocks"] += len(streamed_blocks)
+
+    def _finish_streamed(self, target: GPUBuffer, staging_slot: int) -> None:
+        """Streamed rows are unpacked (on the current stream): the staging
+        slot may be reused once this point has been reached."""
+        self._mark_prefetch("unpack_end")
+        staging_event = torch.cuda.Event()
+        staging_event.record(torch.cuda.current_stream(self.device))
+        self._host_staging_events[staging_slot] = staging_event
+        self.stats["batched_h2d_calls"] += 1
 
     def _local_filters(self, target: GPUBuffer, filters_global) -> List[torch.Tensor]:
         out = []
@@ -632,11 +682,15 @@ class DoubleBufferGPUWorkingSet:
                                    sorted_visible_blocks: List[int], resident_set: set,
                                    evicted_set: set, filters_global: List[torch.Tensor],
                                    allow_resident_copy: bool, defer_resident_copy: bool,
-                                   block_reader, before_target_reuse) -> None:
+                                   block_reader, before_target_reuse, caller_stream=None) -> None:
         start_time = time.time()
         if before_target_reuse is not None:
             before_target_reuse()
         with torch.cuda.device(self.device), torch.cuda.stream(self.prefetch_stream):
+            # the buffer being refilled was last used by the caller's stream
+            # (optimizer, slot copies) and the resident-refresh stream
+            self._retire(target_buffer, *[st for st in (caller_stream, self.resident_refresh_stream)
+                                          if st is not None])
             target_buffer.clear()
             if not sorted_visible_blocks:
                 target_buffer.evicted_blocks = sorted(evicted_set)
@@ -660,6 +714,32 @@ class DoubleBufferGPUWorkingSet:
                 with self.lock:
                     self._prefetch_finalized = True
         self.stats["total_prefetch_time_ms"] += (time.time() - start_time) * 1000.0
+
+    #: blocks per DMA chunk of a page-locked prefetch (each chunk is unpacked
+    #: while the next one is in flight)
+    PREFETCH_CHUNK_BLOCKS = 128
+
+    def _retire(self, buffer: GPUBuffer, *streams) -> None:
+        """Keeps `buffer`'s device memory from being handed out again until
+        the work already enqueued on `streams` (which read or wrote it) has
+        run: the caching allocator would otherwise reuse it at once for the
+        next allocation on the stream it was allocated on."""
+        for t in (buffer.xyz, buffer.scaling, buffer.rotation, buffer.opacity,
+                  buffer.features_dc, buffer.features_rest, buffer.local_to_global_idx,
+                  buffer._block_starts):
+            if t is not None:
+                for st in streams:
+                    t.record_stream(st)
+
+    #: profiling hook (off by default): a dict that receives CUDA events
+    #: recorded on the prefetch stream at "h2d_start", "h2d_end", "unpack_end"
+    prefetch_events = None
+
+    def _mark_prefetch(self, name: str) -> None:
+        if self.prefetch_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.device))
+            self.prefetch_events[name] = ev
 
     def start_prefetch(self, iteration: int, visible_block_ids: List[int],
                        filters_global: Optional[List[torch.Tensor]] = None,
@@ -710,13 +790,31 @@ class DoubleBufferGPUWorkingSet:
                 prefetch_resident_set = resident_set
                 prefetch_deferred = defer_resident_copy
                 worker_fence = before_target_reuse
-            self._prefetch_future = self._prefetch_executor.submit(
-                self._run_block_reader_prefetch,
+            job = dict(
                 target_buffer=self.loading_buffer, source_buffer=self.active_buffer,
                 sorted_visible_blocks=prefetch_blocks, resident_set=prefetch_resident_set,
                 evicted_set=evicted_set, filters_global=list(filters_global or []),
                 allow_resident_copy=allow_resident_copy, defer_resident_copy=prefetch_deferred,
-                block_reader=block_reader, before_target_reuse=worker_fence)
+                block_reader=block_reader, before_target_reuse=worker_fence,
+                caller_stream=torch.cuda.current_stream(self.device))
+            if (plan is not None and worker_fence is None
+                    and callable(getattr(block_reader, "block_host_pointers", None))):
+                # A page-locked pool: reading is a pointer lookup, so the whole
+                # materialization only enqueues GPU work (DMA + unpack). Doing
+                # it here starts the DMA at once instead of when the worker
+                # thread next gets the interpreter lock.
+                future = Future()
+                try:
+                    self._run_block_reader_prefetch(**job)
+                    future.set_result(None)
+                except BaseException as exc:  # surfaced by wait_for_prefetch
+                    future.set_exception(exc)
+                self._prefetch_future = future
+                self._target_layout_ready.set()
+                self.stats["inline_prefetches"] += 1
+                return
+            self._prefetch_future = self._prefetch_executor.submit(
+                self._run_block_reader_prefetch, **job)
             self._prefetch_future.add_done_callback(lambda _f: self._target_layout_ready.set())
             return
         self._legacy_prefetch(visible_block_ids, filters_global, ram_cache, unified_params,
@@ -730,10 +828,12 @@ class DoubleBufferGPUWorkingSet:
         order, retained blocks copied from the active buffer, the rest taken
         from unified_params / block_cache / ram_cache
         (double_buffer_gpu.py:1277-1454)."""
+        caller_stream = torch.cuda.current_stream(self.device)
         with torch.cuda.device(self.device), torch.cuda.stream(self.prefetch_stream):
             start_time = time.time()
             target = self.loading_buffer
             source = self.active_buffer
+            self._retire(target, caller_stream, self.resident_refresh_stream)
             target.clear()
             sorted_visible = sorted(set(int(b) for b in visible_block_ids))
             resident_set = set(int(b) for b in (resident_block_ids or []))
@@ -881,6 +981,7 @@ class DoubleBufferGPUWorkingSet:
                                  unified_params: torch.Tensor) -> Dict[str, torch.Tensor]:
         """Synchronous load into the active buffer (double_buffer_gpu.py:1567-1645)."""
         target = self.active_buffer
+        self._retire(target, self.prefetch_stream, self.resident_refresh_stream)
         target.clear()
         if len(visible_block_ids) == 0:
             raise ValueError("No visible blocks to load!")

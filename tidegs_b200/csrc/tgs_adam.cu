@@ -7,6 +7,8 @@
 //   submodules/clm_kernels/adam.cu:12-41                     (SelectiveAdam math)
 #include <math.h>
 
+#include <mutex>
+
 #include "tgs_common.cuh"
 
 namespace tgs {
@@ -165,14 +167,44 @@ struct __align__(16) RowScale {
   uint32_t pad;
 };
 
+// Contiguous chunks (32 consecutive ids whose state rows are consecutive,
+// e.g. all rows of visible blocks) take a staged path: lane 0 copies the state
+// rows of the warp's next kStateBatch-row batches with one non-multicast bulk
+// copy each into a two-stage ring in shared memory, so that only parameters
+// and gradients travel through registers and twice as many rows are in
+// flight per warp. Waits are bounded; on timeout the warp records
+// TGS_DEV_WAIT_TIMEOUT, waits (bounded) for its copies in flight and exits.
+#ifndef TGS_STATE_BATCH
+#define TGS_STATE_BATCH 4
+#endif
+#ifndef TGS_STATE_STAGES
+#define TGS_STATE_STAGES 2
+#endif
+constexpr int kStateBatch = TGS_STATE_BATCH;
+constexpr int kStateStages = TGS_STATE_STAGES;
+constexpr int kStateStageBytes = kStateBatch * TGS_STATE_ROW_FLOATS * 4;  // 4 KB
+struct __align__(16) ApplyWarpSmem {
+  float4 stage[kStateStages][kStateBatch][32];
+  uint64_t bar[kStateStages];
+};
+constexpr int kApplySmemBytes = kApplyWarps * static_cast<int>(sizeof(ApplyWarpSmem));
+
 template <bool kPow2Batch>
 __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_kernel(const ResidentApplyParams a) {
   __shared__ RowAddr s_addr[kApplyWarps][32];
   __shared__ RowScale s_scale[kApplyWarps][32];
+  extern __shared__ __align__(16) unsigned char apply_smem[];
   if (load_error(a.err) != 0) return;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const unsigned full = 0xffffffffu;
+  ApplyWarpSmem& ws = reinterpret_cast<ApplyWarpSmem*>(apply_smem)[warp];
+  if (lane == 0) {
+    for (int st = 0; st < kStateStages; ++st) mbar_init(&ws.bar[st], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  uint32_t phase = 0;  // bit st: parity of stage st's next completion
   const AdamScalars hp = {a.beta1, a.beta2, a.omb1, a.omb2, a.eps, a.batch_size, a.inv_batch_size};
 
   // Per-lane column bindings (fixed for the whole kernel). Lanes past column
@@ -218,6 +250,79 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
 
     const float* gptr0 = gbase[0] + row0 * width[0];
     const float* gptr1 = gbase[1] + row0 * width[1];
+    const RowAddr first = s_addr[warp][0];
+    if (nr == 32 && s_addr[warp][31].id == first.id + 31 && s_addr[warp][31].sr == first.sr + 31) {
+      // staged path: state rows first.sr .. first.sr + 31 are contiguous
+      const float4* src = a.state + first.sr * 32;
+      if (lane == 0) {
+        for (int st = 0; st < kStateStages; ++st) {
+          mbar_arrive_expect_tx(&ws.bar[st], kStateStageBytes);
+          bulk_g2s(&ws.stage[st][0][0], src + st * kStateBatch * 32, kStateStageBytes,
+                   &ws.bar[st]);
+        }
+      }
+      uint32_t pending = (1u << kStateStages) - 1u;
+      bool timed_out = false;
+#pragma unroll 1
+      for (int q = 0; q < 32 / kStateBatch; ++q) {
+        const int st = q % kStateStages;
+        float g0[kStateBatch], g1[kStateBatch], p0[kStateBatch], p1[kStateBatch];
+#pragma unroll
+        for (int u = 0; u < kStateBatch; ++u) {
+          const int rr = q * kStateBatch + u;
+          const int64_t id = first.id + rr;
+          g0[u] = gptr0[rr * width[0]];
+          g1[u] = gptr1[rr * width[1]];
+          p0[u] = pbase[0][id * width[0]];
+          p1[u] = pbase[1][id * width[1]];
+        }
+        if (!mbar_wait_bounded(&ws.bar[st], (phase >> st) & 1u)) {
+          report_error(const_cast<int32_t*>(a.err), TGS_DEV_WAIT_TIMEOUT, row0);
+          timed_out = true;
+          break;
+        }
+        phase ^= 1u << st;
+        pending &= ~(1u << st);
+#pragma unroll
+        for (int u = 0; u < kStateBatch; ++u) {
+          const int rr = q * kStateBatch + u;
+          const RowScale rs = s_scale[warp][rr];
+          const float4 sv = ws.stage[st][u][lane];
+          const bool fresh = __shfl_sync(full, __float_as_uint(sv.x) == rs.stamp ? 1 : 0, 31) != 0;
+          float m0 = fresh ? sv.x : 0.f, v0 = fresh ? sv.y : 0.f;
+          float m1 = fresh ? sv.z : 0.f, v1 = fresh ? sv.w : 0.f;
+          adam_elem<kPow2Batch>(p0[u], m0, v0, g0[u], hp, fmul(rs.rb1, lr[0]), rs.ds);
+          adam_elem<kPow2Batch>(p1[u], m1, v1, g1[u], hp, fmul(rs.rb1, lr[1]), rs.ds);
+          float4 out;
+          out.x = stamp_lane ? __uint_as_float(rs.stamp) : (keep_lo ? m0 : 0.f);
+          out.y = keep_lo ? v0 : 0.f;
+          out.z = keep_hi ? m1 : 0.f;
+          out.w = keep_hi ? v1 : 0.f;
+          a.state[(first.sr + rr) * 32 + lane] = out;
+          const int64_t id = first.id + rr;
+          if (act[0]) pbase[0][id * width[0]] = p0[u];
+          if (act[1]) pbase[1][id * width[1]] = p1[u];
+        }
+        __syncwarp();  // every lane is done with the stage
+        const int qn = q + kStateStages;
+        if (qn < 32 / kStateBatch) {
+          if (lane == 0) {
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&ws.bar[st], kStateStageBytes);
+            bulk_g2s(&ws.stage[st][0][0], src + qn * kStateBatch * 32, kStateStageBytes,
+                     &ws.bar[st]);
+          }
+          pending |= 1u << st;
+        }
+      }
+      if (timed_out) {
+        for (int st = 0; st < kStateStages; ++st)
+          if ((pending >> st) & 1u) (void)mbar_wait_bounded(&ws.bar[st], (phase >> st) & 1u);
+        return;
+      }
+      __syncwarp();  // the tables are rewritten by the next chunk
+      continue;
+    }
     for (int r = 0; r < nr; r += kApplyUnroll) {
       float4 st[kApplyUnroll];
       float g0[kApplyUnroll], g1[kApplyUnroll], p0[kApplyUnroll], p1[kApplyUnroll];
@@ -831,6 +936,28 @@ int apply_grid(int64_t n_rows, int ctas_per_sm = kApplyMinBlocks) {
   return static_cast<int>(std::min<int64_t>(ctas_needed, cap));
 }
 
+// Launches resident_adam_kernel, raising its dynamic shared-memory limit on
+// first use on the current device.
+template <bool kPow2>
+int launch_apply(const ResidentApplyParams& p, int grid, cudaStream_t s) {
+  static bool configured[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  TGS_CUDA(cudaGetDevice(&dev));
+  TGS_CHECK_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      TGS_CUDA(cudaFuncSetAttribute(resident_adam_kernel<kPow2>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kApplySmemBytes));
+      configured[dev] = true;
+    }
+  }
+  resident_adam_kernel<kPow2><<<grid, kApplyThreads, kApplySmemBytes, s>>>(p);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
 }  // namespace
 
 extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* stream) {
@@ -841,10 +968,8 @@ extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* strea
   const int rc = fill_apply_params(a, true, "tgs_resident_adam_apply", &p, &pow2);
   if (rc != TGS_OK) return rc;
   const int grid = apply_grid(a->n_rows);
-  if (pow2) resident_adam_kernel<true><<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
-  else resident_adam_kernel<false><<<grid, kApplyThreads, 0, as_stream(stream)>>>(p);
-  TGS_LAUNCH_CHECK();
-  return TGS_OK;
+  return pow2 ? launch_apply<true>(p, grid, as_stream(stream))
+              : launch_apply<false>(p, grid, as_stream(stream));
 }
 
 extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void* stream) {

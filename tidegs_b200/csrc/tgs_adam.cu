@@ -112,7 +112,7 @@ struct ResidentApplyParams {
 // Occupancy target (CTAs per SM) and rows in flight per warp of the update
 // kernel; overridable at build time for tuning sweeps.
 #ifndef TGS_APPLY_MIN_BLOCKS
-#define TGS_APPLY_MIN_BLOCKS 3
+#define TGS_APPLY_MIN_BLOCKS 2
 #endif
 #ifndef TGS_APPLY_UNROLL
 #define TGS_APPLY_UNROLL 4
@@ -178,7 +178,10 @@ struct __align__(16) RowScale {
 #define TGS_STATE_BATCH 4
 #endif
 #ifndef TGS_STATE_STAGES
-#define TGS_STATE_STAGES 2
+#define TGS_STATE_STAGES 3
+#endif
+#ifndef TGS_STATE_PG_AHEAD
+#define TGS_STATE_PG_AHEAD 1
 #endif
 constexpr int kStateBatch = TGS_STATE_BATCH;
 constexpr int kStateStages = TGS_STATE_STAGES;
@@ -263,10 +266,40 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
       }
       uint32_t pending = (1u << kStateStages) - 1u;
       bool timed_out = false;
+#if TGS_STATE_PG_AHEAD
+      float ng0[kStateBatch], ng1[kStateBatch], np0[kStateBatch], np1[kStateBatch];
+#pragma unroll
+      for (int u = 0; u < kStateBatch; ++u) {
+        ng0[u] = gptr0[u * width[0]];
+        ng1[u] = gptr1[u * width[1]];
+        np0[u] = pbase[0][(first.id + u) * width[0]];
+        np1[u] = pbase[1][(first.id + u) * width[1]];
+      }
+#endif
 #pragma unroll 1
       for (int q = 0; q < 32 / kStateBatch; ++q) {
         const int st = q % kStateStages;
         float g0[kStateBatch], g1[kStateBatch], p0[kStateBatch], p1[kStateBatch];
+#if TGS_STATE_PG_AHEAD
+#pragma unroll
+        for (int u = 0; u < kStateBatch; ++u) {
+          g0[u] = ng0[u];
+          g1[u] = ng1[u];
+          p0[u] = np0[u];
+          p1[u] = np1[u];
+        }
+        if (q + 1 < 32 / kStateBatch) {
+#pragma unroll
+          for (int u = 0; u < kStateBatch; ++u) {
+            const int rr = (q + 1) * kStateBatch + u;
+            const int64_t id = first.id + rr;
+            ng0[u] = gptr0[rr * width[0]];
+            ng1[u] = gptr1[rr * width[1]];
+            np0[u] = pbase[0][id * width[0]];
+            np1[u] = pbase[1][id * width[1]];
+          }
+        }
+#else
 #pragma unroll
         for (int u = 0; u < kStateBatch; ++u) {
           const int rr = q * kStateBatch + u;
@@ -276,6 +309,7 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
           p0[u] = pbase[0][id * width[0]];
           p1[u] = pbase[1][id * width[1]];
         }
+#endif
         if (!mbar_wait_bounded(&ws.bar[st], (phase >> st) & 1u)) {
           report_error(const_cast<int32_t*>(a.err), TGS_DEV_WAIT_TIMEOUT, row0);
           timed_out = true;

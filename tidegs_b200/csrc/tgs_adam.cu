@@ -123,7 +123,7 @@ constexpr int kApplyUnroll = TGS_APPLY_UNROLL;
 constexpr int kApplyMinBlocks = TGS_APPLY_MIN_BLOCKS;
 // The pulling variant (kernel C') waits on remote reads: its own knobs.
 #ifndef TGS_SUM_MIN_BLOCKS
-#define TGS_SUM_MIN_BLOCKS 3
+#define TGS_SUM_MIN_BLOCKS 2
 #endif
 #ifndef TGS_SUM_UNROLL
 #define TGS_SUM_UNROLL 4
@@ -458,11 +458,19 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
   __shared__ RowAddr s_addr[kApplyWarps][32];
   __shared__ RowScale s_scale[kApplyWarps][32];
   __shared__ RowSeg s_seg[kApplyWarps][32];
+  extern __shared__ __align__(16) unsigned char apply_smem[];
   const ResidentApplyParams& a = q.a;
   if (load_error(a.err) != 0) return;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const unsigned full = 0xffffffffu;
+  ApplyWarpSmem& ws = reinterpret_cast<ApplyWarpSmem*>(apply_smem)[warp];
+  if (lane == 0) {
+    for (int st = 0; st < kStateStages; ++st) mbar_init(&ws.bar[st], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  uint32_t phase = 0;  // bit st: parity of stage st's next completion
   const AdamScalars hp = {a.beta1, a.beta2, a.omb1, a.omb2, a.eps, a.batch_size, a.inv_batch_size};
 
   LaneCols lc;
@@ -558,6 +566,112 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
           }
         }
       };
+      const RowAddr first = s_addr[warp][0];
+      if (nr == 32 && s_addr[warp][31].id == first.id + 31 &&
+          s_addr[warp][31].sr == first.sr + 31) {
+        // Contiguous chunk: state rows staged by bulk copies as in kernel C;
+        // the next batch's parameters and contributions load into registers
+        // while the current batch updates.
+        const float4* src = a.state + first.sr * 32;
+        if (lane == 0) {
+          for (int st = 0; st < kStateStages; ++st) {
+            mbar_arrive_expect_tx(&ws.bar[st], kStateStageBytes);
+            bulk_g2s(&ws.stage[st][0][0], src + st * kStateBatch * 32, kStateStageBytes,
+                     &ws.bar[st]);
+          }
+        }
+        uint32_t pending = (1u << kStateStages) - 1u;
+        bool timed_out = false;
+        float nx0[kStateBatch], nx1[kStateBatch], ny0[kStateBatch], ny1[kStateBatch];
+        float np0[kStateBatch], np1[kStateBatch];
+#pragma unroll
+        for (int u = 0; u < kStateBatch; ++u) {
+          load_grads(u, nx0[u], nx1[u], ny0[u], ny1[u]);
+          np0[u] = pbase[0][(first.id + u) * width[0]];
+          np1[u] = pbase[1][(first.id + u) * width[1]];
+        }
+#pragma unroll 1
+        for (int qb = 0; qb < 32 / kStateBatch; ++qb) {
+          const int st = qb % kStateStages;
+          float x0[kStateBatch], x1[kStateBatch], y0[kStateBatch], y1[kStateBatch];
+          float p0[kStateBatch], p1[kStateBatch];
+#pragma unroll
+          for (int u = 0; u < kStateBatch; ++u) {
+            x0[u] = nx0[u];
+            x1[u] = nx1[u];
+            y0[u] = ny0[u];
+            y1[u] = ny1[u];
+            p0[u] = np0[u];
+            p1[u] = np1[u];
+          }
+          if (qb + 1 < 32 / kStateBatch) {
+#pragma unroll
+            for (int u = 0; u < kStateBatch; ++u) {
+              const int rr = (qb + 1) * kStateBatch + u;
+              load_grads(rr, nx0[u], nx1[u], ny0[u], ny1[u]);
+              np0[u] = pbase[0][(first.id + rr) * width[0]];
+              np1[u] = pbase[1][(first.id + rr) * width[1]];
+            }
+          }
+          if (!mbar_wait_bounded(&ws.bar[st], (phase >> st) & 1u)) {
+            report_error(q.err, TGS_DEV_WAIT_TIMEOUT, row0);
+            timed_out = true;
+            break;
+          }
+          phase ^= 1u << st;
+          pending &= ~(1u << st);
+#pragma unroll
+          for (int u = 0; u < kStateBatch; ++u) {
+            const int rr = qb * kStateBatch + u;
+            const RowScale rs = s_scale[warp][rr];
+            const float4 sv = ws.stage[st][u][lane];
+            float g0 = x0[u], g1 = x1[u];
+            if (ns > 1) {
+              g0 = fadd(g0, y0[u]);
+              g1 = fadd(g1, y1[u]);
+            }
+#pragma unroll 1
+            for (int jj = kStagedContribs; jj < sg_cn; ++jj) {
+              float z0, z1;
+              load_contrib(q, lc, sg_cb + jj, sg_off + rr, z0, z1);
+              g0 = fadd(g0, z0);
+              g1 = fadd(g1, z1);
+            }
+            const bool fresh =
+                __shfl_sync(full, __float_as_uint(sv.x) == rs.stamp ? 1 : 0, 31) != 0;
+            float m0 = fresh ? sv.x : 0.f, v0 = fresh ? sv.y : 0.f;
+            float m1 = fresh ? sv.z : 0.f, v1 = fresh ? sv.w : 0.f;
+            adam_elem<kPow2Batch>(p0[u], m0, v0, g0, hp, fmul(rs.rb1, lr[0]), rs.ds);
+            adam_elem<kPow2Batch>(p1[u], m1, v1, g1, hp, fmul(rs.rb1, lr[1]), rs.ds);
+            float4 out;
+            out.x = stamp_lane ? __uint_as_float(rs.stamp) : (keep_lo ? m0 : 0.f);
+            out.y = keep_lo ? v0 : 0.f;
+            out.z = keep_hi ? m1 : 0.f;
+            out.w = keep_hi ? v1 : 0.f;
+            a.state[(first.sr + rr) * 32 + lane] = out;
+            if (act[0]) pbase[0][(first.id + rr) * width[0]] = p0[u];
+            if (act[1]) pbase[1][(first.id + rr) * width[1]] = p1[u];
+          }
+          __syncwarp();  // every lane is done with the stage
+          const int qn = qb + kStateStages;
+          if (qn < 32 / kStateBatch) {
+            if (lane == 0) {
+              fence_proxy_async_smem();
+              mbar_arrive_expect_tx(&ws.bar[st], kStateStageBytes);
+              bulk_g2s(&ws.stage[st][0][0], src + qn * kStateBatch * 32, kStateStageBytes,
+                       &ws.bar[st]);
+            }
+            pending |= 1u << st;
+          }
+        }
+        if (timed_out) {
+          for (int st = 0; st < kStateStages; ++st)
+            if ((pending >> st) & 1u) (void)mbar_wait_bounded(&ws.bar[st], (phase >> st) & 1u);
+          return;
+        }
+        __syncwarp();
+        continue;
+      }
       // gradients of the next batch load while the current one updates
       float n0[kSumFastUnroll], n1[kSumFastUnroll], m0n[kSumFastUnroll], m1n[kSumFastUnroll];
 #pragma unroll
@@ -992,6 +1106,28 @@ int launch_apply(const ResidentApplyParams& p, int grid, cudaStream_t s) {
   return TGS_OK;
 }
 
+// Launches resident_adam_sum_kernel, raising its dynamic shared-memory limit
+// on first use on the current device.
+template <bool kPow2>
+int launch_sum(const ResidentSumParams& q, int grid, cudaStream_t s) {
+  static bool configured[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  TGS_CUDA(cudaGetDevice(&dev));
+  TGS_CHECK_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      TGS_CUDA(cudaFuncSetAttribute(resident_adam_sum_kernel<kPow2>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kApplySmemBytes));
+      configured[dev] = true;
+    }
+  }
+  resident_adam_sum_kernel<kPow2><<<grid, kApplyThreads, kApplySmemBytes, s>>>(q);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
 }  // namespace
 
 extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* stream) {
@@ -1033,10 +1169,8 @@ extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void
   q.rotate_chunks = (a->rotate_rows / 32) % n_chunks;
   q.err = a->err;
   const int grid = apply_grid(a->adam.n_rows, kSumMinBlocks);
-  if (pow2) resident_adam_sum_kernel<true><<<grid, kApplyThreads, 0, as_stream(stream)>>>(q);
-  else resident_adam_sum_kernel<false><<<grid, kApplyThreads, 0, as_stream(stream)>>>(q);
-  TGS_LAUNCH_CHECK();
-  return TGS_OK;
+  return pow2 ? launch_sum<true>(q, grid, as_stream(stream))
+              : launch_sum<false>(q, grid, as_stream(stream));
 }
 
 extern "C" int tgs_selective_adam(const TgsDenseArgs* args, void* stream) {

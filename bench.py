@@ -71,6 +71,9 @@ def dist_setup():
 
         import torch.distributed as dist
 
+        # the only collectives are one-element barriers and set-up gathers:
+        # no use for NVLink multicast (NVLS) buffers
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))

@@ -19,7 +19,8 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-DEFAULT_REFERENCE = "/root/reference"
+# the reference checkout beside this repository (override: TIDEGS_REFERENCE)
+DEFAULT_REFERENCE = str(HERE.parent.parent / "reference")
 MODULE = "clm_adam_ref"
 
 

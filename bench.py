@@ -57,6 +57,10 @@ WIDTHS = {"xyz": 3, "opacity": 1, "scaling": 3, "rotation": 4, "features_dc": 3,
           "features_rest": 45}
 NAMES = tuple(WIDTHS)
 ADAM_BYTES_PER_ROW = 59 * 4 * 7          # grad r + param r/w + m r/w + v r/w
+# DRAM bytes per updated row of resident_adam_kernel measured by ncu
+# (dram__bytes_read.sum + dram__bytes_write.sum of one launch over its rows,
+# 256-slot case whose inputs all exceed L2: profiles/resident_adam_kernel_staged_256slots.md)
+ADAM_TRAFFIC_BYTES_PER_ROW = 1683.3
 LRS = {"xyz": 1.6e-4, "opacity": 0.05, "scaling": 5e-3, "rotation": 1e-3, "features_dc": 2.5e-3,
        "features_rest": 1.25e-4}
 
@@ -1150,7 +1154,10 @@ def main(argv=None):
                                     "pack + NCCL all-to-all + ordered owner sum"),
                        "l2": "every input larger than L2 (126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": ADAM_TRAFFIC_BYTES_PER_ROW * (sum(adam_rows) / len(adam_rows)),
+                         "traffic_note": "bytes per launch: ncu DRAM bytes per row of the "
+                                         "256-slot capture x rows per launch",
                          "kernel": "resident_adam_kernel",
                          "algorithmic_bytes_per_row": ADAM_BYTES_PER_ROW,
                          "avg_launch_ms": adam_avg_ms, "peak_source": peak_kind,

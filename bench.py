@@ -57,9 +57,9 @@ WIDTHS = {"xyz": 3, "opacity": 1, "scaling": 3, "rotation": 4, "features_dc": 3,
           "features_rest": 45}
 NAMES = tuple(WIDTHS)
 ADAM_BYTES_PER_ROW = 59 * 4 * 7          # grad r + param r/w + m r/w + v r/w
-# DRAM bytes per updated row of resident_adam_kernel measured by ncu
-# (dram__bytes_read.sum + dram__bytes_write.sum of one launch over its rows,
-# 256-slot case whose inputs all exceed L2: profiles/resident_adam_kernel_staged_256slots.md)
+# DRAM bytes per updated row of resident_adam_kernel measured by ncu:
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the 256-slot
+# step (every input larger than L2) = 1654.8 MB over its 983,040 rows
 ADAM_TRAFFIC_BYTES_PER_ROW = 1683.3
 LRS = {"xyz": 1.6e-4, "opacity": 0.05, "scaling": 5e-3, "rotation": 1e-3, "features_dc": 2.5e-3,
        "features_rest": 1.25e-4}

@@ -318,17 +318,19 @@ TGS_API int tgs_h2d_blocks(void* const* dev_dst, const void* const* host_src,
 /* Dirty tracking and write-back                                             */
 /* ------------------------------------------------------------------------ */
 
-/* Bit-packed dirty bitmap: bit (id & 31) of word id >> 5.
- * value != 0 sets the bits of ids, value == 0 clears them.
+/* Bit-packed dirty bitmap of num_blocks blocks: bit (id & 31) of word id >> 5.
+ * value != 0 sets the bits of ids, value == 0 clears them; ids outside
+ * [0, num_blocks) are ignored (the reference range-filters them).
  * Replaces double_buffer_gpu.py:494-508 / :530-543 (bool bitmap index_fill_). */
-TGS_API int tgs_dirty_mark(uint32_t* bitmap, const int64_t* ids, int64_t n, int32_t value,
-                   void* stream);
+TGS_API int tgs_dirty_mark(uint32_t* bitmap, int64_t num_blocks, const int64_t* ids, int64_t n,
+                   int32_t value, void* stream);
 
 /* Order-preserving warp-ballot compaction: out_ids = [ids[i] for i if bit set],
- * *dev_count = its length. Single CTA; n up to ~1M.
+ * *dev_count = its length; ids outside [0, num_blocks) count as clean.
+ * Single CTA; n up to ~1M.
  * Replaces double_buffer_gpu.py:510-523 dirty_blocks_for_eviction. */
-TGS_API int tgs_dirty_select(const uint32_t* bitmap, const int64_t* ids, int64_t n,
-                     int64_t* out_ids, int64_t* dev_count, void* stream);
+TGS_API int tgs_dirty_select(const uint32_t* bitmap, int64_t num_blocks, const int64_t* ids,
+                     int64_t n, int64_t* out_ids, int64_t* dev_count, void* stream);
 
 /* All set bits of the first num_blocks bits, ascending.
  * Replaces double_buffer_gpu.py:525-528 dirty_blocks (nonzero). */

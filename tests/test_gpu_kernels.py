@@ -138,3 +138,24 @@ def test_dirty_select_large_preserves_order():
     got = _ops.dirty_select(bitmap, ids)
     assert got == [b for b in ids if bits[b]]
     assert _ops.dirty_list(bitmap, nb) == np.nonzero(bits)[0].tolist()
+
+
+def test_dirty_mark_and_select_ignore_ids_outside_the_bitmap():
+    """tgs_dirty_mark / tgs_dirty_select bound every id by the bitmap's
+    block count: ids below 0 or past it are neither written nor read."""
+    from tidegs_b200 import _lib
+
+    nb = 40
+    guard = torch.zeros(4, dtype=torch.int32, device="cuda")  # words 0-1: bitmap, 2-3: guard
+    bitmap = guard[:2]
+    ids = torch.tensor([3, -1, 39, 40, 63, 64, 1 << 40], dtype=torch.int64, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.call("tgs_dirty_mark", bitmap.data_ptr(), nb, ids.data_ptr(), ids.numel(), 1, stream)
+    words = guard.cpu().numpy().view(np.uint32)
+    assert words[0] == (1 << 3) and words[1] == (1 << (39 - 32))
+    assert words[2] == 0 and words[3] == 0
+    out = torch.zeros(ids.numel() + 1, dtype=torch.int64, device="cuda")
+    _lib.call("tgs_dirty_select", bitmap.data_ptr(), nb, ids.data_ptr(), ids.numel(),
+              out[1:].data_ptr(), out[:1].data_ptr(), stream)
+    host = out.cpu().numpy()
+    assert host[1:1 + int(host[0])].tolist() == [3, 39]

@@ -252,11 +252,13 @@ def bitmap_words(num_blocks: int) -> int:
 
 
 def dirty_mark(bitmap: torch.Tensor, ids: Sequence[int], value: bool) -> None:
-    if not ids:
+    """Sets (value) or clears the bits of ids; ids beyond the bitmap are
+    ignored."""
+    if len(ids) == 0:
         return
     dev_ids = i64_to_device(ids, bitmap.device)
-    _lib.call("tgs_dirty_mark", bitmap.data_ptr(), dev_ids.data_ptr(), len(ids),
-              1 if value else 0, _stream(bitmap.device))
+    _lib.call("tgs_dirty_mark", bitmap.data_ptr(), bitmap.numel() * 32, dev_ids.data_ptr(),
+              len(ids), 1 if value else 0, _stream(bitmap.device))
     _keepalive(dev_ids, bitmap.device)
 
 
@@ -267,8 +269,8 @@ def dirty_select(bitmap: torch.Tensor, ids: Sequence[int]) -> List[int]:
     n = len(ids)
     dev_ids = i64_to_device(ids, device)
     out = torch.empty(n + 1, dtype=torch.int64, device=device)
-    _lib.call("tgs_dirty_select", bitmap.data_ptr(), dev_ids.data_ptr(), n, out[1:].data_ptr(),
-              out[:1].data_ptr(), _stream(device))
+    _lib.call("tgs_dirty_select", bitmap.data_ptr(), bitmap.numel() * 32, dev_ids.data_ptr(), n,
+              out[1:].data_ptr(), out[:1].data_ptr(), _stream(device))
     host = out.cpu().numpy()
     return host[1:1 + int(host[0])].tolist()
 

@@ -8,11 +8,12 @@
 namespace tgs {
 namespace {
 
-__global__ void dirty_mark_kernel(uint32_t* __restrict__ bitmap, const int64_t* __restrict__ ids,
-                                  int64_t n, int value) {
+__global__ void dirty_mark_kernel(uint32_t* __restrict__ bitmap, int64_t num_blocks,
+                                  const int64_t* __restrict__ ids, int64_t n, int value) {
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t id = ids[i];
+    if (id < 0 || id >= num_blocks) continue;  // not a block of this bitmap
     const uint32_t bit = 1u << (id & 31);
     if (value) atomicOr(bitmap + (id >> 5), bit);
     else atomicAnd(bitmap + (id >> 5), ~bit);
@@ -49,8 +50,8 @@ __device__ __forceinline__ int ballot_rank(bool flag, int* warp_counts, int& tot
 // One CTA walks the id list in order; each pass ranks its 1024 flags with
 // ballots and appends behind the running total, so output order = input order.
 __global__ void __launch_bounds__(kSelectThreads) dirty_select_kernel(
-    const uint32_t* __restrict__ bitmap, const int64_t* __restrict__ ids, int64_t n,
-    int64_t* __restrict__ out, int64_t* __restrict__ count) {
+    const uint32_t* __restrict__ bitmap, int64_t num_blocks, const int64_t* __restrict__ ids,
+    int64_t n, int64_t* __restrict__ out, int64_t* __restrict__ count) {
   __shared__ int warp_counts[32];
   int64_t written = 0;
   for (int64_t base = 0; base < n; base += kSelectThreads) {
@@ -59,7 +60,7 @@ __global__ void __launch_bounds__(kSelectThreads) dirty_select_kernel(
     bool flag = false;
     if (i < n) {
       id = ids[i];
-      flag = (bitmap[id >> 5] >> (id & 31)) & 1u;
+      flag = id >= 0 && id < num_blocks && ((bitmap[id >> 5] >> (id & 31)) & 1u);
     }
     int total;
     const int rank = ballot_rank(flag, warp_counts, total);
@@ -122,20 +123,20 @@ __global__ void __launch_bounds__(kSelectThreads) dirty_list_kernel(
 
 using namespace tgs;
 
-extern "C" int tgs_dirty_mark(uint32_t* bitmap, const int64_t* ids, int64_t n, int32_t value,
-                              void* stream) {
-  TGS_CHECK_ARG(n >= 0, "tgs_dirty_mark: n < 0");
+extern "C" int tgs_dirty_mark(uint32_t* bitmap, int64_t num_blocks, const int64_t* ids,
+                              int64_t n, int32_t value, void* stream) {
+  TGS_CHECK_ARG(n >= 0 && num_blocks >= 0, "tgs_dirty_mark: bad sizes");
   if (n == 0) return TGS_OK;
   TGS_CHECK_ARG(bitmap && ids, "tgs_dirty_mark: NULL pointer");
   const int grid = static_cast<int>(std::min<int64_t>(ceil_div<int64_t>(n, 256), 4096));
-  dirty_mark_kernel<<<grid, 256, 0, as_stream(stream)>>>(bitmap, ids, n, value);
+  dirty_mark_kernel<<<grid, 256, 0, as_stream(stream)>>>(bitmap, num_blocks, ids, n, value);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }
 
-extern "C" int tgs_dirty_select(const uint32_t* bitmap, const int64_t* ids, int64_t n,
-                                int64_t* out_ids, int64_t* dev_count, void* stream) {
-  TGS_CHECK_ARG(n >= 0, "tgs_dirty_select: n < 0");
+extern "C" int tgs_dirty_select(const uint32_t* bitmap, int64_t num_blocks, const int64_t* ids,
+                                int64_t n, int64_t* out_ids, int64_t* dev_count, void* stream) {
+  TGS_CHECK_ARG(n >= 0 && num_blocks >= 0, "tgs_dirty_select: bad sizes");
   TGS_CHECK_ARG(dev_count != nullptr, "tgs_dirty_select: dev_count is NULL");
   cudaStream_t s = as_stream(stream);
   if (n == 0) {
@@ -143,7 +144,8 @@ extern "C" int tgs_dirty_select(const uint32_t* bitmap, const int64_t* ids, int6
     return TGS_OK;
   }
   TGS_CHECK_ARG(bitmap && ids && out_ids, "tgs_dirty_select: NULL pointer");
-  dirty_select_kernel<<<1, kSelectThreads, 0, s>>>(bitmap, ids, n, out_ids, dev_count);
+  dirty_select_kernel<<<1, kSelectThreads, 0, s>>>(bitmap, num_blocks, ids, n, out_ids,
+                                                    dev_count);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

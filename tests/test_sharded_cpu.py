@@ -65,6 +65,26 @@ def test_push_destinations_match_all_to_all_delivery(W):
         assert pushed.tolist() == delivered
 
 
+@pytest.mark.parametrize("W", [2, 4, 7])
+def test_pull_sources_point_at_each_senders_rows(W):
+    """recv_src_tiles[t] is the row tile of received block t in its sender's
+    gradients (the sender's rendered blocks in ascending id): the pull kernel
+    reads contribution j of out block k from sender s at that tile."""
+    rng = np.random.default_rng(30 + W)
+    vis = [np.unique(rng.choice(200, 50, replace=False)) for _ in range(W)]
+    for owner in range(W):
+        plan = make_plan(vis, W, owner, block_size=1)
+        sender = np.repeat(np.arange(W), plan.recv_counts)
+        for t, b in enumerate(plan.recv_blocks.tolist()):
+            rendered = np.unique(vis[sender[t]])
+            assert rendered[plan.recv_src_tiles[t]] == b
+        for k, b in enumerate(plan.out_blocks.tolist()):
+            cs = plan.contrib_blocks[plan.contrib_offsets[k]:plan.contrib_offsets[k + 1]]
+            ranks = sender[cs].tolist()
+            assert ranks == sorted(ranks)  # summation in rank order
+            assert ranks == [r for r in range(W) if b in set(vis[r].tolist())]
+
+
 def test_plan_accepts_dense_order_table():
     vis = [[2, 6, 4], [4, 0]]
     table = np.full(10, -1, np.int64)

@@ -12,7 +12,10 @@ Gaussians x 59 fp32 (33.5 M Gaussians per GPU):
   3. dirty-and-evicted compaction of 512 evicted blocks (25 % turnover) and
      the CACHE-layout write-back pack of the dirty ones,
   4. materialization of 512 incoming blocks into the freed slots (packed rows
-     -> component arrays + global ids, then the slot remap).
+     -> component arrays + global ids, then the slot remap). The unpack into
+     the loading buffer is enqueued before the pack: it does not depend on the
+     write-back, and it keeps the device busy while the host waits for the
+     dirty list.
 `value` runs the step through the library entry points with every input
 already in HBM; `e2e` runs it through the Python drop-in classes with the
 incoming blocks streamed from a page-locked host pool (H2D inside the timed
@@ -518,19 +521,26 @@ class DeviceStep:
         evicted_blocks = sched.slot_block[evict_pos]
         _ops.dirty_mark(self.bitmap, evicted_blocks[dirty].tolist(), True)
         _ops.dirty_mark(self.bitmap, evicted_blocks[~dirty].tolist(), False)
-        wb_ids = _ops.dirty_select(self.bitmap, sorted(evicted_blocks.tolist()))
-        pos_of = {int(b): int(p) for b, p in zip(evicted_blocks, evict_pos)}
-        wb_pos = [pos_of[b] for b in wb_ids]
-        _ops.pack_rows(self.arena, [p * B for p in wb_pos], [B] * len(wb_pos),
-                       self.wb_staging[: len(wb_pos) * B], self._lib.LAYOUT_CACHE)
-        _ops.dirty_mark(self.bitmap, wb_ids, False)
-        self._phase("writeback")
-        # 4. materialize the incoming blocks into the freed slots
+        order = np.argsort(evicted_blocks, kind="stable")
+        selection = _ops.dirty_select_async(self.bitmap, evicted_blocks[order].tolist())
+        self._phase("dirty_select")
+        # 4. materialize the incoming blocks into the loading buffer; this does
+        # not depend on the write-back, so the device runs it while the host
+        # waits for the dirty list and plans the pack
         src = self.incoming_pool[(k % 2) * TURNOVER * B:(k % 2 + 1) * TURNOVER * B]
         ids_dev = _ops.i64_to_device(incoming, self.device)
         _ops.unpack_rows(src, self._lib.LAYOUT_CACHE, self.loading, 0,
                          global_ids=self.loading_gids, block_ids=ids_dev, block_size=B)
         self._phase("unpack")
+        wb_ids = selection.wait()
+        sorted_blocks = evicted_blocks[order]
+        wb_pos = evict_pos[order][np.searchsorted(sorted_blocks, np.asarray(wb_ids, np.int64))]
+        _ops.pack_rows(self.arena, (wb_pos * B).tolist(), [B] * wb_pos.size,
+                       self.wb_staging[: wb_pos.size * B], self._lib.LAYOUT_CACHE)
+        self._phase("pack")
+        _ops.dirty_mark(self.bitmap, wb_ids, False)
+        self._phase("writeback")
+        # 5. evicted slots take the incoming blocks
         _ops.copy_blocks(self.loading, self.loading_gids, self.arena, self.gids,
                          (np.arange(TURNOVER) * B).tolist(), (evict_pos * B).tolist(),
                          [B] * TURNOVER, self.device)

@@ -346,10 +346,12 @@ typedef struct {
   int64_t max_rows;           /* max(row_count) */
   float* out;                 /* [sum rows, 59] CACHE layout */
   int32_t layout;             /* output column order, normally TGS_LAYOUT_CACHE */
+  int32_t* err;               /* [4] device error word (may be NULL) */
 } TgsPackArgs;
 
-/* SoA -> packed CACHE rows for write-back, AoS tile assembled in shared memory
- * and written with TMA bulk stores where aligned.
+/* SoA -> packed CACHE rows for write-back: each 64-row tile's component ranges
+ * are streamed into shared memory with TMA bulk copies (plain loads where a
+ * range is not 16-byte aligned), then stored as packed rows.
  * Replaces gpu_working_set.py:35-86 _pack_resident_rows_kernel (:948-967). */
 TGS_API int tgs_pack_rows(const TgsPackArgs* args, void* stream);
 

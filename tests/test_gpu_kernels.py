@@ -45,6 +45,51 @@ def test_unpack_pack_roundtrip(layout, rows, offset):
     assert torch.equal(out, packed)
 
 
+@pytest.mark.parametrize("layout", ["cache", "unified"])
+@pytest.mark.parametrize("case", ["blocks", "ragged", "views"])
+def test_pack_many_plans_against_oracle(layout, case):
+    """Many plans: whole 16384-row blocks (bulk-staged tiles, more tiles than
+    the persistent grid holds stages, so every stage is refilled), ragged
+    counts and starts (plain-load tiles and short tail tiles), and component
+    views whose bases are not 16-byte aligned (every tile on plain loads)."""
+    from tidegs_b200 import _lib, _ops
+
+    code = _lib.LAYOUT_CACHE if layout == "cache" else _lib.LAYOUT_UNIFIED
+    rng = np.random.default_rng({"blocks": 1, "ragged": 2, "views": 3}[case])
+    B = 16384
+    if case == "blocks":
+        nsrc = 160
+        starts = (rng.permutation(nsrc)[:120] * B).tolist()
+        counts = [B] * len(starts)
+    else:
+        nsrc = 40
+        counts = rng.integers(1, 3 * 64 + 7, 300).tolist()
+        starts = [int(rng.integers(0, nsrc * B - c)) for c in counts]
+        counts[::7] = [64] * len(counts[::7])
+        starts[::5] = [int(s) & ~3 for s in starts[::5]]
+    rows = nsrc * B
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    if case == "views":
+        base = {n: torch.randn((rows + 1, w), generator=gen, device="cuda") for n, w in ob.WIDTHS.items()}
+        comps = {n: base[n][1:] for n in NAMES}
+        assert any(comps[n].data_ptr() % 16 for n in NAMES)
+    else:
+        comps = {n: torch.randn((rows, w), generator=gen, device="cuda") for n, w in ob.WIDTHS.items()}
+    total = int(sum(counts))
+    out_base = torch.full((total + 1, 59), -1.0, device="cuda")
+    out = out_base[1:] if case == "ragged" else out_base[:total]
+    err = torch.zeros(4, dtype=torch.int32, device="cuda")
+    _ops.pack_rows(comps, starts, counts, out, code, err=err)
+    torch.cuda.synchronize()
+    assert err.tolist() == [0, 0, 0, 0]
+    want = ob.pack_rows({n: comps[n].cpu().numpy() for n in NAMES}, starts, counts, layout)
+    np.testing.assert_array_equal(out.cpu().numpy(), want)
+    if case != "ragged":
+        assert (out_base[total:] == -1).all()
+    else:
+        assert (out_base[0] == -1).all()
+
+
 def test_unpack_misaligned_source_view():
     from tidegs_b200 import _lib, _ops
 

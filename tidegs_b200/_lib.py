@@ -97,7 +97,7 @@ class PackArgs(C.Structure):
     _fields_ = [
         ("comp", _vp * NUM_COMPONENTS), ("src_start", _vp), ("row_count", _vp),
         ("out_start", _vp), ("n_plans", _i32), ("max_rows", _i64), ("out", _vp),
-        ("layout", _i32),
+        ("layout", _i32), ("err", _vp),
     ]
 
 

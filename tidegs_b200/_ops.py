@@ -202,7 +202,8 @@ def global_to_local_compact(global_ids: torch.Tensor, block_starts: torch.Tensor
 
 
 def pack_rows(sources: Mapping[str, torch.Tensor], src_starts: Sequence[int],
-              row_counts: Sequence[int], out: torch.Tensor, layout_code: int) -> List[torch.Tensor]:
+              row_counts: Sequence[int], out: torch.Tensor, layout_code: int,
+              err: Optional[torch.Tensor] = None) -> List[torch.Tensor]:
     """Packs plan k's rows [src_starts[k], +row_counts[k]) into consecutive
     rows of `out` ([sum rows, 59]). Returns device tensors to keep alive."""
     n = len(row_counts)
@@ -225,6 +226,7 @@ def pack_rows(sources: Mapping[str, torch.Tensor], src_starts: Sequence[int],
     args.max_rows = int(max(row_counts))
     args.out = out.data_ptr()
     args.layout = int(layout_code)
+    args.err = _lib.ptr(err)
     _lib.call("tgs_pack_rows", args, _stream(device))
     return [plan]
 
@@ -262,17 +264,42 @@ def dirty_mark(bitmap: torch.Tensor, ids: Sequence[int], value: bool) -> None:
     _keepalive(dev_ids, bitmap.device)
 
 
-def dirty_select(bitmap: torch.Tensor, ids: Sequence[int]) -> List[int]:
-    if not ids:
-        return []
+class PendingIds:
+    """A device-side id list on its way to page-locked host memory: `wait()`
+    blocks until the copy has landed and returns the ids."""
+
+    def __init__(self, host: Optional[torch.Tensor], event, keep=()):
+        self._host, self._event, self._keep = host, event, keep
+
+    def wait(self) -> List[int]:
+        if self._host is None:
+            return []
+        self._event.synchronize()
+        host = self._host.numpy()
+        return host[1:1 + int(host[0])].tolist()
+
+
+def dirty_select_async(bitmap: torch.Tensor, ids: Sequence[int]) -> PendingIds:
+    """Enqueues the order-preserving dirty compaction of `ids` and the copy of
+    its result to the host on the current stream; the caller keeps enqueuing
+    work and collects the ids with `wait()`."""
+    if len(ids) == 0:
+        return PendingIds(None, None)
     device = bitmap.device
     n = len(ids)
     dev_ids = i64_to_device(ids, device)
     out = torch.empty(n + 1, dtype=torch.int64, device=device)
     _lib.call("tgs_dirty_select", bitmap.data_ptr(), bitmap.numel() * 32, dev_ids.data_ptr(), n,
               out[1:].data_ptr(), out[:1].data_ptr(), _stream(device))
-    host = out.cpu().numpy()
-    return host[1:1 + int(host[0])].tolist()
+    host = torch.empty(n + 1, dtype=torch.int64, pin_memory=True)
+    host.copy_(out, non_blocking=True)
+    event = torch.cuda.Event()
+    event.record(torch.cuda.current_stream(device))
+    return PendingIds(host, event, (dev_ids, out))
+
+
+def dirty_select(bitmap: torch.Tensor, ids: Sequence[int]) -> List[int]:
+    return dirty_select_async(bitmap, ids).wait()
 
 
 def dirty_list(bitmap: torch.Tensor, num_blocks: int) -> List[int]:

@@ -377,60 +377,145 @@ __global__ void __launch_bounds__(kCompactThreads) g2l_write_kernel(
 
 // ---------------------------------------------------------------------------
 // Write-back pack: SoA components -> packed rows (CACHE order by default).
-// Grid (64-row tile, plan). Threads gather the tile's component rows (each
-// component's rows are contiguous) into an AoS tile in shared memory; the
-// tile then leaves with one bulk store when the output rows are 16-byte
-// aligned, else with plain coalesced stores.
+// Persistent CTAs walk (plan, 64-row tile) pairs. A tile's rows of one
+// component are contiguous in the SoA arrays, so one thread streams the six
+// ranges into a shared-memory stage with bulk (TMA) copies, kPackStages tiles
+// ahead of the consumer; all threads then write the tile's packed rows with
+// coalesced stores, each element read from its component's range. Tiles whose
+// ranges are not 16-byte aligned are read with plain loads instead.
 // ---------------------------------------------------------------------------
 constexpr int kPackThreads = 256;
+constexpr int kPackStages = 4;
+constexpr int kPackCtasPerSm = 3;
+
+// First float of component c inside a staged tile (component order; every
+// offset is a multiple of 64 floats, so each range starts 16-byte aligned).
+__host__ __device__ constexpr int staged_offset(int c) {
+  return kTileRows * unified_offset(c);
+}
 
 struct PackParams {
   ConstComp6 comp;
   const int64_t* src_start;
   const int64_t* row_count;
   const int64_t* out_start;
-  int n_plans;
+  int64_t n_tiles;     // n_plans * tiles_per_plan
+  int tiles_per_plan;
   float* out;
-  int out_aligned;
+  int comp_aligned;    // all six component bases are 16-byte aligned
+  int32_t* err;
 };
 
+struct PackSmem {
+  float stage[kPackStages][kTileFloats];
+  uint64_t bar[kPackStages];
+  // Output column j: staged offset of its component (low 16 bits) + column
+  // within the component, and the component width (high 16 bits).
+  uint32_t col[kRowWidth];
+};
+constexpr size_t kPackSmemBytes = sizeof(PackSmem);
+
+struct PackTile {
+  int rows;       // <= 0: nothing to do
+  int64_t src;    // first source row
+  int64_t dst;    // first output row
+  bool bulk;
+};
+
+__device__ __forceinline__ PackTile pack_tile(const PackParams& a, int64_t t) {
+  PackTile d;
+  const int64_t k = t / a.tiles_per_plan;
+  const int64_t r0 = (t - k * a.tiles_per_plan) * kTileRows;
+  d.rows = static_cast<int>(min64(kTileRows, a.row_count[k] - r0));
+  d.src = a.src_start[k] + r0;
+  d.dst = a.out_start[k] + r0;
+  d.bulk = a.comp_aligned && (d.src & 3) == 0 && (d.rows & 3) == 0;
+  return d;
+}
+
 template <int kLayout>
-__global__ void __launch_bounds__(kPackThreads) pack_kernel(const PackParams a) {
-  __shared__ __align__(128) float tile[kTileFloats];
-  for (int k = blockIdx.y; k < a.n_plans; k += gridDim.y) {
-    const int64_t rows_total = a.row_count[k];
-    const int64_t r0 = static_cast<int64_t>(blockIdx.x) * kTileRows;
-    if (r0 >= rows_total) continue;
-    const int rows = static_cast<int>(min64(kTileRows, rows_total - r0));
-    const int64_t src = a.src_start[k] + r0;
-    const int64_t dst = a.out_start[k] + r0;
+__global__ void __launch_bounds__(kPackThreads, kPackCtasPerSm) pack_kernel(const PackParams a) {
+  extern __shared__ __align__(128) unsigned char pack_smem_raw[];
+  PackSmem& sm = *reinterpret_cast<PackSmem*>(pack_smem_raw);
+  const int tid = threadIdx.x;
+  if (tid < kRowWidth) {
+    const int c = layout_comp_of(kLayout, tid);
+    const int k = tid - layout_offset(kLayout, c);
+    sm.col[tid] = static_cast<uint32_t>(staged_offset(c) + k) |
+                  (static_cast<uint32_t>(comp_width(c)) << 16);
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kPackStages; ++s) mbar_init(&sm.bar[s], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  uint32_t pending = 0;  // stages with a bulk copy in flight (thread 0)
+  auto issue = [&](int64_t t, int s) {
+    if (t >= a.n_tiles) return;
+    const PackTile d = pack_tile(a, t);
+    if (d.rows <= 0 || !d.bulk) return;
+    mbar_arrive_expect_tx(&sm.bar[s], static_cast<uint32_t>(d.rows) * kRowWidth * sizeof(float));
 #pragma unroll
     for (int c = 0; c < kNumComp; ++c) {
       const int w = comp_width(c);
-      const int col = layout_offset(kLayout, c);
-      const float* __restrict__ s = a.comp.p[c] + src * w;
-      for (int e = threadIdx.x; e < rows * w; e += kPackThreads) {
-        const int r = e / w;
-        tile[r * kRowWidth + col + (e - r * w)] = s[e];
+      bulk_g2s(&sm.stage[s][staged_offset(c)], a.comp.p[c] + d.src * w,
+               static_cast<uint32_t>(d.rows * w) * sizeof(float), &sm.bar[s]);
+    }
+    pending |= 1u << s;
+  };
+
+  if (tid == 0) {
+    for (int s = 0; s < kPackStages; ++s) issue(blockIdx.x + static_cast<int64_t>(s) * gridDim.x, s);
+  }
+  uint32_t phase = 0;  // bit s: parity of stage s's next completion
+  int s = 0;
+  for (int64_t t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+    const PackTile d = pack_tile(a, t);
+    if (d.rows > 0) {
+      bool ok = true;
+      if (d.bulk) {
+        ok = mbar_wait_bounded(&sm.bar[s], (phase >> s) & 1u);
+        phase ^= 1u << s;
+        if (tid == 0) pending &= ~(1u << s);
+      }
+      if (__syncthreads_or(!ok)) {
+        report_error(a.err, TGS_DEV_WAIT_TIMEOUT, t);
+        // Wait (bounded) for the copies still in flight before the shared
+        // memory they target is released.
+        if (tid == 0) {
+          for (int q = 0; q < kPackStages; ++q)
+            if (pending & (1u << q)) mbar_wait_bounded(&sm.bar[q], (phase >> q) & 1u);
+        }
+        __syncthreads();
+        return;
+      }
+      float* __restrict__ out = a.out + d.dst * kRowWidth;
+      const int n = d.rows * kRowWidth;
+      if (d.bulk) {
+        const float* __restrict__ tile = sm.stage[s];
+#pragma unroll 4
+        for (int e = tid; e < n; e += kPackThreads) {
+          const int r = e / kRowWidth;
+          const uint32_t cw = sm.col[e - r * kRowWidth];
+          out[e] = tile[(cw & 0xffffu) + r * (cw >> 16)];
+        }
+      } else {
+        for (int e = tid; e < n; e += kPackThreads) {
+          const int r = e / kRowWidth;
+          const int j = e - r * kRowWidth;
+          const int c = layout_comp_of(kLayout, j);
+          const int w = comp_width(c);
+          out[e] = pick6(a.comp.p, c)[(d.src + r) * w + (j - layout_offset(kLayout, c))];
+        }
       }
     }
-    // Make this thread's shared-memory writes visible to the bulk store.
+    // Every thread's reads of this stage precede the bulk copy that refills it.
     fence_proxy_async_smem();
     __syncthreads();
-    float* out = a.out + dst * kRowWidth;
-    const bool bulk = a.out_aligned && (dst & 3) == 0 && (rows & 3) == 0;
-    if (bulk) {
-      if (threadIdx.x == 0) {
-        bulk_s2g(out, tile, static_cast<uint32_t>(rows) * kRowWidth * sizeof(float));
-        bulk_commit();
-        bulk_wait_read<0>();
-      }
-    } else {
-      for (int e = threadIdx.x; e < rows * kRowWidth; e += kPackThreads) out[e] = tile[e];
-    }
-    __syncthreads();
+    if (tid == 0) issue(t + static_cast<int64_t>(kPackStages) * gridDim.x, s);
+    s = (s + 1 == kPackStages) ? 0 : s + 1;
   }
-  if (threadIdx.x == 0) bulk_wait_all();
 }
 
 // ---------------------------------------------------------------------------
@@ -719,22 +804,43 @@ extern "C" int tgs_pack_rows(const TgsPackArgs* a, void* stream) {
   if (a->n_plans == 0 || a->max_rows == 0) return TGS_OK;
   TGS_CHECK_ARG(a->src_start && a->row_count && a->out_start && a->out, "tgs_pack_rows: NULL plan");
   PackParams p;
+  p.comp_aligned = 1;
   for (int c = 0; c < kNumComp; ++c) {
     TGS_CHECK_ARG(a->comp[c] != nullptr, "tgs_pack_rows: component %d is NULL", c);
     p.comp.p[c] = a->comp[c];
+    if (!aligned16(a->comp[c])) p.comp_aligned = 0;
   }
   p.src_start = a->src_start;
   p.row_count = a->row_count;
   p.out_start = a->out_start;
-  p.n_plans = a->n_plans;
   p.out = a->out;
-  p.out_aligned = aligned16(a->out) ? 1 : 0;
+  p.err = a->err;
   const int64_t tiles = ceil_div<int64_t>(a->max_rows, kTileRows);
   TGS_CHECK_ARG(tiles < (1ll << 31), "tgs_pack_rows: max_rows too large");
-  dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(std::min(a->n_plans, 65535)));
+  p.tiles_per_plan = static_cast<int>(tiles);
+  p.n_tiles = tiles * a->n_plans;
+  const int grid = static_cast<int>(
+      std::min<int64_t>(p.n_tiles, static_cast<int64_t>(sm_count()) * kPackCtasPerSm));
+  static bool configured[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  TGS_CUDA(cudaGetDevice(&dev));
+  TGS_CHECK_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      TGS_CUDA(cudaFuncSetAttribute(pack_kernel<TGS_LAYOUT_CACHE>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmemBytes));
+      TGS_CUDA(cudaFuncSetAttribute(pack_kernel<TGS_LAYOUT_UNIFIED>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPackSmemBytes));
+      configured[dev] = true;
+    }
+  }
   cudaStream_t s = as_stream(stream);
-  if (a->layout == TGS_LAYOUT_CACHE) pack_kernel<TGS_LAYOUT_CACHE><<<grid, kPackThreads, 0, s>>>(p);
-  else pack_kernel<TGS_LAYOUT_UNIFIED><<<grid, kPackThreads, 0, s>>>(p);
+  if (a->layout == TGS_LAYOUT_CACHE)
+    pack_kernel<TGS_LAYOUT_CACHE><<<grid, kPackThreads, kPackSmemBytes, s>>>(p);
+  else
+    pack_kernel<TGS_LAYOUT_UNIFIED><<<grid, kPackThreads, kPackSmemBytes, s>>>(p);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

@@ -4,7 +4,7 @@ PendingBlockWriteback :132-184, GPUWorkingSet :187-1119).
 
 Device work goes through libtidegs_b200.so:
 * stage_updated_blocks (:895-988): SoA -> packed CACHE rows in one launch of
-  `tgs_pack_rows` (AoS tile assembled in shared memory, TMA bulk store), then
+  `tgs_pack_rows` (component ranges staged in shared memory by bulk copies), then
   one D2H into rotating pinned staging on the write-back stream.
 * stage_block_bounds (:990-1061): `tgs_block_bounds`, exact min/max per block.
 * load_visible_blocks_with_retention (:447-793): retained blocks move with the

@@ -745,10 +745,10 @@ class ApiStep:
             step_ev.record()
             db.prefetch_events = {}
         evict_pos, incoming_arr, _ = self.trace.turn[k]
-        loaded = [int(b) for b in sched.slot_block]
-        evicted = sorted(int(b) for b in sched.slot_block[evict_pos])
-        incoming = [int(b) for b in incoming_arr]
-        keep = sorted(set(loaded) - set(evicted))
+        evicted_arr = np.sort(sched.slot_block[evict_pos])
+        evicted = evicted_arr.tolist()
+        incoming = incoming_arr.tolist()
+        keep = np.setdiff1d(sched.slot_block, evicted_arr, assume_unique=True).tolist()
         t = self._mark("plan", t)
         db.start_prefetch(iteration=k + 1, visible_block_ids=keep + incoming,
                           resident_block_ids=keep, evicted_block_ids=evicted,

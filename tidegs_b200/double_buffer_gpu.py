@@ -302,19 +302,19 @@ class DoubleBufferGPUWorkingSet:
         if (not allow_resident_copy or not defer_resident_copy or source.is_empty()
                 or not current_blocks or len(next_blocks) != len(current_blocks)):
             return None
-        current_set = set(int(b) for b in current_blocks)
-        next_set = set(int(b) for b in next_blocks)
+        current_set = set(map(int, current_blocks))
+        next_set = set(map(int, next_blocks))
         keep_set = current_set & next_set
         incoming = sorted(next_set - current_set)
         evicted = current_set - next_set
-        if (keep_set != set(int(b) for b in resident_set)
-                or evicted != set(int(b) for b in evicted_set)
+        if (keep_set != set(map(int, resident_set))
+                or evicted != set(map(int, evicted_set))
                 or len(incoming) != len(evicted)):
             return None
-        for block_id in current_blocks:
-            sl = source.block_to_local_slice.get(int(block_id))
-            if sl is None or int(sl.stop - sl.start) != self.block_size:
-                return None
+        slices = source.block_to_local_slice
+        if not current_set.issubset(slices.keys()) or any(
+                slices[b].stop - slices[b].start != self.block_size for b in current_set):
+            return None
         for block_id in incoming:
             if min(self.block_size, self.num_total - int(block_id) * self.block_size) != self.block_size:
                 return None
@@ -347,6 +347,7 @@ class DoubleBufferGPUWorkingSet:
         plan["next_order"] = [b for b, _ in sorted(next_slices.items(),
                                                    key=lambda it: int(it[1].start))]
         plan["keep_blocks"] = sorted(keep_set)
+        plan["block_starts"] = _build_block_starts(next_slices, self.num_blocks, self.device)
 
     @property
     def loaded_blocks(self) -> List[int]:
@@ -375,8 +376,7 @@ class DoubleBufferGPUWorkingSet:
             target.streamed_blocks = list(incoming_blocks)
             target.evicted_blocks = list(persistent_plan["evicted_blocks"])
             target.num_gaussians = int(target.xyz.shape[0])
-            target._block_starts = _build_block_starts(target.block_to_local_slice,
-                                                       self.num_blocks, self.device)
+            target._block_starts = persistent_plan["block_starts"]
             # the slot copy above reads the staging buffer on this stream
             self._retire(source, torch.cuda.current_stream(self.device))
             source.clear()
@@ -771,9 +771,9 @@ class DoubleBufferGPUWorkingSet:
             self._before_persistent_apply = None
 
         if block_reader is not None:
-            sorted_visible = sorted(set(int(b) for b in visible_block_ids))
-            resident_set = set(int(b) for b in (resident_block_ids or []))
-            evicted_set = set(int(b) for b in (evicted_block_ids or []))
+            sorted_visible = sorted(set(map(int, visible_block_ids)))
+            resident_set = set(map(int, resident_block_ids or []))
+            evicted_set = set(map(int, evicted_block_ids or []))
             plan = self._build_persistent_plan(sorted_visible, resident_set, evicted_set,
                                                allow_resident_copy=allow_resident_copy,
                                                defer_resident_copy=defer_resident_copy)
@@ -806,6 +806,8 @@ class DoubleBufferGPUWorkingSet:
                 future = Future()
                 try:
                     self._run_block_reader_prefetch(**job)
+                    # the slot map of the next step, built while the DMA runs
+                    self._persistent_plan_layout(plan)
                     future.set_result(None)
                 except BaseException as exc:  # surfaced by wait_for_prefetch
                     future.set_exception(exc)

@@ -573,6 +573,27 @@ class _Skipped(Exception):
 # ---------------------------------------------------------------------------
 # e2e leg: Python drop-in classes, host pool -> HBM -> host
 # ---------------------------------------------------------------------------
+class _SceneStore:
+    """Block store behind the e2e host tier: block b's rows are
+    distinct[b % len(distinct)]; write_patch (the disk tier, not measured)
+    only counts. Once sealed, a read means the host tier missed."""
+
+    def __init__(self, distinct: torch.Tensor):
+        self.distinct = distinct
+        self.sealed = False
+        self.patches = 0
+
+    def read_blocks(self, block_ids):
+        if self.sealed:
+            raise RuntimeError(f"host tier miss for blocks {list(block_ids)[:8]}")
+        n = self.distinct.shape[0]
+        return {int(b): self.distinct[int(b) % n] for b in block_ids}
+
+    def write_patch(self, blocks):
+        self.patches += 1
+        return self.patches
+
+
 class ApiStep:
     """The step through the Python drop-ins. Slice position i of the active
     buffer holds sched.slot_block[i]; the persistent-slot plan gives incoming
@@ -590,11 +611,12 @@ class ApiStep:
         return t
 
     def __init__(self, device, scheds, trace: ScheduleTrace, rank: int, world: int,
-                 pool_blocks: int, exchange: str = "pull"):
+                 pool_blocks: int, exchange: str = "pull", host_tier: str = "cache"):
         import types
 
-        from tidegs_b200 import (BlockLayout, DoubleBufferGPUWorkingSet, GPUResidentAdam,
-                                 GPUWorkingSet, PinnedBlockPool, _ops)
+        from tidegs_b200 import (BlockLayout, CachedBlockReader, DoubleBufferGPUWorkingSet,
+                                 GPUResidentAdam, GPUWorkingSet, PinnedBlockCache,
+                                 PinnedBlockPool, _ops)
 
         self.device = device
         self.scheds = scheds
@@ -603,10 +625,27 @@ class ApiStep:
         self.rank, self.world = rank, world
         num_total = int(max(int(o.pool_ids.max()) for o in scheds) + 1) * B
         gen = torch.Generator().manual_seed(99 + rank)
-        data = torch.empty((pool_blocks, B, 59), pin_memory=True)
-        for i in range(pool_blocks):
-            data[i].normal_(0.0, 1.0, generator=gen)
-        self.pool = PinnedBlockPool(data, B, num_total, layout=BlockLayout.CACHE)
+        self.cache = None
+        if host_tier == "cache":
+            # the host tier holds every scene block of this rank (4 x SLOTS
+            # blocks, BASELINE configs[3]'s pinned pool): pool_blocks distinct
+            # seeded blocks, block b holding distinct[b % pool_blocks], read
+            # into the cache's page-locked slab through its prefetch; room
+            # for one write-back batch of fresh entries on top
+            distinct = torch.empty((pool_blocks, B, 59))
+            for i in range(pool_blocks):
+                distinct[i].normal_(0.0, 1.0, generator=gen)
+            store = _SceneStore(distinct)
+            self.cache = PinnedBlockCache(store, max_ram_gb=1e9, block_size=B, verbose=False,
+                                          capacity_blocks=sched.pool_ids.size + TURNOVER)
+            self.cache.prefetch(sched.pool_ids.tolist())
+            store.sealed = True  # a host-tier miss inside the steps is an error
+            self.pool = CachedBlockReader(self.cache, num_total, B)
+        else:
+            data = torch.empty((pool_blocks, B, 59), pin_memory=True)
+            for i in range(pool_blocks):
+                data[i].normal_(0.0, 1.0, generator=gen)
+            self.pool = PinnedBlockPool(data, B, num_total, layout=BlockLayout.CACHE)
         self.db = DoubleBufferGPUWorkingSet(num_total, B, device=device, verbose=False)
         self.ws = GPUWorkingSet(num_total, B, device=device)
         self.opt = GPUResidentAdam(batch_size=16, block_size=B, capacity_blocks=SLOTS,
@@ -658,9 +697,12 @@ class ApiStep:
                 self.recv_buf = torch.empty((recv_max * B, 59), device=device)
         # page-lock the write-back staging once, at its largest size (every
         # evicted block dirty), instead of growing it inside timed steps
-        for _ in range(2):
-            _, _, ready = self.ws._acquire_writeback_staging(TURNOVER * B)
-            ready.set()
+        if self.cache is None:
+            for _ in range(2):
+                _, _, ready = self.ws._acquire_writeback_staging(TURNOVER * B)
+                ready.set()
+        else:
+            self.ws.ensure_direct_writeback_capacity(TURNOVER * B)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         torch.cuda.synchronize()
@@ -716,12 +758,15 @@ class ApiStep:
         return self._upload_ids(ids_host), grads
 
     def close(self):
-        """Releases the peer mappings (collective over the ranks)."""
+        """Releases the peer mappings (collective over the ranks) and stops
+        the host tier's workers."""
         for attr in ("peer", "pull"):
             obj = getattr(self, attr)
             if obj is not None:
                 obj.close()
                 setattr(self, attr, None)
+        if self.cache is not None:
+            self.cache.shutdown()
 
     def _upload_ids(self, ids_host: torch.Tensor) -> torch.Tensor:
         """Row ids from page-locked memory, read by a kernel (not queued
@@ -774,7 +819,7 @@ class ApiStep:
         t = self._mark("dirty_mark_bounds", t)
         wb_ids = db.dirty_blocks_for_eviction(evicted)
         t = self._mark("dirty_select", t)
-        pending = ws.stage_updated_blocks(wb_ids)
+        pending = ws.stage_updated_blocks(wb_ids, host_cache=self.cache)
         t = self._mark("stage_writeback", t)
         if pending is not None:
             payload = pending.wait()
@@ -1016,7 +1061,11 @@ def main(argv=None):
     ap.add_argument("--e2e-warmup", type=int, default=6)
     ap.add_argument("--e2e-profile", action="store_true",
                     help="print a per-phase wall-time breakdown of the e2e step to stderr")
-    ap.add_argument("--pool-blocks", type=int, default=1024)
+    ap.add_argument("--pool-blocks", type=int, default=1024,
+                    help="distinct seeded host blocks (scene block b holds block b mod this)")
+    ap.add_argument("--host-tier", default="cache", choices=["cache", "pool"],
+                    help="e2e host side: PinnedBlockCache over every scene block of the rank "
+                         "(write-back lands in it), or the fixed modulo PinnedBlockPool")
     ap.add_argument("--slots", type=int, default=SLOTS,
                     help="resident slots per GPU (default: the configs[3] value; smaller "
                          "values make small profiling cases of the same step)")
@@ -1105,7 +1154,7 @@ def main(argv=None):
         if args.no_e2e:
             raise _Skipped("--no-e2e")
         api = ApiStep(device, [Schedule(o, world) for o in range(world)], trace, rank, world,
-                      args.pool_blocks, exchange=args.exchange)
+                      args.pool_blocks, exchange=args.exchange, host_tier=args.host_tier)
         for k in range(args.e2e_warmup):
             api.step(k)
         torch.cuda.synchronize()
@@ -1125,7 +1174,11 @@ def main(argv=None):
                "h2d_bytes_per_step": int(api.h2d_bytes / args.e2e_steps),
                "d2h_bytes_per_step": int(api.d2h_bytes / args.e2e_steps),
                "ms_per_step": e_ms / args.e2e_steps, "steps": args.e2e_steps,
-               "host_pool_blocks": args.pool_blocks}
+               "host_pool_blocks": args.pool_blocks,
+               "host_tier": (f"PinnedBlockCache of the rank's {4 * SLOTS} scene blocks "
+                             f"(+{TURNOVER} write-back entries); write-back DMA into it"
+                             if args.host_tier == "cache" else
+                             f"PinnedBlockPool of {args.pool_blocks} blocks (block id mod pool)")}
         if api.profile is not None and rank == 0:
             print("e2e phase wall ms/step: " + json.dumps(
                 {k: round(v * 1e3 / args.e2e_steps, 2) for k, v in api.profile.items()})

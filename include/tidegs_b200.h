@@ -314,6 +314,14 @@ TGS_API int tgs_copy_small(void* dst, const void* src, int64_t bytes, void* stre
 TGS_API int tgs_h2d_blocks(void* const* dev_dst, const void* const* host_src,
                    const int64_t* bytes, int32_t n, void* stream);
 
+/* Issues one cudaMemcpyAsync per block (device -> host): the write-back
+ * payload lands in page-locked host-cache entries, host_dst[k] <- dev_src[k].
+ * Replaces the pinned staging copy of gpu_working_set.py:960-967 followed by
+ * the CPU copy into the cache's slab in
+ * storage/tiered_cache_manager.py:524-599 (upsert_dirty_block_batch). */
+TGS_API int tgs_d2h_blocks(void* const* host_dst, const void* const* dev_src,
+                   const int64_t* bytes, int32_t n, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Dirty tracking and write-back                                             */
 /* ------------------------------------------------------------------------ */

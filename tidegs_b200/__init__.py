@@ -7,17 +7,23 @@ Drop-in classes (same names and behaviour as the reference's):
     DoubleBufferGPUWorkingSet, GPUBuffer strategies/tide_engine/double_buffer_gpu.py
     GPUWorkingSet, PendingBlockWriteback strategies/tide_engine/gpu_working_set.py
     SparseGradAccumulator                strategies/tide_engine/engine.py:1793-1826, 2434-2471
+    PinnedBlockCache, BlockLogStore,     storage/tiered_cache_manager.py,
+    CachedBlockReader                    storage/log_storage_manager.py, storage/block_reader.py
 plus SelectiveSophia (no reference counterpart) and PinnedBlockPool.
 
-All compute runs in libtidegs_b200.so (include/tidegs_b200.h); importing the
-package does not touch the GPU, constructing any class requires CUDA and the
-built library.
+All device work runs in libtidegs_b200.so (include/tidegs_b200.h); importing
+the package does not touch the GPU, and constructing any class that owns
+device memory requires CUDA and the built library. The host-tier classes are
+host code (page-locked memory when CUDA is present) whose device transfers
+are issued by GPUWorkingSet and DoubleBufferGPUWorkingSet.
 """
 from .block_reader import (BlockBatch, BlockLayout, BlockReader, PinnedBlockPool,
                            UnifiedParamsBlockReader, parse_block_row_components)
 from .double_buffer_gpu import DoubleBufferGPUWorkingSet, GPUBuffer, ResidentHandoffResult
 from .gpu_resident_optimizer import GPUResidentAdam
-from .gpu_working_set import GPUWorkingSet, PendingBlockBounds, PendingBlockWriteback
+from .gpu_working_set import (GPUWorkingSet, PendingBlockBounds, PendingBlockWriteback,
+                              PendingCacheWriteback)
+from .host_tier import BlockLogStore, CachedBlockReader, PinnedBlockCache
 from .optimizer import ResidentAdamContext, SelectiveAdam, SelectiveSophia
 from .sparse_grad import SparseGradAccumulator
 
@@ -26,5 +32,6 @@ __all__ = [
     "parse_block_row_components", "DoubleBufferGPUWorkingSet", "GPUBuffer",
     "ResidentHandoffResult", "GPUResidentAdam", "GPUWorkingSet", "PendingBlockBounds",
     "PendingBlockWriteback", "ResidentAdamContext", "SelectiveAdam", "SelectiveSophia",
-    "SparseGradAccumulator",
+    "SparseGradAccumulator", "PendingCacheWriteback", "BlockLogStore", "CachedBlockReader",
+    "PinnedBlockCache",
 ]

@@ -156,6 +156,7 @@ SIGNATURES = {
     "tgs_global_to_local_compact": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp]),
     "tgs_global_to_local_compact_noalloc": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "tgs_h2d_blocks": (C.c_int, [C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_i64), _i32, _vp]),
+    "tgs_d2h_blocks": (C.c_int, [C.POINTER(_vp), C.POINTER(_vp), C.POINTER(_i64), _i32, _vp]),
     "tgs_dirty_mark": (C.c_int, [_vp, _i64, _vp, _i64, _i32, _vp]),
     "tgs_dirty_select": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp]),
     "tgs_dirty_list": (C.c_int, [_vp, _i64, _vp, _vp, _vp]),

@@ -321,3 +321,16 @@ def h2d_blocks(dst_ptrs: Sequence[int], src_ptrs: Sequence[int], nbytes: Sequenc
     src = (C.c_void_p * n)(*src_ptrs)
     sizes = (C.c_int64 * n)(*nbytes)
     _lib.call("tgs_h2d_blocks", dst, src, sizes, n, _stream(device))
+
+
+def d2h_blocks(dst_ptrs: Sequence[int], src_ptrs: Sequence[int], nbytes: Sequence[int],
+               device: torch.device) -> None:
+    """One device-to-host DMA per block on the current stream."""
+    import ctypes as C
+    n = len(nbytes)
+    if n == 0:
+        return
+    dst = (C.c_void_p * n)(*dst_ptrs)
+    src = (C.c_void_p * n)(*src_ptrs)
+    sizes = (C.c_int64 * n)(*nbytes)
+    _lib.call("tgs_d2h_blocks", dst, src, sizes, n, _stream(device))

@@ -104,3 +104,18 @@ extern "C" int tgs_h2d_blocks(void* const* dev_dst, const void* const* host_src,
   }
   return TGS_OK;
 }
+
+extern "C" int tgs_d2h_blocks(void* const* host_dst, const void* const* dev_src,
+                              const int64_t* bytes, int32_t n, void* stream) {
+  TGS_CHECK_ARG(n >= 0, "tgs_d2h_blocks: n=%d < 0", n);
+  if (n == 0) return TGS_OK;
+  TGS_CHECK_ARG(host_dst && dev_src && bytes, "tgs_d2h_blocks: null array");
+  cudaStream_t s = tgs::as_stream(stream);
+  for (int32_t k = 0; k < n; ++k) {
+    TGS_CHECK_ARG(bytes[k] >= 0, "tgs_d2h_blocks: bytes[%d]=%lld < 0", k, (long long)bytes[k]);
+    if (bytes[k] == 0) continue;
+    TGS_CUDA(cudaMemcpyAsync(host_dst[k], dev_src[k], static_cast<size_t>(bytes[k]),
+                             cudaMemcpyDeviceToHost, s));
+  }
+  return TGS_OK;
+}

@@ -609,6 +609,12 @@ class DoubleBufferGPUWorkingSet:
                                          block_ids=ids_all[c0:c1], block_size=self.block_size,
                                          err=self._err)
                 self._mark_prefetch("h2d_end")
+                note_reads = getattr(block_reader, "note_dma_reads", None)
+                if callable(note_reads):
+                    # the reader's entries are not rewritten before the DMAs ran
+                    read_done = torch.cuda.Event()
+                    read_done.record(dma_stream)
+                    note_reads(streamed_blocks, read_done)
                 dma_stream.wait_stream(self._unpack_stream)
                 ids_all.record_stream(self._unpack_stream)
                 packed_gpu.record_stream(self._unpack_stream)

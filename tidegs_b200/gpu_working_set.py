@@ -90,6 +90,31 @@ class PendingBlockWriteback:
             self.release_event.set()
 
 
+class PendingCacheWriteback(PendingBlockWriteback):
+    """A write-back whose per-block DMAs land in fresh entries of a host block
+    cache: `wait()` publishes them there (each block dirty, version + 1) and
+    returns {block: entry view}. There is no staging copy, so `packed_cpu`
+    is None."""
+
+    def __init__(self, plans, ready_event, host_cache, views, gpu_refs=None):
+        super().__init__(plans, None, ready_event, gpu_refs=gpu_refs)
+        self.host_cache = host_cache
+        self._views = list(views)
+
+    def wait(self) -> Dict[int, torch.Tensor]:
+        if self._result is not None:
+            return self._result
+        with self._wait_lock:
+            if self._result is None:
+                self.wait_gpu()
+                self.host_cache.commit_writeback(self.plans, self._views)
+                self._result = {b: v for (b, _), v in zip(self.plans, self._views)}
+        return self._result
+
+    def release(self) -> None:
+        self.wait()
+
+
 class GPUWorkingSet:
     """GPU working set of the resident blocks (59 fp32 columns per Gaussian,
     stored as six contiguous component tensors)."""
@@ -138,7 +163,9 @@ class GPUWorkingSet:
             "pinned_staging_bytes": 0,
             "pinned_staging": False,
             "bounds_updates": 0,
+            "direct_cache_d2h_blocks": 0,
         }
+        self._direct_staging: Optional[torch.Tensor] = None
         self._log(f"[GPUWorkingSet] Initialized for {self.num_total:,} Gaussians")
 
     def _log(self, message: str) -> None:
@@ -449,8 +476,11 @@ class GPUWorkingSet:
             s.is_pinned() for s in self._writeback_staging_slots if s is not None)
         return staging, gpu_staging, available
 
-    def stage_updated_blocks(self, updated_block_ids: List[int]) -> Optional[PendingBlockWriteback]:
-        """Pack updated blocks and enqueue one batched D2H copy."""
+    def stage_updated_blocks(self, updated_block_ids: List[int],
+                             host_cache=None) -> Optional[PendingBlockWriteback]:
+        """Pack updated blocks and enqueue one batched D2H copy. With a
+        `host_cache` (PinnedBlockCache) each block's rows go by DMA straight
+        into a fresh cache entry instead (PendingCacheWriteback)."""
         sources = self._components()
         if not updated_block_ids or any(t is None for t in sources.values()):
             return None
@@ -468,6 +498,8 @@ class GPUWorkingSet:
             src_starts.append(int(local_slice.start))
         if not plans:
             return None
+        if host_cache is not None:
+            return self._stage_into_cache(plans, src_starts, sources, host_cache)
         total_rows = sum(r for _, r in plans)
         staging, gpu_staging, release_event = self._acquire_writeback_staging(total_rows)
         pinned = bool(self.writeback_stats["pinned_staging"])
@@ -488,6 +520,49 @@ class GPUWorkingSet:
         self.writeback_stats["batched_writeback_rows"] += total_rows
         self.writeback_stats["async_d2h_calls"] += 1
         return PendingBlockWriteback(plans, packed_cpu, ready_event, release_event=release_event,
+                                     gpu_refs=[packed_gpu, *refs])
+
+    def ensure_direct_writeback_capacity(self, rows: int) -> torch.Tensor:
+        """Device staging of the direct (host-cache) write-back, grown
+        geometrically and allocated on the write-back stream, so that a
+        regrown buffer is not handed out again before the DMAs reading the
+        old one ran; call it once with the largest batch to keep device
+        allocations out of the steps."""
+        cur = self._direct_staging
+        if cur is None or cur.shape[0] < rows:
+            capacity = max(int(rows), 2 * (0 if cur is None else int(cur.shape[0])))
+            with torch.cuda.stream(self._writeback_stream):
+                self._direct_staging = torch.empty((capacity, 59), dtype=torch.float32,
+                                                   device=self.device)
+        return self._direct_staging
+
+    def _stage_into_cache(self, plans, src_starts, sources, host_cache) -> PendingCacheWriteback:
+        total_rows = sum(r for _, r in plans)
+        views = host_cache.reserve_writeback(plans)
+        ready_event = torch.cuda.Event()
+        current = torch.cuda.current_stream(self.device)
+        row_bytes = 59 * 4
+        try:
+            with torch.cuda.stream(self._writeback_stream):
+                self._writeback_stream.wait_stream(current)
+                packed_gpu = self.ensure_direct_writeback_capacity(total_rows)[:total_rows]
+                counts = [r for _, r in plans]
+                refs = _ops.pack_rows(sources, src_starts, counts, packed_gpu, _lib.LAYOUT_CACHE)
+                offsets = np.concatenate([[0], np.cumsum(counts[:-1])]).astype(np.int64)
+                src = (packed_gpu.data_ptr() + offsets * row_bytes).tolist()
+                _ops.d2h_blocks([v.data_ptr() for v in views], src,
+                                [r * row_bytes for r in counts], self.device)
+                ready_event.record(self._writeback_stream)
+        except BaseException:
+            host_cache.abort_writeback(views)
+            raise
+        for t in sources.values():
+            t.record_stream(self._writeback_stream)
+        self.writeback_stats["batched_writebacks"] += 1
+        self.writeback_stats["batched_writeback_blocks"] += len(plans)
+        self.writeback_stats["batched_writeback_rows"] += total_rows
+        self.writeback_stats["direct_cache_d2h_blocks"] += len(plans)
+        return PendingCacheWriteback(plans, ready_event, host_cache, views,
                                      gpu_refs=[packed_gpu, *refs])
 
     def stage_block_bounds(self, block_ids: List[int]) -> Optional[PendingBlockBounds]:

@@ -896,6 +896,90 @@ def pull_probe(args, modes):
 # ---------------------------------------------------------------------------
 # Diagnostic: touched-only gradient accumulation of a camera batch
 # ---------------------------------------------------------------------------
+def _look_at(eye, target, up=(0.0, 0.0, 1.0)) -> np.ndarray:
+    """OpenGL view matrix (camera looks down -Z)."""
+    eye, target, up = (np.asarray(v, dtype=np.float64) for v in (eye, target, up))
+    f = (target - eye) / np.linalg.norm(target - eye)
+    s = np.cross(f, up)
+    s /= np.linalg.norm(s)
+    m = np.eye(4)
+    m[0, :3], m[1, :3], m[2, :3] = s, np.cross(s, f), -f
+    m[:3, 3] = -m[:3, :3] @ eye
+    return m
+
+
+def _perspective(fovy_deg: float, aspect: float, near: float, far: float) -> np.ndarray:
+    t = 1.0 / np.tan(np.radians(fovy_deg) / 2.0)
+    m = np.zeros((4, 4))
+    m[0, 0], m[1, 1] = t / aspect, t
+    m[2, 2], m[2, 3] = (far + near) / (near - far), 2.0 * far * near / (near - far)
+    m[3, 2] = -1.0
+    return m
+
+
+def cull_probe(args):
+    """Not the bench line. Frustum culling of a configs[4]-sized scene
+    (61,036 block spheres, blocks of 16,384 Gaussians in a 200^3 box) for a
+    16-camera batch: BlockCuller (one launch; device time with CUDA events,
+    and with the per-camera id lists read back to Python lists) against the
+    reference's per-camera numpy evaluation (oracle/culling.py, the same
+    numpy operations) on the host; checks the visible sets are equal."""
+    import warnings
+
+    from oracle import culling as oc
+    from tidegs_b200 import BlockCuller
+
+    warnings.filterwarnings("ignore", message="Suspicious plane orientations")
+    torch.cuda.set_device(0)
+    rng = np.random.default_rng(11)
+    n = 61036
+    centers = rng.uniform(-100.0, 100.0, (n, 3))
+    half = rng.uniform(1.0, 6.0, (n, 3))
+    bounds = np.concatenate([centers - half, centers + half], axis=1).astype(np.float32)
+    cams = []
+    for _ in range(16):
+        ang = rng.uniform(0, 2 * np.pi)
+        eye = np.array([110 * np.cos(ang), 110 * np.sin(ang), rng.uniform(10, 60)])
+        cams.append((_look_at(eye, rng.uniform(-60, 60, 3)),
+                     _perspective(rng.uniform(25, 45), 16 / 9, 0.5, 260.0)))
+    from tidegs_b200.culling import extract_frustum_planes
+
+    cu = BlockCuller(torch.from_numpy(bounds).cuda(), verbose=False)
+    planes_ms, dev_ms, list_ms = [], [], []
+    for k in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        planes = np.stack([extract_frustum_planes(v, p) for v, p in cams])
+        t1 = time.perf_counter()
+        cu.cull_cameras(None, planes=planes, as_tensors=True)  # uploads stay out of the timing
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ids, counts = cu.cull_cameras(None, planes=planes, as_tensors=True)
+        e1.record()
+        torch.cuda.synchronize()
+        t2 = time.perf_counter()
+        lists = cu.cull_cameras(cams)
+        t3 = time.perf_counter()
+        if k >= args.warmup:
+            planes_ms.append((t1 - t0) * 1e3)
+            dev_ms.append(e0.elapsed_time(e1))
+            list_ms.append((t3 - t2) * 1e3)
+    c_np, r_np = oc.spheres(bounds)
+    t0 = time.perf_counter()
+    want = [oc.visible(c_np, r_np, oc.planes(v, p)).tolist() for v, p in cams]
+    cpu_ms = (time.perf_counter() - t0) * 1e3
+    if want != lists:
+        raise RuntimeError("cull-probe: visible sets differ from the oracle")
+    vis = sum(len(x) for x in want)
+    print(json.dumps({"probe": "frustum_cull", "blocks": n, "cameras": 16,
+                      "visible_fraction": round(vis / (16 * n), 3),
+                      "host_planes_ms": round(statistics.median(planes_ms), 3),
+                      "gpu_launch_ms": round(statistics.median(dev_ms), 4),
+                      "gpu_with_python_lists_ms": round(statistics.median(list_ms), 3),
+                      "reference_numpy_ms": round(cpu_ms, 2), "equal": True}), flush=True)
+
+
 def accum_probe(args):
     """Not the bench line. A camera batch of the configs[3] shape (16 cameras,
     each seeing a contiguous run of 24-56 resident blocks of 16,384 rows out
@@ -1077,6 +1161,8 @@ def main(argv=None):
     ap.add_argument("--pull-probe", default=None, metavar="MODES",
                     help="diagnostic instead of the bench: comma list of remote,local,plain "
                          "(needs two GPUs for remote)")
+    ap.add_argument("--cull-probe", action="store_true",
+                    help="diagnostic: frustum culling of a 61,036-block scene, 16 cameras")
     ap.add_argument("--accum-probe", action="store_true",
                     help="diagnostic instead of the bench: touched-only gradient accumulation "
                          "of a camera batch against the reference's torch operations")
@@ -1094,6 +1180,8 @@ def main(argv=None):
         return pull_probe(args, args.pull_probe.split(","))
     if args.accum_probe:
         return accum_probe(args)
+    if args.cull_probe:
+        return cull_probe(args)
 
     from tidegs_b200 import _lib
 

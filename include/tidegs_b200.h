@@ -540,6 +540,46 @@ typedef struct {
 
 TGS_API int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* args, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Block frustum culling                                                     */
+/* Replaces: storage/gaussian_block.py                                       */
+/*   :264-312  FrustumCuller bounding spheres (center, radius * 1.15)        */
+/*   :318-340  update_block_bounds                                           */
+/*   :359-406  cull_subset, :408-465 cull (6-plane test); the planes        */
+/*             (:145-228) are extracted on the host                          */
+/* ------------------------------------------------------------------------ */
+
+/* centers[b] = (min+max)/2 and radii[b] = |max-min|/2 * 1.15f from
+ * bounds[b] = (min x, min y, min z, max x, max y, max z), in float32 with
+ * every operation rounded once, sums left to right (the reference's numpy
+ * evaluation). */
+TGS_API int tgs_block_spheres(const float* bounds, int64_t n_blocks, float* centers,
+                      float* radii, void* stream);
+
+typedef struct {
+  const float* centers;   /* [n_blocks, 3] device */
+  const float* radii;     /* [n_blocks] device */
+  int64_t n_blocks;
+  const int64_t* subset;  /* [n_items] candidate block ids (device), or NULL = all blocks */
+  int64_t n_items;
+  const float* planes;    /* [n_cameras, 6, 4] normalized planes (device) */
+  int32_t n_cameras;      /* 0 .. 65535 */
+  int64_t* out_ids;       /* [n_cameras, out_stride] visible ids, in candidate order */
+  int64_t out_stride;     /* >= n_items */
+  int64_t* out_counts;    /* [n_cameras] visible blocks per camera */
+  int64_t* slice_counts;  /* [n_cameras * tgs_frustum_cull_slices(n_items)] device scratch */
+  int32_t* err;           /* [4] TGS_DEV_ID_OUT_OF_RANGE for a subset id (skipped) */
+} TgsCullArgs;
+
+/* Slices of 4096 candidates each camera's candidates are split into (the
+ * scratch size per camera of tgs_frustum_cull). */
+TGS_API int64_t tgs_frustum_cull_slices(int64_t n_items);
+
+/* For every camera, the candidates whose sphere has signed distance >= -radius
+ * to all six planes (gaussian_block.py:429-465): a counting pass and an
+ * ordered writing pass, each a grid of (slice, camera) CTAs. */
+TGS_API int tgs_frustum_cull(const TgsCullArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

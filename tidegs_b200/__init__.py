@@ -9,6 +9,7 @@ Drop-in classes (same names and behaviour as the reference's):
     SparseGradAccumulator                strategies/tide_engine/engine.py:1793-1826, 2434-2471
     PinnedBlockCache, BlockLogStore,     storage/tiered_cache_manager.py,
     CachedBlockReader                    storage/log_storage_manager.py, storage/block_reader.py
+    BlockCuller                          storage/gaussian_block.py (FrustumCuller)
 plus SelectiveSophia (no reference counterpart) and PinnedBlockPool.
 
 All device work runs in libtidegs_b200.so (include/tidegs_b200.h); importing
@@ -17,6 +18,7 @@ device memory requires CUDA and the built library. The host-tier classes are
 host code (page-locked memory when CUDA is present) whose device transfers
 are issued by GPUWorkingSet and DoubleBufferGPUWorkingSet.
 """
+from .culling import BlockCuller
 from .block_reader import (BlockBatch, BlockLayout, BlockReader, PinnedBlockPool,
                            UnifiedParamsBlockReader, parse_block_row_components)
 from .double_buffer_gpu import DoubleBufferGPUWorkingSet, GPUBuffer, ResidentHandoffResult
@@ -33,5 +35,5 @@ __all__ = [
     "ResidentHandoffResult", "GPUResidentAdam", "GPUWorkingSet", "PendingBlockBounds",
     "PendingBlockWriteback", "ResidentAdamContext", "SelectiveAdam", "SelectiveSophia",
     "SparseGradAccumulator", "PendingCacheWriteback", "BlockLogStore", "CachedBlockReader",
-    "PinnedBlockCache",
+    "PinnedBlockCache", "BlockCuller",
 ]

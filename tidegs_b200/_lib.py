@@ -139,6 +139,14 @@ class SparseAccumArgs(C.Structure):
     ]
 
 
+class CullArgs(C.Structure):
+    _fields_ = [
+        ("centers", _vp), ("radii", _vp), ("n_blocks", _i64), ("subset", _vp), ("n_items", _i64),
+        ("planes", _vp), ("n_cameras", _i32), ("out_ids", _vp), ("out_stride", _i64),
+        ("out_counts", _vp), ("slice_counts", _vp), ("err", _vp),
+    ]
+
+
 # name -> (restype, argtypes). Keep in sync with include/tidegs_b200.h.
 SIGNATURES = {
     "tgs_version": (C.c_int, []),
@@ -177,6 +185,9 @@ SIGNATURES = {
     "tgs_bitmap_list": (C.c_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp]),
     "tgs_gather_i64": (C.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _vp]),
     "tgs_sparse_grad_accumulate": (C.c_int, [C.POINTER(SparseAccumArgs), _vp]),
+    "tgs_block_spheres": (C.c_int, [_vp, _i64, _vp, _vp, _vp]),
+    "tgs_frustum_cull": (C.c_int, [C.POINTER(CullArgs), _vp]),
+    "tgs_frustum_cull_slices": (_i64, [_i64]),
 }
 
 _lock = threading.Lock()
@@ -225,7 +236,7 @@ KERNELS_PER_CALL = {
     "tgs_dirty_mark": 1, "tgs_dirty_select": 1, "tgs_dirty_list": 1, "tgs_pack_rows": 1,
     "tgs_block_bounds": 1, "tgs_block_grad_sum": 1, "tgs_copy_small": 1, "tgs_grad_push": 1,
     "tgs_resident_adam_apply_sum": 1, "tgs_bitmap_list": 3, "tgs_gather_i64": 1, "tgs_bitmap_set": 1,
-    "tgs_sparse_grad_accumulate": 1,
+    "tgs_sparse_grad_accumulate": 1, "tgs_block_spheres": 1, "tgs_frustum_cull": 2,
 }
 launch_counter = {"kernels": 0}
 

@@ -1,0 +1,62 @@
+"""CPU: the vectorized resident-set planner (tidegs_b200/resident_policy.py)
+against the reference planner's transitions recorded in
+tests/golden/planner.json (7 policy/capacity/seed-fraction cases x 30 steps,
+recency scores and resident sets fed back between steps): every field of
+every transition equal (per-field digests of the canonical JSON), with the
+recency scores passed as the reference's dict and as RecencyScores."""
+import json
+import sys
+from pathlib import Path
+
+import pytest
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE / "golden"))
+import make_planner_golden as G  # noqa: E402
+
+from tidegs_b200 import resident_policy as rp  # noqa: E402
+
+FIX = json.loads((HERE / "golden" / "planner.json").read_text())
+
+
+def _replay(case, dense: bool):
+    sched = G.camera_schedule(case["seed"], case["steps"] + 1)
+    recency = rp.RecencyScores() if dense else {}
+    resident = None
+    for k in range(case["steps"]):
+        cur, nxt = G.union(sched[k]), G.union(sched[k + 1])
+        given = resident if (resident is None or k % 7 != 3) else resident[: len(resident) // 2]
+        kw = dict(current_active_blocks=cur, next_active_blocks=nxt,
+                  current_resident_blocks=given, next_camera_ids=sorted(sched[k + 1]),
+                  next_camera_blocks=sched[k + 1], previous_recency_scores=recency,
+                  recency_decay=0.9)
+        if case["policy"] == "passthrough":
+            tr = rp.compute_passthrough_resident_transition(**kw)
+        else:
+            tr = rp.compute_topc_resident_transition(
+                **kw, lambda_weight=0.7, resident_capacity_blocks=case["capacity"],
+                balanced_camera_seeds=(case["policy"] == "topc_balanced"),
+                balanced_seed_fraction=case["fraction"])
+        got = G.field_digests(tr)
+        want = case["records"][k]
+        bad = [f for f in want if got.get(f) != want[f]]
+        assert not bad, f"{case['policy']} cap {case['capacity']} step {k}: {bad}"
+        assert isinstance(tr.updated_recency_scores, rp.RecencyScores if dense else dict)
+        recency = tr.updated_recency_scores
+        resident = list(tr.next_resident_blocks)
+
+
+@pytest.mark.parametrize("dense", [False, True])
+@pytest.mark.parametrize("k", range(len(FIX["cases"])))
+def test_planner_matches_reference(k, dense):
+    _replay(FIX["cases"][k], dense)
+
+
+def test_recency_scores_mapping():
+    s = rp.RecencyScores.from_dict({5: 0.5, 2: 1.0})
+    assert dict(s) == {2: 1.0, 5: 0.5} and len(s) == 2 and 3 not in s
+    tr = rp.compute_passthrough_resident_transition([1, 2], [2, 3], previous_recency_scores=s,
+                                                    recency_decay=0.5)
+    assert dict(tr.updated_recency_scores) == {1: 1.0, 2: 1.0, 5: 0.25}
+    empty = rp.compute_topc_resident_transition([], [], resident_capacity_blocks=4)
+    assert empty.next_resident_blocks == [] and empty.topc_cutoff_score == 0.0

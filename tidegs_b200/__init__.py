@@ -10,6 +10,8 @@ Drop-in classes (same names and behaviour as the reference's):
     PinnedBlockCache, BlockLogStore,     storage/tiered_cache_manager.py,
     CachedBlockReader                    storage/log_storage_manager.py, storage/block_reader.py
     BlockCuller                          storage/gaussian_block.py (FrustumCuller)
+    compute_topc_resident_transition,    strategies/tide_engine/resident_policy.py
+    compute_passthrough_resident_transition
 plus SelectiveSophia (no reference counterpart) and PinnedBlockPool.
 
 All device work runs in libtidegs_b200.so (include/tidegs_b200.h); importing
@@ -19,6 +21,9 @@ host code (page-locked memory when CUDA is present) whose device transfers
 are issued by GPUWorkingSet and DoubleBufferGPUWorkingSet.
 """
 from .culling import BlockCuller
+from .resident_policy import (RecencyScores, ResidentTransition,
+                              compute_passthrough_resident_transition,
+                              compute_topc_resident_transition)
 from .block_reader import (BlockBatch, BlockLayout, BlockReader, PinnedBlockPool,
                            UnifiedParamsBlockReader, parse_block_row_components)
 from .double_buffer_gpu import DoubleBufferGPUWorkingSet, GPUBuffer, ResidentHandoffResult
@@ -35,5 +40,6 @@ __all__ = [
     "ResidentHandoffResult", "GPUResidentAdam", "GPUWorkingSet", "PendingBlockBounds",
     "PendingBlockWriteback", "ResidentAdamContext", "SelectiveAdam", "SelectiveSophia",
     "SparseGradAccumulator", "PendingCacheWriteback", "BlockLogStore", "CachedBlockReader",
-    "PinnedBlockCache", "BlockCuller",
+    "PinnedBlockCache", "BlockCuller", "RecencyScores", "ResidentTransition",
+    "compute_passthrough_resident_transition", "compute_topc_resident_transition",
 ]

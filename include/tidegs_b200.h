@@ -580,6 +580,116 @@ TGS_API int64_t tgs_frustum_cull_slices(int64_t n_items);
  * ordered writing pass, each a grid of (slice, camera) CTAs. */
 TGS_API int tgs_frustum_cull(const TgsCullArgs* args, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Render path before the optimizer (the engine's gsplat 1.0.0 calls,        */
+/* strategies/tide_engine/engine.py:481-561)                                 */
+/* Replaces: submodules/gsplat/gsplat/cuda/csrc                              */
+/*   fully_fused_projection_fwd.cu:19-121, fully_fused_projection_bwd.cu     */
+/*   isect_tiles.cu:15-280, rasterize_to_pixels_fwd.cu:15-158,               */
+/*   rasterize_to_pixels_bwd.cu:15-250                                       */
+/* Layouts are gsplat's non-packed ones: per camera c and Gaussian n the      */
+/* flat index c * N + n.                                                      */
+/* ------------------------------------------------------------------------ */
+
+typedef struct {
+  const float* means;     /* [N, 3] world positions */
+  const float* quats;     /* [N, 4] (w, x, y, z), normalized in the kernel */
+  const float* scales;    /* [N, 3] */
+  const float* viewmats;  /* [C, 4, 4] row-major world-to-camera */
+  const float* Ks;        /* [C, 3, 3] row-major intrinsics */
+  int32_t n_cameras;
+  int64_t n_gaussians;
+  int32_t image_width;
+  int32_t image_height;
+  float eps2d;            /* added to the 2D covariance diagonal */
+  float near_plane;
+  float far_plane;
+  float radius_clip;      /* radii <= this are culled */
+  int32_t* radii;         /* [C, N] 0 = culled */
+  float* means2d;         /* [C, N, 2] */
+  float* depths;          /* [C, N] */
+  float* conics;          /* [C, N, 3] inverse 2D covariance (xx, xy, yy) */
+  float* compensations;   /* [C, N] sqrt(det / det_blurred), or NULL */
+} TgsProjectArgs;
+
+/* Projection of every Gaussian into every camera
+ * (fully_fused_projection_fwd.cu:19-121). Outputs of culled entries other
+ * than radii are left unwritten. */
+TGS_API int tgs_project_fwd(const TgsProjectArgs* args, void* stream);
+
+typedef struct {
+  TgsProjectArgs fwd;              /* forward inputs; radii, conics, compensations read */
+  const float* v_means2d;          /* [C, N, 2] */
+  const float* v_depths;           /* [C, N] */
+  const float* v_conics;           /* [C, N, 3] */
+  const float* v_compensations;    /* [C, N] or NULL */
+  float* v_means;                  /* [N, 3] accumulated (caller zeroes) */
+  float* v_quats;                  /* [N, 4] accumulated */
+  float* v_scales;                 /* [N, 3] accumulated */
+} TgsProjectBwdArgs;
+
+/* Gradients of the projection with respect to means, quats and scales
+ * (fully_fused_projection_bwd.cu:19-190; camera gradients not computed). */
+TGS_API int tgs_project_bwd(const TgsProjectBwdArgs* args, void* stream);
+
+/* Tiles each projected Gaussian overlaps (isect_tiles.cu first pass). */
+TGS_API int tgs_isect_count(const float* means2d, const int32_t* radii, int64_t n,
+                    int32_t tile_size, int32_t tile_width, int32_t tile_height,
+                    int32_t* tiles_per_gauss, void* stream);
+/* floor(log2(n_tiles)) + 1: bits of the tile id in an intersection key. */
+TGS_API int32_t tgs_isect_tile_bits(int32_t n_tiles);
+/* Keys camera << (32 + tile_bits) | tile << 32 | depth bits and flat
+ * Gaussian ids, written at the inclusive prefix sums cum_tiles of the
+ * counts (isect_tiles.cu second pass; the caller sorts them, stably). */
+TGS_API int tgs_isect_write(const float* means2d, const int32_t* radii, const float* depths,
+                    int64_t n, int64_t n_per_camera, int32_t tile_size, int32_t tile_width,
+                    int32_t tile_height, const int64_t* cum_tiles, int64_t* isect_ids,
+                    int32_t* flatten_ids, void* stream);
+/* offsets[c, tile] = index of the first sorted key of (c, tile)
+ * (isect_offset_encode, isect_tiles.cu:227-280). */
+TGS_API int tgs_isect_offsets(const int64_t* isect_ids, int64_t n_isects, int32_t n_cameras,
+                      int32_t tile_width, int32_t tile_height, int32_t* offsets, void* stream);
+
+typedef struct {
+  const float* means2d;       /* [C, N, 2] */
+  const float* conics;        /* [C, N, 3] */
+  const float* colors;        /* [C, N, channels] */
+  const float* opacities;     /* [C, N] */
+  const float* backgrounds;   /* [C, channels] or NULL */
+  int32_t n_cameras;
+  int64_t n_gaussians;        /* N */
+  int32_t channels;           /* 1 .. 4 */
+  int32_t image_width;
+  int32_t image_height;
+  int32_t tile_size;          /* tile_size^2 threads per CTA: a multiple of 32, <= 1024 */
+  int32_t tile_width;
+  int32_t tile_height;
+  const int32_t* tile_offsets; /* [C, tile_height, tile_width] */
+  const int32_t* flatten_ids;  /* [n_isects] sorted */
+  int64_t n_isects;
+  float* render_colors;       /* [C, H, W, channels] */
+  float* render_alphas;       /* [C, H, W] */
+  int32_t* last_ids;          /* [C, H, W] index of the last contributing intersection */
+} TgsRasterArgs;
+
+/* Front-to-back alpha compositing per 16x16 tile (rasterize_to_pixels_fwd.cu). */
+TGS_API int tgs_rasterize_fwd(const TgsRasterArgs* args, void* stream);
+
+typedef struct {
+  TgsRasterArgs fwd;              /* render_alphas, last_ids read */
+  const float* v_render_colors;   /* [C, H, W, channels] */
+  const float* v_render_alphas;   /* [C, H, W] */
+  float* v_means2d_abs;           /* [C, N, 2] or NULL; accumulated */
+  float* v_means2d;               /* [C, N, 2] accumulated (caller zeroes) */
+  float* v_conics;                /* [C, N, 3] accumulated */
+  float* v_colors;                /* [C, N, channels] accumulated */
+  float* v_opacities;             /* [C, N] accumulated */
+} TgsRasterBwdArgs;
+
+/* Back-to-front gradient of the compositing (rasterize_to_pixels_bwd.cu);
+ * per Gaussian and tile, one set of global additions. */
+TGS_API int tgs_rasterize_bwd(const TgsRasterBwdArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -46,11 +46,55 @@ def build(root: Path, verbose: bool = False):
     )
 
 
+GSPLAT_MODULE = "gsplat_ref"
+GSPLAT_OUT = OUT / "gsplat"
+# the kernels of the engine's render path (projection, tile intersection,
+# rasterization), compiled with gsplat's own nvcc flags (its setup.py:79-94)
+GSPLAT_SOURCES = ("fully_fused_projection_fwd.cu", "fully_fused_projection_bwd.cu",
+                  "isect_tiles.cu", "rasterize_to_pixels_fwd.cu", "rasterize_to_pixels_bwd.cu")
+
+
+def build_gsplat(root: Path, verbose: bool = False):
+    """Compiles the reference's gsplat 1.0.0 render-path kernels (vendored
+    sources, read in place) into oracle/_ref/gsplat/gsplat_ref*.so."""
+    from torch.utils.cpp_extension import load
+
+    csrc = root / "submodules" / "gsplat" / "gsplat" / "cuda" / "csrc"
+    GSPLAT_OUT.mkdir(parents=True, exist_ok=True)
+    return load(
+        name=GSPLAT_MODULE,
+        sources=[str(csrc / f) for f in GSPLAT_SOURCES] + [str(HERE / "gsplat_ref_binding.cpp")],
+        extra_include_paths=[str(csrc), str(csrc / "third_party" / "glm")],
+        extra_cuda_cflags=["-O3", "--use_fast_math", "--expt-relaxed-constexpr",
+                           "-diag-suppress", "20012",
+                           "-gencode", "arch=compute_100a,code=sm_100a"],
+        extra_cflags=["-O3", "-Wno-sign-compare"],
+        build_directory=str(GSPLAT_OUT),
+        verbose=verbose,
+    )
+
+
+def load_prebuilt_gsplat():
+    """Imports the prebuilt reference gsplat module (None if absent)."""
+    import importlib.util
+
+    import torch  # noqa: F401
+
+    for path in sorted(GSPLAT_OUT.glob(f"{GSPLAT_MODULE}*.so")):
+        spec = importlib.util.spec_from_file_location(GSPLAT_MODULE, path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod
+    return None
+
+
 def build_if_reference_present() -> bool:
     root = reference_root()
     if root is None:
         return False
     build(root)
+    if (root / "submodules" / "gsplat" / "gsplat" / "cuda" / "csrc").exists():
+        build_gsplat(root)
     return True
 
 
@@ -78,6 +122,7 @@ def main(argv=None) -> int:
         print("reference tree not found; nothing built")
         return 1
     build(root, verbose=args.verbose)
+    build_gsplat(root, verbose=args.verbose)
     print("built into", OUT)
     return 0
 

@@ -75,7 +75,8 @@ def test_struct_offsets_match_the_c_compiler(tmp_path):
     structs = {name: getattr(_lib, name) for name in (
         "ResidentCountArgs", "ResidentAdamArgs", "DenseGroup", "DenseArgs", "UnpackArgs",
         "CopyBlocksArgs", "PackArgs", "BlockSumArgs", "GradPushArgs", "PeerHandle",
-        "ResidentAdamSumArgs", "SparseAccumArgs", "CullArgs")}
+        "ResidentAdamSumArgs", "SparseAccumArgs", "CullArgs", "ProjectArgs",
+        "ProjectBwdArgs", "RasterArgs", "RasterBwdArgs")}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "tidegs_b200.h"',
              'int main(void) {']
     expect = []

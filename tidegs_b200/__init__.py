@@ -12,6 +12,9 @@ Drop-in classes (same names and behaviour as the reference's):
     BlockCuller                          storage/gaussian_block.py (FrustumCuller)
     compute_topc_resident_transition,    strategies/tide_engine/resident_policy.py
     compute_passthrough_resident_transition
+    render.fully_fused_projection,       gsplat 1.0.0 (the engine's render path,
+    render.isect_tiles, isect_offset_encode, strategies/tide_engine/engine.py:481-561)
+    render.rasterize_to_pixels
 plus SelectiveSophia (no reference counterpart) and PinnedBlockPool.
 
 All device work runs in libtidegs_b200.so (include/tidegs_b200.h); importing

@@ -147,6 +147,42 @@ class CullArgs(C.Structure):
     ]
 
 
+class ProjectArgs(C.Structure):
+    _fields_ = [
+        ("means", _vp), ("quats", _vp), ("scales", _vp), ("viewmats", _vp), ("Ks", _vp),
+        ("n_cameras", _i32), ("n_gaussians", _i64), ("image_width", _i32),
+        ("image_height", _i32), ("eps2d", C.c_float), ("near_plane", C.c_float),
+        ("far_plane", C.c_float), ("radius_clip", C.c_float), ("radii", _vp), ("means2d", _vp),
+        ("depths", _vp), ("conics", _vp), ("compensations", _vp),
+    ]
+
+
+class ProjectBwdArgs(C.Structure):
+    _fields_ = [
+        ("fwd", ProjectArgs), ("v_means2d", _vp), ("v_depths", _vp), ("v_conics", _vp),
+        ("v_compensations", _vp), ("v_means", _vp), ("v_quats", _vp), ("v_scales", _vp),
+    ]
+
+
+class RasterArgs(C.Structure):
+    _fields_ = [
+        ("means2d", _vp), ("conics", _vp), ("colors", _vp), ("opacities", _vp),
+        ("backgrounds", _vp), ("n_cameras", _i32), ("n_gaussians", _i64), ("channels", _i32),
+        ("image_width", _i32), ("image_height", _i32), ("tile_size", _i32),
+        ("tile_width", _i32), ("tile_height", _i32), ("tile_offsets", _vp),
+        ("flatten_ids", _vp), ("n_isects", _i64), ("render_colors", _vp),
+        ("render_alphas", _vp), ("last_ids", _vp),
+    ]
+
+
+class RasterBwdArgs(C.Structure):
+    _fields_ = [
+        ("fwd", RasterArgs), ("v_render_colors", _vp), ("v_render_alphas", _vp),
+        ("v_means2d_abs", _vp), ("v_means2d", _vp), ("v_conics", _vp), ("v_colors", _vp),
+        ("v_opacities", _vp),
+    ]
+
+
 # name -> (restype, argtypes). Keep in sync with include/tidegs_b200.h.
 SIGNATURES = {
     "tgs_version": (C.c_int, []),
@@ -188,6 +224,15 @@ SIGNATURES = {
     "tgs_block_spheres": (C.c_int, [_vp, _i64, _vp, _vp, _vp]),
     "tgs_frustum_cull": (C.c_int, [C.POINTER(CullArgs), _vp]),
     "tgs_frustum_cull_slices": (_i64, [_i64]),
+    "tgs_project_fwd": (C.c_int, [C.POINTER(ProjectArgs), _vp]),
+    "tgs_project_bwd": (C.c_int, [C.POINTER(ProjectBwdArgs), _vp]),
+    "tgs_isect_count": (C.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp]),
+    "tgs_isect_tile_bits": (_i32, [_i32]),
+    "tgs_isect_write": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp,
+                                  _vp]),
+    "tgs_isect_offsets": (C.c_int, [_vp, _i64, _i32, _i32, _i32, _vp, _vp]),
+    "tgs_rasterize_fwd": (C.c_int, [C.POINTER(RasterArgs), _vp]),
+    "tgs_rasterize_bwd": (C.c_int, [C.POINTER(RasterBwdArgs), _vp]),
 }
 
 _lock = threading.Lock()
@@ -237,6 +282,8 @@ KERNELS_PER_CALL = {
     "tgs_block_bounds": 1, "tgs_block_grad_sum": 1, "tgs_copy_small": 1, "tgs_grad_push": 1,
     "tgs_resident_adam_apply_sum": 1, "tgs_bitmap_list": 3, "tgs_gather_i64": 1, "tgs_bitmap_set": 1,
     "tgs_sparse_grad_accumulate": 1, "tgs_block_spheres": 1, "tgs_frustum_cull": 2,
+    "tgs_project_fwd": 1, "tgs_project_bwd": 1, "tgs_isect_count": 1, "tgs_isect_write": 1,
+    "tgs_isect_offsets": 1, "tgs_rasterize_fwd": 1, "tgs_rasterize_bwd": 1,
 }
 launch_counter = {"kernels": 0}
 

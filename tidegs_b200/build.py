@@ -25,7 +25,7 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libtidegs_b200.so"
 
 SOURCES = ("tgs_abi.cu", "tgs_adam.cu", "tgs_blocks.cu", "tgs_dirty.cu", "tgs_exchange.cu",
-           "tgs_sparse.cu", "tgs_cull.cu")
+           "tgs_sparse.cu", "tgs_cull.cu", "tgs_render.cu")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

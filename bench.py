@@ -980,6 +980,108 @@ def cull_probe(args):
                       "reference_numpy_ms": round(cpu_ms, 2), "equal": True}), flush=True)
 
 
+def render_probe(args):
+    """Not the bench line. The engine's render path for one camera batch
+    (strategies/tide_engine/engine.py:481-561): projection, tile intersection,
+    rasterization forward and the two backward kernels, tidegs_b200 against
+    the reference's gsplat 1.0.0 kernels compiled from its sources
+    (oracle/_ref/gsplat) on the same inputs. Seeded scene: 2 M Gaussians in
+    a box in front of a 1920 x 1080 camera, log-normal scales, uniform
+    opacities and colors. One JSON line per implementation (CUDA events,
+    median over --steps after --warmup)."""
+    from oracle import build_ref
+    from oracle import render as orc
+    from tidegs_b200 import render as tr
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    Wd, Hd, tile, n = 1920, 1080, 16, 2_000_000
+    g = torch.Generator(device=dev).manual_seed(3)
+    means = (torch.rand((n, 3), generator=g, device=dev) * torch.tensor([16.0, 9.0, 20.0], device=dev)
+             + torch.tensor([-8.0, -4.5, 4.0], device=dev))
+    quats = torch.randn((n, 4), generator=g, device=dev)
+    scales = torch.exp(torch.randn((n, 3), generator=g, device=dev) * 0.5 - 3.2)
+    opac = torch.rand((1, n), generator=g, device=dev) * 0.9 + 0.05
+    colors = torch.rand((1, n, 3), generator=g, device=dev)
+    view = orc.look_at((0.0, 0.0, -1.0), (0.0, 0.0, 10.0), up=(0.0, -1.0, 0.0))[None].float().to(dev)
+    K = orc.intrinsics(Wd, Hd, 70.0)[None].float().to(dev)
+    tw, th = (Wd + tile - 1) // tile, (Hd + tile - 1) // tile
+    ref = build_ref.load_prebuilt_gsplat()
+    means_g, quats_g, scales_g = (t.clone().requires_grad_(True) for t in (means, quats, scales))
+
+    def run_ours():
+        marks = {}
+        radii, m2, dep, con, _ = tr._Projection.apply(means_g, quats_g, scales_g, view, K, Wd, Hd,
+                                                      0.3, 0.01, 1e10, 0.0, False)
+        marks["projection"] = torch.cuda.Event(enable_timing=True)
+        marks["projection"].record()
+        _, ids, flat = tr.isect_tiles(m2, radii, dep, tile, tw, th)
+        offs = tr.isect_offset_encode(ids, 1, tw, th)
+        marks["intersect"] = torch.cuda.Event(enable_timing=True)
+        marks["intersect"].record()
+        m2r = m2.detach().requires_grad_(True)
+        conr = con.detach().requires_grad_(True)
+        colr = colors.detach().requires_grad_(True)
+        opr = opac.detach().requires_grad_(True)
+        rc, ra = tr.rasterize_to_pixels(m2r, conr, colr, opr, Wd, Hd, tile, offs, flat)
+        marks["raster_fwd"] = torch.cuda.Event(enable_timing=True)
+        marks["raster_fwd"].record()
+        (rc.sum() + ra.sum()).backward()
+        marks["raster_bwd"] = torch.cuda.Event(enable_timing=True)
+        marks["raster_bwd"].record()
+        torch.autograd.backward([m2, dep, con], [m2r.grad, torch.zeros_like(dep), conr.grad])
+        marks["projection_bwd"] = torch.cuda.Event(enable_timing=True)
+        marks["projection_bwd"].record()
+        return marks, int(flat.numel())
+
+    def run_ref():
+        marks = {}
+        radii, m2, dep, con, _ = ref.fully_fused_projection_fwd(means, None, quats, scales, view, K,
+                                                                Wd, Hd, 0.3, 0.01, 1e10, 0.0, False)
+        marks["projection"] = torch.cuda.Event(enable_timing=True)
+        marks["projection"].record()
+        _, ids, flat = ref.isect_tiles(m2, radii, dep, None, None, 1, tile, tw, th, True, True)
+        offs = ref.isect_offset_encode(ids, 1, tw, th)
+        marks["intersect"] = torch.cuda.Event(enable_timing=True)
+        marks["intersect"].record()
+        rc, ra, last = ref.rasterize_to_pixels_fwd(m2, con, colors, opac, None, Wd, Hd, tile, offs, flat)
+        marks["raster_fwd"] = torch.cuda.Event(enable_timing=True)
+        marks["raster_fwd"].record()
+        _, vm, vc, vcol, vo = ref.rasterize_to_pixels_bwd(m2, con, colors, opac, None, Wd, Hd, tile,
+                                                          offs, flat, ra, last, torch.ones_like(rc),
+                                                          torch.ones_like(ra), False)
+        marks["raster_bwd"] = torch.cuda.Event(enable_timing=True)
+        marks["raster_bwd"].record()
+        ref.fully_fused_projection_bwd(means, None, quats, scales, view, K, Wd, Hd, 0.3, radii, con,
+                                       None, vm, torch.zeros_like(dep), vc, None, False)
+        marks["projection_bwd"] = torch.cuda.Event(enable_timing=True)
+        marks["projection_bwd"].record()
+        return marks, int(flat.numel())
+
+    arms = [("tidegs_b200", run_ours)]
+    if ref is not None:
+        arms.append(("reference_gsplat", run_ref))
+    for name, fn in arms:
+        per = {}
+        for k in range(args.warmup + args.steps):
+            torch.cuda.synchronize()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            marks, n_isects = fn()
+            torch.cuda.synchronize()
+            if k < args.warmup:
+                continue
+            prev = e0
+            for stage, ev in marks.items():
+                per.setdefault(stage, []).append(prev.elapsed_time(ev))
+                prev = ev
+        out = {"probe": "render", "impl": name, "gaussians": n, "image": [Wd, Hd],
+               "intersections": n_isects}
+        out.update({k + "_ms": round(statistics.median(v), 3) for k, v in per.items()})
+        out["total_ms"] = round(sum(out[k + "_ms"] for k in per), 3)
+        print(json.dumps(out), flush=True)
+
+
 def accum_probe(args):
     """Not the bench line. A camera batch of the configs[3] shape (16 cameras,
     each seeing a contiguous run of 24-56 resident blocks of 16,384 rows out
@@ -1163,6 +1265,8 @@ def main(argv=None):
                          "(needs two GPUs for remote)")
     ap.add_argument("--cull-probe", action="store_true",
                     help="diagnostic: frustum culling of a 61,036-block scene, 16 cameras")
+    ap.add_argument("--render-probe", action="store_true",
+                    help="diagnostic: render path, ours vs the reference gsplat kernels")
     ap.add_argument("--accum-probe", action="store_true",
                     help="diagnostic instead of the bench: touched-only gradient accumulation "
                          "of a camera batch against the reference's torch operations")
@@ -1182,6 +1286,8 @@ def main(argv=None):
         return accum_probe(args)
     if args.cull_probe:
         return cull_probe(args)
+    if args.render_probe:
+        return render_probe(args)
 
     from tidegs_b200 import _lib
 

@@ -613,8 +613,8 @@ typedef struct {
 } TgsProjectArgs;
 
 /* Projection of every Gaussian into every camera
- * (fully_fused_projection_fwd.cu:19-121). Outputs of culled entries other
- * than radii are left unwritten. */
+ * (fully_fused_projection_fwd.cu:19-121); culled entries get radius 0 and
+ * zero outputs. */
 TGS_API int tgs_project_fwd(const TgsProjectArgs* args, void* stream);
 
 typedef struct {

@@ -19,9 +19,8 @@
 //   stops when its transmittance would fall to 1e-4 or below;
 // * backward: the same traversal back to front, transmittance recovered by
 //   division; per Gaussian the warp's partial gradients are summed with
-//   shuffles, then the eight warps of the tile add into one shared-memory
-//   slot per Gaussian of the batch, and each slot reaches global memory with
-//   one set of atomics per tile (instead of one set per warp).
+//   shuffles and lane 0 adds them to global memory (atomics; combining the
+//   tile's warps in shared memory first measured slower).
 #include <math.h>
 
 #include "tgs_common.cuh"
@@ -125,10 +124,21 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const TgsProj
   const int64_t total = static_cast<int64_t>(a.n_cameras) * a.n_gaussians;
   if (idx >= total) return;
   const int64_t cam = idx / a.n_gaussians, g = idx - cam * a.n_gaussians;
+  // culled entries: radius 0 and zero outputs
+  auto cull = [&]() {
+    a.radii[idx] = 0;
+    a.means2d[idx * 2] = 0.f;
+    a.means2d[idx * 2 + 1] = 0.f;
+    a.depths[idx] = 0.f;
+    a.conics[idx * 3] = 0.f;
+    a.conics[idx * 3 + 1] = 0.f;
+    a.conics[idx * 3 + 2] = 0.f;
+    if (a.compensations != nullptr) a.compensations[idx] = 0.f;
+  };
   ProjectGeom G;
   project_geometry(a, cam, g, G);
   if (G.pc[2] < a.near_plane || G.pc[2] > a.far_plane) {
-    a.radii[idx] = 0;
+    cull();
     return;
   }
   const Persp P = persp_setup(a, cam, G.pc);
@@ -146,7 +156,7 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const TgsProj
   c11 += a.eps2d;
   const float det = c00 * c11 - c01 * c01;
   if (!(det > 0.f)) {
-    a.radii[idx] = 0;
+    cull();
     return;
   }
   const float inv_det = 1.f / det;
@@ -154,13 +164,13 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const TgsProj
   const float v1 = bmid + sqrtf(fmaxf(0.01f, bmid * bmid - det));
   const float radius = ceilf(3.f * sqrtf(v1));
   if (radius <= a.radius_clip) {
-    a.radii[idx] = 0;
+    cull();
     return;
   }
   const float mx = P.fx * G.pc[0] * P.rz + P.cx, my = P.fy * G.pc[1] * P.rz + P.cy;
   if (mx + radius <= 0.f || mx - radius >= a.image_width || my + radius <= 0.f ||
       my - radius >= a.image_height) {
-    a.radii[idx] = 0;
+    cull();
     return;
   }
   a.radii[idx] = static_cast<int32_t>(radius);
@@ -474,7 +484,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int D>
 __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
   const TgsRasterArgs& a = b.fwd;
-  // per-Gaussian gradient slot: means2d (2), conic (3), colors (D), opacity,
+  // per-Gaussian gradient: means2d (2), conic (3), colors (D), opacity,
   // |means2d| (2)
   constexpr int K = 2 + 3 + D + 1 + 2;
   extern __shared__ __align__(16) unsigned char raster_smem[];
@@ -483,7 +493,6 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
   float3* xyo = reinterpret_cast<float3*>(ids + nthreads);
   float3* con = xyo + nthreads;
   float* rgb = reinterpret_cast<float*>(con + nthreads);
-  float* slot = rgb + nthreads * D;  // [nthreads][K]
 
   const int cam = blockIdx.x;
   const int tile_id = blockIdx.y * a.tile_width + blockIdx.z;
@@ -536,8 +545,6 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
 #pragma unroll
       for (int k = 0; k < D; ++k) rgb[tr * D + k] = a.colors[static_cast<int64_t>(g) * D + k];
     }
-#pragma unroll
-    for (int k = 0; k < K; ++k) slot[tr * K + k] = 0.f;
     __syncthreads();
     for (int t = max(0, batch_end - warp_bin_final); t < batch_size; ++t) {
       bool valid = inside && (batch_end - t <= bin_final);
@@ -559,7 +566,8 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
 #pragma unroll
       for (int k = 0; k < K; ++k) gv[k] = 0.f;
       if (valid) {
-        const float ra = 1.f / (1.f - alpha);
+        // fast reciprocal (the render path is compared within tolerance)
+        const float ra = __fdividef(1.f, 1.f - alpha);
         T *= ra;
         const float fac = alpha * T;
         float v_alpha = 0.f;
@@ -584,30 +592,22 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
 #pragma unroll
         for (int k = 0; k < D; ++k) buffer[k] += rgb[t * D + k] * fac;
       }
+      float sv[K];
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        if (k >= 6 + D && !absgrad) continue;
-        const float s = warp_sum(gv[k]);
-        if (lane == 0 && s != 0.f) atomicAdd(&slot[t * K + k], s);
-      }
-    }
-    __syncthreads();
-    // one set of global additions per Gaussian of the batch
-    if (tr < batch_size) {
-      const int64_t g = ids[tr];
-      const float* sv = slot + tr * K;
-      if (sv[0] != 0.f) atomicAdd(b.v_means2d + 2 * g, sv[0]);
-      if (sv[1] != 0.f) atomicAdd(b.v_means2d + 2 * g + 1, sv[1]);
+      for (int k = 0; k < K; ++k) sv[k] = (k >= 6 + D && !absgrad) ? 0.f : warp_sum(gv[k]);
+      if (lane == 0) {
+        const int64_t g = ids[t];
+        atomicAdd(b.v_means2d + 2 * g, sv[0]);
+        atomicAdd(b.v_means2d + 2 * g + 1, sv[1]);
 #pragma unroll
-      for (int k = 0; k < 3; ++k)
-        if (sv[2 + k] != 0.f) atomicAdd(b.v_conics + 3 * g + k, sv[2 + k]);
+        for (int k = 0; k < 3; ++k) atomicAdd(b.v_conics + 3 * g + k, sv[2 + k]);
 #pragma unroll
-      for (int k = 0; k < D; ++k)
-        if (sv[5 + k] != 0.f) atomicAdd(b.v_colors + D * g + k, sv[5 + k]);
-      if (sv[5 + D] != 0.f) atomicAdd(b.v_opacities + g, sv[5 + D]);
-      if (absgrad) {
-        if (sv[6 + D] != 0.f) atomicAdd(b.v_means2d_abs + 2 * g, sv[6 + D]);
-        if (sv[7 + D] != 0.f) atomicAdd(b.v_means2d_abs + 2 * g + 1, sv[7 + D]);
+        for (int k = 0; k < D; ++k) atomicAdd(b.v_colors + D * g + k, sv[5 + k]);
+        atomicAdd(b.v_opacities + g, sv[5 + D]);
+        if (absgrad) {
+          atomicAdd(b.v_means2d_abs + 2 * g, sv[6 + D]);
+          atomicAdd(b.v_means2d_abs + 2 * g + 1, sv[7 + D]);
+        }
       }
     }
   }
@@ -616,7 +616,7 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
 template <int D>
 size_t raster_smem_bytes(int nthreads, bool bwd) {
   size_t s = nthreads * (sizeof(int32_t) + 2 * sizeof(float3));
-  if (bwd) s += nthreads * sizeof(float) * (D + (2 + 3 + D + 1 + 2));
+  if (bwd) s += nthreads * sizeof(float) * D;
   return s;
 }
 

@@ -61,10 +61,10 @@ class _Projection(torch.autograd.Function):
         view_, Ks_ = _f32(viewmats, "viewmats"), _f32(Ks, "Ks")
         C, N = int(view_.shape[0]), int(means_.shape[0])
         radii = torch.empty((C, N), dtype=torch.int32, device=dev)
-        means2d = torch.zeros((C, N, 2), dtype=torch.float32, device=dev)
-        depths = torch.zeros((C, N), dtype=torch.float32, device=dev)
-        conics = torch.zeros((C, N, 3), dtype=torch.float32, device=dev)
-        comps = torch.zeros((C, N), dtype=torch.float32, device=dev) if calc_compensations else None
+        means2d = torch.empty((C, N, 2), dtype=torch.float32, device=dev)
+        depths = torch.empty((C, N), dtype=torch.float32, device=dev)
+        conics = torch.empty((C, N, 3), dtype=torch.float32, device=dev)
+        comps = torch.empty((C, N), dtype=torch.float32, device=dev) if calc_compensations else None
         args = _project_args(means_, quats_, scales_, view_, Ks_, width, height, eps2d, near_plane,
                              far_plane, radius_clip, radii, means2d, depths, conics, comps)
         _lib.call("tgs_project_fwd", args, _stream(means_))

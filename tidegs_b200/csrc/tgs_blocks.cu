@@ -24,13 +24,16 @@ struct ConstComp6 {
 
 // ---------------------------------------------------------------------------
 // Unpack: packed [rows, 59] -> six SoA components (+ global ids).
-// Persistent CTAs walk 64-row tiles; one thread streams each tile into shared
-// memory with a bulk (TMA) copy, double-buffered, while all threads scatter
-// the previous tile's columns into the component arrays with coalesced stores.
+// Persistent CTAs walk 64-row tiles; one thread keeps kUnpackStages tiles in
+// flight with bulk (TMA) copies into a shared-memory ring, while all threads
+// scatter the oldest tile's columns into the component arrays with coalesced
+// stores.
 // ---------------------------------------------------------------------------
 constexpr int kTileRows = 64;
 constexpr int kTileFloats = kTileRows * kRowWidth;  // 3776 floats = 15104 B (multiple of 16)
 constexpr int kUnpackThreads = 256;
+constexpr int kUnpackStages = 4;
+constexpr int kUnpackCtasPerSm = 3;
 
 struct UnpackParams {
   const float* packed;
@@ -44,6 +47,12 @@ struct UnpackParams {
   int use_bulk;  // packed is 16-byte aligned
   int32_t* err;
 };
+
+struct UnpackSmem {
+  float tile[kUnpackStages][kTileFloats];
+  uint64_t bar[kUnpackStages];
+};
+constexpr size_t kUnpackSmemBytes = sizeof(UnpackSmem);
 
 template <int kLayout>
 __device__ __forceinline__ void scatter_tile(const float* __restrict__ tile, int rows,
@@ -63,9 +72,9 @@ __device__ __forceinline__ void scatter_tile(const float* __restrict__ tile, int
 }
 
 template <int kLayout>
-__global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackParams a) {
-  __shared__ __align__(128) float tiles[2][kTileFloats];
-  __shared__ __align__(8) uint64_t bars[2];
+__global__ void __launch_bounds__(kUnpackThreads, kUnpackCtasPerSm) unpack_kernel(const UnpackParams a) {
+  extern __shared__ __align__(128) unsigned char unpack_smem_raw[];
+  UnpackSmem& sm = *reinterpret_cast<UnpackSmem*>(unpack_smem_raw);
   const int64_t n_tiles = ceil_div<int64_t>(a.n_rows, kTileRows);
   const int tid = threadIdx.x;
 
@@ -77,48 +86,53 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackPara
   auto bulk_rows = [&](int rows) -> int { return a.use_bulk ? (rows & ~3) : 0; };
 
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
-    fence_proxy_async_smem();
+    for (int q = 0; q < kUnpackStages; ++q) mbar_init(&sm.bar[q], 1);
+    fence_mbar_init();
   }
   __syncthreads();
 
-  auto issue = [&](int64_t t, int buf) {
+  uint32_t pending = 0;  // stages with a bulk copy in flight (thread 0)
+  auto issue = [&](int64_t t, int q) {
+    if (t >= n_tiles) return;
     const int br = bulk_rows(tile_rows(t));
     if (br > 0) {
-      // Earlier generic-proxy accesses of this buffer precede the bulk write.
-      fence_proxy_async_smem();
       const uint32_t bytes = static_cast<uint32_t>(br) * kRowWidth * sizeof(float);
-      mbar_arrive_expect_tx(&bars[buf], bytes);
-      bulk_g2s(tiles[buf], a.packed + t * kTileFloats, bytes, &bars[buf]);
+      mbar_arrive_expect_tx(&sm.bar[q], bytes);
+      bulk_g2s(sm.tile[q], a.packed + t * kTileFloats, bytes, &sm.bar[q]);
+      pending |= 1u << q;
     }
   };
 
-  uint32_t phase[2] = {0u, 0u};
-  int64_t t = blockIdx.x;
-  if (t < n_tiles && tid == 0) issue(t, 0);
-  int buf = 0;
-  for (; t < n_tiles; t += gridDim.x, buf ^= 1) {
-    const int64_t next = t + gridDim.x;
-    // The other buffer was released by the __syncthreads ending the previous
-    // iteration, so the next tile can stream in while this one is scattered.
-    if (next < n_tiles && tid == 0) issue(next, buf ^ 1);
+  if (tid == 0)
+    for (int q = 0; q < kUnpackStages; ++q) issue(blockIdx.x + static_cast<int64_t>(q) * gridDim.x, q);
+  uint32_t phase = 0;  // bit q: parity of stage q's next completion
+  int q = 0;
+  for (int64_t t = blockIdx.x; t < n_tiles; t += gridDim.x) {
     const int rows = tile_rows(t);
     const int br = bulk_rows(rows);
-    // Plain loads for rows the bulk copy does not cover.
+    float* tile = sm.tile[q];
+    // Plain loads for rows the bulk copy does not cover (disjoint bytes).
     for (int e = br * kRowWidth + tid; e < rows * kRowWidth; e += kUnpackThreads)
-      tiles[buf][e] = a.packed[t * kTileFloats + e];
+      tile[e] = a.packed[t * kTileFloats + e];
     bool ok = true;
     if (br > 0) {
-      ok = mbar_wait_bounded(&bars[buf], phase[buf]);
-      phase[buf] ^= 1u;
+      ok = mbar_wait_bounded(&sm.bar[q], (phase >> q) & 1u);
+      phase ^= 1u << q;
+      if (tid == 0) pending &= ~(1u << q);
     }
     if (__syncthreads_or(!ok)) {
       report_error(a.err, TGS_DEV_WAIT_TIMEOUT, t);
+      // Wait (bounded) for the copies still in flight before the shared
+      // memory they target is released.
+      if (tid == 0) {
+        for (int k = 0; k < kUnpackStages; ++k)
+          if (pending & (1u << k)) mbar_wait_bounded(&sm.bar[k], (phase >> k) & 1u);
+      }
+      __syncthreads();
       return;
     }
     const int64_t dst_row0 = a.target_offset + t * kTileRows;
-    scatter_tile<kLayout>(tiles[buf], rows, dst_row0, a.comp);
+    scatter_tile<kLayout>(tile, rows, dst_row0, a.comp);
     if (a.gids != nullptr) {
       for (int r = tid; r < rows; r += kUnpackThreads) {
         const int64_t row = t * kTileRows + r;
@@ -126,10 +140,12 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackPara
         a.gids[dst_row0 + r] = a.block_ids[pos] * a.block_size + (row - pos * a.block_size);
       }
     }
-    // This buffer's generic-proxy reads/writes precede the bulk copy that
-    // refills it two tiles later.
+    // This stage's generic-proxy reads/writes precede the bulk copy that
+    // refills it.
     fence_proxy_async_smem();
     __syncthreads();
+    if (tid == 0) issue(t + static_cast<int64_t>(kUnpackStages) * gridDim.x, q);
+    q = (q + 1 == kUnpackStages) ? 0 : q + 1;
   }
 }
 
@@ -603,10 +619,28 @@ extern "C" int tgs_unpack_rows(const TgsUnpackArgs* a, void* stream) {
   p.use_bulk = aligned16(a->packed) ? 1 : 0;
   p.err = a->err;
   const int64_t n_tiles = ceil_div<int64_t>(a->n_rows, kTileRows);
-  const int grid = static_cast<int>(std::min<int64_t>(n_tiles, static_cast<int64_t>(sm_count()) * 6));
+  const int grid = static_cast<int>(
+      std::min<int64_t>(n_tiles, static_cast<int64_t>(sm_count()) * kUnpackCtasPerSm));
+  static bool unpack_configured[64] = {};
+  static std::mutex unpack_mu;
+  int dev = 0;
+  TGS_CUDA(cudaGetDevice(&dev));
+  TGS_CHECK_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(unpack_mu);
+    if (!unpack_configured[dev]) {
+      TGS_CUDA(cudaFuncSetAttribute(unpack_kernel<TGS_LAYOUT_UNIFIED>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kUnpackSmemBytes));
+      TGS_CUDA(cudaFuncSetAttribute(unpack_kernel<TGS_LAYOUT_CACHE>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kUnpackSmemBytes));
+      unpack_configured[dev] = true;
+    }
+  }
   cudaStream_t s = as_stream(stream);
-  if (a->layout == TGS_LAYOUT_UNIFIED) unpack_kernel<TGS_LAYOUT_UNIFIED><<<grid, kUnpackThreads, 0, s>>>(p);
-  else unpack_kernel<TGS_LAYOUT_CACHE><<<grid, kUnpackThreads, 0, s>>>(p);
+  if (a->layout == TGS_LAYOUT_UNIFIED)
+    unpack_kernel<TGS_LAYOUT_UNIFIED><<<grid, kUnpackThreads, kUnpackSmemBytes, s>>>(p);
+  else
+    unpack_kernel<TGS_LAYOUT_CACHE><<<grid, kUnpackThreads, kUnpackSmemBytes, s>>>(p);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

@@ -124,9 +124,10 @@ typedef struct {
 } TgsResidentCountArgs;
 
 /* Validates local_ids (range, strict order, residency), counts touched rows
- * per position, and for every touched position increments its slot's step
- * counter and fills slot_bias from step_table. Enqueues: memset of pos_count
- * and err, 2 kernels. Replaces gpu_resident_optimizer.py:266-337. */
+ * per position (from each position's first and last row), and for every
+ * touched position increments its slot's step counter and fills slot_bias
+ * from step_table. Enqueues: memsets of pos_count and err, 2 kernels.
+ * Replaces gpu_resident_optimizer.py:266-337. */
 TGS_API int tgs_resident_adam_count(const TgsResidentCountArgs* args, void* stream);
 
 typedef struct {

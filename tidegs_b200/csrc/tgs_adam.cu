@@ -25,36 +25,50 @@ __device__ __forceinline__ int upper_bound_i64(const int64_t* __restrict__ a, in
 }
 
 // ---------------------------------------------------------------------------
-// Kernel A: validate ids and count touched rows per resident position.
+// Kernel A: validate the ids (in range, strictly ascending, inside a resident
+// position) and count touched rows per position.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) resident_count_kernel(
     const int64_t* __restrict__ ids, int64_t n, int64_t param_rows,
     const int64_t* __restrict__ pos_start, const int64_t* __restrict__ pos_end, int n_pos,
-    int32_t* __restrict__ pos_count, int32_t* __restrict__ err) {
+    int64_t block_size, int32_t* __restrict__ pos_count, int32_t* __restrict__ err) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
   int p = -1;
-  if (i < n) {
-    const int64_t id = ids[i];
-    int code = TGS_DEV_OK;
-    if (id < 0 || id >= param_rows) {
-      code = TGS_DEV_ID_OUT_OF_RANGE;
-    } else if (i > 0 && ids[i - 1] >= id) {
-      code = TGS_DEV_ID_NOT_SORTED;
+  const int64_t id = ids[i];
+  int code = TGS_DEV_OK;
+  if (id < 0 || id >= param_rows) {
+    code = TGS_DEV_ID_OUT_OF_RANGE;
+  } else if (i > 0 && __ldg(ids + i - 1) >= id) {
+    code = TGS_DEV_ID_NOT_SORTED;
+  } else {
+    // Positions are the working set's block slices in slice order; when they
+    // are whole blocks from row 0 (the persistent-slot layout) position
+    // id / block_size holds the row, so a search is only needed when that
+    // guess misses (a short tail block earlier in the working set).
+    const int g = static_cast<int>(min64(id / block_size, n_pos - 1));
+    if (__ldg(pos_start + g) <= id && id < __ldg(pos_end + g)) {
+      p = g;
     } else {
       p = upper_bound_i64(pos_end, n_pos, id);
       if (p >= n_pos || __ldg(pos_start + p) > id) code = TGS_DEV_ID_NOT_RESIDENT;
     }
-    if (code != TGS_DEV_OK) {
-      report_error(err, code, i);
-      p = -1;
-    }
   }
-  // Rows are sorted, so a warp's rows fall in very few positions: aggregate
-  // per position before touching global memory.
-  const unsigned have = __ballot_sync(0xffffffffu, p >= 0);
+  if (code != TGS_DEV_OK) {
+    report_error(err, code, i);
+    p = -1;
+  }
+  // Rows of a position are consecutive (ids ascending): its first row
+  // subtracts its index and its last row adds its index + 1, so the count
+  // costs two uncontended additions per position (an addition per row or per
+  // warp serializes on one counter while a block's rows are counted). int32
+  // wrap-around keeps the difference exact. Counts are only used when no row
+  // reported an error.
   if (p >= 0) {
-    const unsigned peers = __match_any_sync(have, p);
-    if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(pos_count + p, __popc(peers));
+    if (i == 0 || __ldg(ids + i - 1) < __ldg(pos_start + p))
+      atomicSub(pos_count + p, static_cast<int32_t>(static_cast<uint32_t>(i)));
+    if (i == n - 1 || __ldg(ids + i + 1) >= __ldg(pos_end + p))
+      atomicAdd(pos_count + p, static_cast<int32_t>(static_cast<uint32_t>(i + 1)));
   }
 }
 
@@ -1023,7 +1037,7 @@ extern "C" int tgs_resident_adam_count(const TgsResidentCountArgs* a, void* stre
   TGS_CHECK_ARG(blocks < (1ll << 31), "tgs_resident_adam_count: n_rows too large");
   resident_count_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
       a->local_ids, a->n_rows, a->param_rows, a->pos_start, a->pos_end, a->n_positions,
-      a->pos_count, a->err);
+      a->block_size, a->pos_count, a->err);
   TGS_LAUNCH_CHECK();
   resident_slot_kernel<<<ceil_div(a->n_positions, 256), 256, 0, s>>>(
       a->pos_count, a->pos_slot, a->n_positions, a->slot_step,

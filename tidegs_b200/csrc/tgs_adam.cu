@@ -24,6 +24,21 @@ __device__ __forceinline__ int upper_bound_i64(const int64_t* __restrict__ a, in
   return lo;
 }
 
+// Position of the working-set row `id` (pos_start[p] <= id < pos_end[p]), or
+// the upper bound when no position holds it. Positions are the block slices
+// in slice order; when they are whole blocks from row 0 (the persistent-slot
+// layout) position id / block_size holds the row, so the search only runs
+// when that guess misses (a short tail block earlier in the working set).
+__device__ __forceinline__ int find_position(const int64_t* __restrict__ pos_start,
+                                             const int64_t* __restrict__ pos_end, int n_pos,
+                                             int64_t block_size, int64_t id) {
+  const int64_t q = (block_size & (block_size - 1)) == 0 ? (id >> (__ffsll(block_size) - 1))
+                                                          : id / block_size;
+  const int g = static_cast<int>(q < n_pos - 1 ? q : n_pos - 1);
+  if (__ldg(pos_start + g) <= id && id < __ldg(pos_end + g)) return g;
+  return upper_bound_i64(pos_end, n_pos, id);
+}
+
 // ---------------------------------------------------------------------------
 // Kernel A: validate the ids (in range, strictly ascending, inside a resident
 // position) and count touched rows per position.
@@ -42,17 +57,8 @@ __global__ void __launch_bounds__(256) resident_count_kernel(
   } else if (i > 0 && __ldg(ids + i - 1) >= id) {
     code = TGS_DEV_ID_NOT_SORTED;
   } else {
-    // Positions are the working set's block slices in slice order; when they
-    // are whole blocks from row 0 (the persistent-slot layout) position
-    // id / block_size holds the row, so a search is only needed when that
-    // guess misses (a short tail block earlier in the working set).
-    const int g = static_cast<int>(min64(id / block_size, n_pos - 1));
-    if (__ldg(pos_start + g) <= id && id < __ldg(pos_end + g)) {
-      p = g;
-    } else {
-      p = upper_bound_i64(pos_end, n_pos, id);
-      if (p >= n_pos || __ldg(pos_start + p) > id) code = TGS_DEV_ID_NOT_RESIDENT;
-    }
+    p = find_position(pos_start, pos_end, n_pos, block_size, id);
+    if (p >= n_pos || __ldg(pos_start + p) > id) code = TGS_DEV_ID_NOT_RESIDENT;
   }
   if (code != TGS_DEV_OK) {
     report_error(err, code, i);
@@ -257,7 +263,7 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
 
     if (lane < nr) {
       const int64_t id = a.ids[row0 + lane];
-      const int p = upper_bound_i64(a.pos_end, a.n_pos, id);
+      const int p = find_position(a.pos_start, a.pos_end, a.n_pos, a.block_size, id);
       const int s = __ldg(a.pos_slot + p);
       const float2 bb = a.slot_bias[s];
       s_addr[warp][lane] = {id, static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p))};
@@ -521,7 +527,7 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
 
     if (lane < nr) {
       const int64_t id = a.ids[row0 + lane];
-      const int p = upper_bound_i64(a.pos_end, a.n_pos, id);
+      const int p = find_position(a.pos_start, a.pos_end, a.n_pos, a.block_size, id);
       const int s = __ldg(a.pos_slot + p);
       const float2 bb = a.slot_bias[s];
       s_addr[warp][lane] = {id, static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p))};

@@ -1019,17 +1019,18 @@ def render_probe(args):
         offs = tr.isect_offset_encode(ids, 1, tw, th)
         marks["intersect"] = torch.cuda.Event(enable_timing=True)
         marks["intersect"].record()
-        m2r = m2.detach().requires_grad_(True)
-        conr = con.detach().requires_grad_(True)
-        colr = colors.detach().requires_grad_(True)
-        opr = opac.detach().requires_grad_(True)
-        rc, ra = tr.rasterize_to_pixels(m2r, conr, colr, opr, Wd, Hd, tile, offs, flat)
+        # the raw kernels, called as the reference arm calls its binding
+        m2d, cond = m2.detach(), con.detach()
+        rc, ra, last = tr.rasterize_to_pixels_fwd(m2d, cond, colors, opac, None, Wd, Hd, tile,
+                                                  offs, flat)
         marks["raster_fwd"] = torch.cuda.Event(enable_timing=True)
         marks["raster_fwd"].record()
-        (rc.sum() + ra.sum()).backward()
+        _, vm, vc, _, _ = tr.rasterize_to_pixels_bwd(m2d, cond, colors, opac, None, Wd, Hd, tile,
+                                                     offs, flat, ra, last, torch.ones_like(rc),
+                                                     torch.ones_like(ra), False)
         marks["raster_bwd"] = torch.cuda.Event(enable_timing=True)
         marks["raster_bwd"].record()
-        torch.autograd.backward([m2, dep, con], [m2r.grad, torch.zeros_like(dep), conr.grad])
+        torch.autograd.backward([m2, dep, con], [vm, torch.zeros_like(dep), vc])
         marks["projection_bwd"] = torch.cuda.Event(enable_timing=True)
         marks["projection_bwd"].record()
         return marks, int(flat.numel())

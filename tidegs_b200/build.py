@@ -41,6 +41,17 @@ NVCC_FLAGS = [
     "-fvisibility=hidden",
     "--expt-relaxed-constexpr",
 ]
+_IEEE_FLAGS = ("-prec-div=true", "-prec-sqrt=true", "-ftz=false")
+# The render path is compared with the reference within tolerance and the
+# reference builds it with fast math (gsplat setup.py:81); every other file
+# keeps IEEE rounding (bit-exact parity).
+FAST_MATH_SOURCES = ("tgs_render.cu",)
+
+
+def _flags(name: str) -> list[str]:
+    if name in FAST_MATH_SOURCES:
+        return [f for f in NVCC_FLAGS if f not in _IEEE_FLAGS] + ["--use_fast_math"]
+    return list(NVCC_FLAGS)
 
 
 def nvcc_path() -> str:
@@ -62,8 +73,8 @@ def _stale(target: Path, deps: list[Path]) -> bool:
 
 
 def _compile(nvcc: str, src: Path, obj: Path, extra: list[str], verbose: bool) -> None:
-    cmd = [nvcc, *ARCH_FLAGS, *NVCC_FLAGS, *extra, f"-I{INCLUDE}", f"-I{CSRC}", "-c", str(src),
-           "-o", str(obj)]
+    cmd = [nvcc, *ARCH_FLAGS, *_flags(src.name), *extra, f"-I{INCLUDE}", f"-I{CSRC}", "-c",
+           str(src), "-o", str(obj)]
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -21,7 +21,8 @@ import torch
 
 from . import _lib
 
-__all__ = ["fully_fused_projection", "isect_tiles", "isect_offset_encode", "rasterize_to_pixels"]
+__all__ = ["fully_fused_projection", "isect_tiles", "isect_offset_encode", "rasterize_to_pixels",
+           "rasterize_to_pixels_fwd", "rasterize_to_pixels_bwd"]
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -188,6 +189,46 @@ def _raster_args(means2d, conics, colors, opacities, backgrounds, width, height,
     return a
 
 
+def rasterize_to_pixels_fwd(means2d, conics, colors, opacities, backgrounds, width: int,
+                            height: int, tile_size: int, isect_offsets, flatten_ids):
+    """(render_colors [C,H,W,D], render_alphas [C,H,W,1], last_ids [C,H,W]):
+    the forward kernel alone, on contiguous float32 / int32 CUDA tensors
+    (gsplat's rasterize_to_pixels_fwd binding)."""
+    C, D = int(isect_offsets.shape[0]), int(colors.shape[-1])
+    dev = means2d.device
+    render_colors = torch.empty((C, height, width, D), dtype=torch.float32, device=dev)
+    render_alphas = torch.empty((C, height, width, 1), dtype=torch.float32, device=dev)
+    last_ids = torch.empty((C, height, width), dtype=torch.int32, device=dev)
+    args = _raster_args(means2d, conics, colors, opacities, backgrounds, width, height, tile_size,
+                        isect_offsets, flatten_ids, render_colors, render_alphas, last_ids)
+    _lib.call("tgs_rasterize_fwd", args, _stream(means2d))
+    return render_colors, render_alphas, last_ids
+
+
+def rasterize_to_pixels_bwd(means2d, conics, colors, opacities, backgrounds, width: int,
+                            height: int, tile_size: int, isect_offsets, flatten_ids, render_alphas,
+                            last_ids, v_render_colors, v_render_alphas, absgrad: bool):
+    """(v_means2d_abs or None, v_means2d, v_conics, v_colors, v_opacities):
+    the backward kernel alone, on contiguous float32 / int32 CUDA tensors
+    (gsplat's rasterize_to_pixels_bwd binding)."""
+    dev = means2d.device
+    v_means2d = torch.zeros_like(means2d)
+    v_conics = torch.zeros_like(conics)
+    v_colors = torch.zeros_like(colors)
+    v_opac = torch.zeros_like(opacities)
+    v_abs = torch.zeros_like(means2d) if absgrad else None
+    b = _lib.RasterBwdArgs()
+    b.fwd = _raster_args(means2d, conics, colors, opacities, backgrounds, width, height, tile_size,
+                         isect_offsets, flatten_ids, torch.empty(0, device=dev), render_alphas,
+                         last_ids)
+    b.v_render_colors, b.v_render_alphas = v_render_colors.data_ptr(), v_render_alphas.data_ptr()
+    b.v_means2d_abs = _ptr(v_abs)
+    b.v_means2d, b.v_conics, b.v_colors, b.v_opacities = (v_means2d.data_ptr(), v_conics.data_ptr(),
+                                                          v_colors.data_ptr(), v_opac.data_ptr())
+    _lib.call("tgs_rasterize_bwd", b, _stream(means2d))
+    return v_abs, v_means2d, v_conics, v_colors, v_opac
+
+
 class _Rasterize(torch.autograd.Function):
     @staticmethod
     def forward(ctx, means2d, conics, colors, opacities, backgrounds, width, height, tile_size,
@@ -197,14 +238,8 @@ class _Rasterize(torch.autograd.Function):
         bg_ = None if backgrounds is None else _f32(backgrounds, "backgrounds")
         offsets = isect_offsets.detach().to(torch.int32).contiguous()
         flat = flatten_ids.detach().to(torch.int32).contiguous()
-        C, D = int(offsets.shape[0]), int(colors_.shape[-1])
-        dev = means2d_.device
-        render_colors = torch.empty((C, height, width, D), dtype=torch.float32, device=dev)
-        render_alphas = torch.empty((C, height, width, 1), dtype=torch.float32, device=dev)
-        last_ids = torch.empty((C, height, width), dtype=torch.int32, device=dev)
-        args = _raster_args(means2d_, conics_, colors_, opac_, bg_, width, height, tile_size,
-                            offsets, flat, render_colors, render_alphas, last_ids)
-        _lib.call("tgs_rasterize_fwd", args, _stream(means2d_))
+        render_colors, render_alphas, last_ids = rasterize_to_pixels_fwd(
+            means2d_, conics_, colors_, opac_, bg_, width, height, tile_size, offsets, flat)
         ctx.save_for_backward(means2d_, conics_, colors_, opac_, bg_, offsets, flat,
                               render_alphas, last_ids)
         ctx.shape = (width, height, tile_size, absgrad)
@@ -220,20 +255,9 @@ class _Rasterize(torch.autograd.Function):
                 if v_render_colors is None else v_render_colors.to(torch.float32).contiguous())
         v_ra = (torch.zeros_like(render_alphas) if v_render_alphas is None
                 else v_render_alphas.to(torch.float32).contiguous())
-        v_means2d = torch.zeros_like(means2d)
-        v_conics = torch.zeros_like(conics)
-        v_colors = torch.zeros_like(colors)
-        v_opac = torch.zeros_like(opac)
-        v_abs = torch.zeros_like(means2d) if absgrad else None
-        b = _lib.RasterBwdArgs()
-        b.fwd = _raster_args(means2d, conics, colors, opac, bg, width, height, tile_size, offsets,
-                             flat, torch.empty(0, device=dev), render_alphas, last_ids)
-        b.v_render_colors, b.v_render_alphas = v_rc.data_ptr(), v_ra.data_ptr()
-        b.v_means2d_abs = _ptr(v_abs)
-        b.v_means2d, b.v_conics, b.v_colors, b.v_opacities = (v_means2d.data_ptr(),
-                                                              v_conics.data_ptr(),
-                                                              v_colors.data_ptr(), v_opac.data_ptr())
-        _lib.call("tgs_rasterize_bwd", b, _stream(means2d))
+        v_abs, v_means2d, v_conics, v_colors, v_opac = rasterize_to_pixels_bwd(
+            means2d, conics, colors, opac, bg, width, height, tile_size, offsets, flat,
+            render_alphas, last_ids, v_rc, v_ra, absgrad)
         if absgrad:
             ctx.means2d_input.absgrad = v_abs
         v_bg = None

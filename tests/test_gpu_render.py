@@ -146,6 +146,43 @@ def test_intersections_match_reference_exactly():
     assert torch.equal(offsets, ref.isect_offset_encode(r_ids, 3, tw, th))
 
 
+def test_intersection_order_with_depth_ties_and_negative_depths():
+    """Equal depths keep Gaussian order inside a tile; negative depths (and
+    -0.0) sign-extend into the reference key and sort as its all-ones
+    (camera, tile) bits. Checked against the reference's rule restated here
+    (a stable sort of the written keys by their low 32 + tile + camera bits)
+    and against the reference kernels."""
+    from tidegs_b200.render import isect_tiles
+
+    C, N = 3, 6000
+    tw, th = (W + TILE - 1) // TILE, (H + TILE - 1) // TILE
+    g = torch.Generator().manual_seed(11)
+    means2d = (torch.rand((C, N, 2), generator=g) * torch.tensor([W * 1.2, H * 1.2])
+               - torch.tensor([W * 0.1, H * 0.1])).cuda()
+    radii = torch.randint(0, 40, (C, N), generator=g, dtype=torch.int32)
+    radii[torch.rand((C, N), generator=g) < 0.2] = 0
+    levels = torch.tensor([0.5, 1.0, 1.0, 2.5, 7.0, -0.0, -1.5, 3.0e-38, float("inf")])
+    depths = levels[torch.randint(0, levels.numel(), (C, N), generator=g)].cuda()
+    radii = radii.cuda()
+    tiles, ids, flat = isect_tiles(means2d, radii, depths, TILE, tw, th)
+    u_tiles, u_ids, u_flat = isect_tiles(means2d, radii, depths, TILE, tw, th, sort=False)
+    assert torch.equal(tiles, u_tiles) and ids.numel() == u_ids.numel() > 10000
+    bits = 32 + (int(np.floor(np.log2(tw * th))) + 1) + (int(np.floor(np.log2(C))) + 1)
+    order = torch.sort(u_ids & ((1 << bits) - 1), stable=True).indices
+    assert torch.equal(ids, u_ids[order])
+    assert torch.equal(flat, u_flat[order])
+    assert bool((ids < 0).any()), "no negative-depth keys were made"
+    ref = _ref()
+    if ref is None:
+        pytest.skip("reference gsplat kernels not built")
+    r_tiles, r_ids, r_flat = ref.isect_tiles(means2d, radii, depths, None, None, C, TILE, tw, th,
+                                             True, True)
+    assert torch.equal(ids, r_ids) and torch.equal(flat, r_flat)
+    r_tiles, r_ids, r_flat = ref.isect_tiles(means2d, radii, depths, None, None, C, TILE, tw, th,
+                                             False, True)
+    assert torch.equal(u_ids, r_ids) and torch.equal(u_flat, r_flat)
+
+
 def _render_inputs(N, C, seed, w=W, h=H):
     means, quats, scales, opac, colors, views, Ks = _scene(N, C, seed, w, h)
     m, q, s, v, k = _cuda32(means, quats, scales, views, Ks)

@@ -25,6 +25,8 @@
 
 #include "tgs_common.cuh"
 
+#include <cub/device/device_radix_sort.cuh>
+
 namespace tgs {
 namespace {
 
@@ -369,6 +371,63 @@ __global__ void isect_write_kernel(const float* __restrict__ means2d, const int3
       flatten[out] = static_cast<int32_t>(i);
       ++out;
     }
+}
+
+// Depth-ordered intersection (the sort that is not a 64-bit key sort).
+// The reference sorts keys camera | tile | depth bits with cub over their
+// low 32 + tile_bits + camera_bits bits, stably: within one (camera, tile)
+// the entries come by the depth's bits (as an unsigned number), then in
+// write order (Gaussian index). The same order results from
+//   1. a stable sort of all C*N Gaussians by the depth bits (C*N items),
+//   2. emitting each Gaussian's tiles in that order with the 32-bit key
+//      bits [32, 32 + tile_bits + camera_bits) of its reference key,
+//   3. a stable sort of those keys (tile_bits + camera_bits bits),
+// after which the reference's 64-bit keys are put back (expand). A negative
+// depth sign-extends into the reference key, whose bits 32 and up are then
+// all ones: such entries get the all-ones key here, as they do there.
+__global__ void iota_kernel(int32_t* __restrict__ out, int64_t n) {
+  const int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (i < n) out[i] = static_cast<int32_t>(i);
+}
+
+__global__ void isect_write_ordered_kernel(const float* __restrict__ means2d,
+                                           const int32_t* __restrict__ radii,
+                                           const float* __restrict__ depths,
+                                           const int32_t* __restrict__ order, int64_t n,
+                                           int64_t per_camera, int tile_size, int tile_width,
+                                           int tile_height, int tile_bits, uint32_t key_mask,
+                                           const int64_t* __restrict__ cum,
+                                           uint32_t* __restrict__ tile_keys,
+                                           int32_t* __restrict__ flatten) {
+  const int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (j >= n) return;
+  const int32_t i = order[j];
+  const int32_t r = radii[i];
+  if (r <= 0) return;
+  const TileRect t = tile_rect(means2d[2 * static_cast<int64_t>(i)],
+                               means2d[2 * static_cast<int64_t>(i) + 1], static_cast<float>(r),
+                               tile_size, tile_width, tile_height);
+  const bool negative = __float_as_int(depths[i]) < 0;
+  const uint32_t hi = static_cast<uint32_t>(i / per_camera) << tile_bits;
+  int64_t out = j == 0 ? 0 : cum[j - 1];
+  for (int y = t.y0; y < t.y1; ++y)
+    for (int x = t.x0; x < t.x1; ++x) {
+      tile_keys[out] = negative ? key_mask : (hi | static_cast<uint32_t>(y * tile_width + x));
+      flatten[out] = i;
+      ++out;
+    }
+}
+
+__global__ void isect_expand_kernel(const uint32_t* __restrict__ tile_keys,
+                                    const int32_t* __restrict__ flatten,
+                                    const float* __restrict__ depths, int64_t n,
+                                    int64_t* __restrict__ keys) {
+  const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  if (k >= n) return;
+  const int32_t d = __float_as_int(depths[flatten[k]]);
+  keys[k] = d < 0 ? static_cast<int64_t>(d)
+                  : static_cast<int64_t>((static_cast<uint64_t>(tile_keys[k]) << 32) |
+                                         static_cast<uint32_t>(d));
 }
 
 // offsets[k] = number of keys whose (camera, tile) index is below k.
@@ -729,6 +788,125 @@ extern "C" int tgs_isect_write(const float* means2d, const int32_t* radii, const
   isect_write_kernel<<<static_cast<unsigned>(ceil_div<int64_t>(n, 256)), 256, 0, as_stream(stream)>>>(
       means2d, radii, depths, n, n_per_camera, tile_size, tile_width, tile_height, tile_bits,
       cum_tiles, isect_ids, flatten_ids);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+namespace {
+constexpr size_t kScratchAlign = 256;
+size_t align_up(size_t v) { return (v + kScratchAlign - 1) / kScratchAlign * kScratchAlign; }
+
+int isect_key_bits(int64_t n_cameras, int32_t n_tiles) {
+  return tgs_isect_tile_bits(n_tiles) + tgs_isect_tile_bits(static_cast<int32_t>(n_cameras));
+}
+
+// cub's scratch for a stable (uint32 key, int32 value) sort of n items over `bits` bits.
+cudaError_t pair_sort_temp_bytes(int64_t n, int bits, size_t* bytes) {
+  *bytes = 0;
+  return cub::DeviceRadixSort::SortPairs(nullptr, *bytes, static_cast<const uint32_t*>(nullptr),
+                                         static_cast<uint32_t*>(nullptr),
+                                         static_cast<const int32_t*>(nullptr),
+                                         static_cast<int32_t*>(nullptr), static_cast<int>(n), 0,
+                                         bits);
+}
+}  // namespace
+
+extern "C" int tgs_isect_depth_order_scratch_bytes(int64_t n, size_t* bytes) {
+  TGS_CHECK_ARG(bytes && n >= 0 && n < (1ll << 31), "tgs_isect_depth_order_scratch_bytes: bad n");
+  size_t temp = 0;
+  TGS_CUDA(pair_sort_temp_bytes(n, 32, &temp));
+  *bytes = align_up(temp) + 2 * align_up(static_cast<size_t>(n) * 4);
+  return TGS_OK;
+}
+
+extern "C" int tgs_isect_depth_order(const float* depths, int64_t n, int32_t* order, void* scratch,
+                                     size_t scratch_bytes, void* stream) {
+  TGS_CHECK_ARG(n >= 0 && n < (1ll << 31), "tgs_isect_depth_order: bad n");
+  if (n == 0) return TGS_OK;
+  TGS_CHECK_ARG(depths && order && scratch, "tgs_isect_depth_order: NULL pointer");
+  size_t temp = 0;
+  TGS_CUDA(pair_sort_temp_bytes(n, 32, &temp));
+  const size_t need = align_up(temp) + 2 * align_up(static_cast<size_t>(n) * 4);
+  TGS_CHECK_ARG(scratch_bytes >= need, "tgs_isect_depth_order: scratch holds %zu bytes, needs %zu",
+                scratch_bytes, need);
+  char* base = static_cast<char*>(scratch);
+  uint32_t* keys_out = reinterpret_cast<uint32_t*>(base + align_up(temp));
+  int32_t* iota = reinterpret_cast<int32_t*>(base + align_up(temp) + align_up(static_cast<size_t>(n) * 4));
+  cudaStream_t s = as_stream(stream);
+  iota_kernel<<<static_cast<unsigned>(ceil_div<int64_t>(n, 256)), 256, 0, s>>>(iota, n);
+  TGS_LAUNCH_CHECK();
+  TGS_CUDA(cub::DeviceRadixSort::SortPairs(base, temp, reinterpret_cast<const uint32_t*>(depths),
+                                           keys_out, iota, order, static_cast<int>(n), 0, 32, s));
+  return TGS_OK;
+}
+
+extern "C" int tgs_isect_write_ordered(const float* means2d, const int32_t* radii,
+                                       const float* depths, const int32_t* order, int64_t n,
+                                       int64_t n_per_camera, int32_t tile_size, int32_t tile_width,
+                                       int32_t tile_height, const int64_t* cum_tiles,
+                                       uint32_t* tile_keys, int32_t* flatten_ids, void* stream) {
+  TGS_CHECK_ARG(n >= 0 && n_per_camera > 0 && tile_size > 0 && tile_width > 0 && tile_height > 0,
+                "tgs_isect_write_ordered: bad sizes");
+  TGS_CHECK_ARG(n < (1ll << 31), "tgs_isect_write_ordered: more than 2^31 projected Gaussians");
+  if (n == 0) return TGS_OK;
+  TGS_CHECK_ARG(means2d && radii && depths && order && cum_tiles && tile_keys && flatten_ids,
+                "tgs_isect_write_ordered: NULL pointer");
+  const int n_tiles = tile_width * tile_height;
+  const int bits = isect_key_bits(ceil_div<int64_t>(n, n_per_camera), n_tiles);
+  TGS_CHECK_ARG(bits <= 32, "tgs_isect_write_ordered: camera and tile ids need %d bits", bits);
+  const uint32_t mask = static_cast<uint32_t>((1ull << bits) - 1);
+  isect_write_ordered_kernel<<<static_cast<unsigned>(ceil_div<int64_t>(n, 256)), 256, 0,
+                               as_stream(stream)>>>(
+      means2d, radii, depths, order, n, n_per_camera, tile_size, tile_width, tile_height,
+      tgs_isect_tile_bits(n_tiles), mask, cum_tiles, tile_keys, flatten_ids);
+  TGS_LAUNCH_CHECK();
+  return TGS_OK;
+}
+
+extern "C" int tgs_isect_sort_tiles_scratch_bytes(int64_t n_isects, int32_t n_cameras,
+                                                  int32_t tile_width, int32_t tile_height,
+                                                  size_t* bytes) {
+  TGS_CHECK_ARG(bytes && n_isects >= 0 && n_isects < (1ll << 31) && n_cameras > 0 &&
+                    tile_width > 0 && tile_height > 0,
+                "tgs_isect_sort_tiles_scratch_bytes: bad sizes");
+  size_t temp = 0;
+  TGS_CUDA(pair_sort_temp_bytes(n_isects, isect_key_bits(n_cameras, tile_width * tile_height),
+                                &temp));
+  *bytes = temp;
+  return TGS_OK;
+}
+
+extern "C" int tgs_isect_sort_tiles(const uint32_t* tile_keys_in, const int32_t* flatten_in,
+                                    int64_t n_isects, int32_t n_cameras, int32_t tile_width,
+                                    int32_t tile_height, uint32_t* tile_keys_out,
+                                    int32_t* flatten_out, void* scratch, size_t scratch_bytes,
+                                    void* stream) {
+  TGS_CHECK_ARG(n_isects >= 0 && n_isects < (1ll << 31) && n_cameras > 0 && tile_width > 0 &&
+                    tile_height > 0,
+                "tgs_isect_sort_tiles: bad sizes");
+  if (n_isects == 0) return TGS_OK;
+  TGS_CHECK_ARG(tile_keys_in && flatten_in && tile_keys_out && flatten_out && scratch,
+                "tgs_isect_sort_tiles: NULL pointer");
+  const int bits = isect_key_bits(n_cameras, tile_width * tile_height);
+  TGS_CHECK_ARG(bits <= 32, "tgs_isect_sort_tiles: camera and tile ids need %d bits", bits);
+  size_t temp = 0;
+  TGS_CUDA(pair_sort_temp_bytes(n_isects, bits, &temp));
+  TGS_CHECK_ARG(scratch_bytes >= temp, "tgs_isect_sort_tiles: scratch holds %zu bytes, needs %zu",
+                scratch_bytes, temp);
+  TGS_CUDA(cub::DeviceRadixSort::SortPairs(scratch, temp, tile_keys_in, tile_keys_out, flatten_in,
+                                           flatten_out, static_cast<int>(n_isects), 0, bits,
+                                           as_stream(stream)));
+  return TGS_OK;
+}
+
+extern "C" int tgs_isect_expand_ids(const uint32_t* tile_keys, const int32_t* flatten_ids,
+                                    const float* depths, int64_t n_isects, int64_t* isect_ids,
+                                    void* stream) {
+  TGS_CHECK_ARG(n_isects >= 0, "tgs_isect_expand_ids: bad n_isects");
+  if (n_isects == 0) return TGS_OK;
+  TGS_CHECK_ARG(tile_keys && flatten_ids && depths && isect_ids, "tgs_isect_expand_ids: NULL pointer");
+  isect_expand_kernel<<<static_cast<unsigned>(ceil_div<int64_t>(n_isects, 256)), 256, 0,
+                        as_stream(stream)>>>(tile_keys, flatten_ids, depths, n_isects, isect_ids);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

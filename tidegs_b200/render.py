@@ -5,9 +5,10 @@ the four calls the engine makes (strategies/tide_engine/engine.py:481-561):
 `from tidegs_b200.render import ...` replaces `from gsplat import ...`.
 
 Kernels: tgs_project_fwd/bwd, tgs_isect_count/write/offsets,
-tgs_rasterize_fwd/bwd (libtidegs_b200.so). The intersection keys are sorted
-with torch's stable radix sort (a library sort, like gsplat's cub sort; the
-stable order keeps equal keys in Gaussian order, as cub's does).
+tgs_rasterize_fwd/bwd (libtidegs_b200.so). The sorted intersections come
+from a stable sort of the Gaussians by depth and a stable sort of 32-bit
+(camera, tile) keys (cub radix sorts, as gsplat sorts with cub) instead of
+one sort of 64-bit keys; keys, flatten ids and their order are gsplat's.
 
 Supported: gsplat's non-packed layout ([C, N, ...]), Gaussians given by
 quats + scales, 1-4 color channels, no camera-pose gradients. Other options
@@ -15,6 +16,7 @@ raise (the engine uses none of them).
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Tuple
 
 import torch
@@ -143,18 +145,48 @@ def isect_tiles(means2d: torch.Tensor, radii: torch.Tensor, depths: torch.Tensor
     s = _stream(means2d_)
     _lib.call("tgs_isect_count", means2d_.data_ptr(), radii_.data_ptr(), n, int(tile_size),
               int(tile_width), int(tile_height), tiles.data_ptr(), s)
-    cum = torch.cumsum(tiles.view(-1), 0)
-    n_isects = int(cum[-1].item()) if n else 0
+    if not sort or n == 0:
+        cum = torch.cumsum(tiles.view(-1), 0)
+        n_isects = int(cum[-1].item()) if n else 0
+        isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
+        flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+        if n_isects:
+            _lib.call("tgs_isect_write", means2d_.data_ptr(), radii_.data_ptr(),
+                      depths_.data_ptr(), n, N, int(tile_size), int(tile_width),
+                      int(tile_height), cum.data_ptr(), isect_ids.data_ptr(),
+                      flatten_ids.data_ptr(), s)
+        return tiles, isect_ids, flatten_ids
+    # sorted: Gaussians in depth order, their tiles emitted in that order with
+    # 32-bit (camera, tile) keys, a stable sort of those, 64-bit keys put back
+    order = torch.empty(n, dtype=torch.int32, device=dev)
+    scratch = _scratch(dev, "tgs_isect_depth_order_scratch_bytes", n)
+    _lib.call("tgs_isect_depth_order", depths_.data_ptr(), n, order.data_ptr(),
+              scratch.data_ptr(), scratch.numel(), s)
+    cum = torch.cumsum(tiles.view(-1)[order], 0)
+    n_isects = int(cum[-1].item())
     isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
     flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
     if n_isects:
-        _lib.call("tgs_isect_write", means2d_.data_ptr(), radii_.data_ptr(), depths_.data_ptr(), n,
-                  N, int(tile_size), int(tile_width), int(tile_height), cum.data_ptr(),
-                  isect_ids.data_ptr(), flatten_ids.data_ptr(), s)
-        if sort:
-            isect_ids, order = torch.sort(isect_ids, stable=True)
-            flatten_ids = flatten_ids[order]
+        keys = torch.empty(n_isects, dtype=torch.int32, device=dev)
+        unsorted_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
+        _lib.call("tgs_isect_write_ordered", means2d_.data_ptr(), radii_.data_ptr(),
+                  depths_.data_ptr(), order.data_ptr(), n, N, int(tile_size), int(tile_width),
+                  int(tile_height), cum.data_ptr(), keys.data_ptr(), unsorted_ids.data_ptr(), s)
+        sorted_keys = torch.empty_like(keys)
+        scratch = _scratch(dev, "tgs_isect_sort_tiles_scratch_bytes", n_isects, C,
+                           int(tile_width), int(tile_height))
+        _lib.call("tgs_isect_sort_tiles", keys.data_ptr(), unsorted_ids.data_ptr(), n_isects, C,
+                  int(tile_width), int(tile_height), sorted_keys.data_ptr(),
+                  flatten_ids.data_ptr(), scratch.data_ptr(), scratch.numel(), s)
+        _lib.call("tgs_isect_expand_ids", sorted_keys.data_ptr(), flatten_ids.data_ptr(),
+                  depths_.data_ptr(), n_isects, isect_ids.data_ptr(), s)
     return tiles, isect_ids, flatten_ids
+
+
+def _scratch(dev: torch.device, query: str, *sizes) -> torch.Tensor:
+    nbytes = ctypes.c_size_t(0)
+    _lib.call(query, *sizes, ctypes.byref(nbytes))
+    return torch.empty(max(int(nbytes.value), 1), dtype=torch.uint8, device=dev)
 
 
 def isect_offset_encode(isect_ids: torch.Tensor, n_cameras: int, tile_width: int,

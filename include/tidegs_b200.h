@@ -649,37 +649,42 @@ TGS_API int tgs_isect_write(const float* means2d, const int32_t* radii, const fl
 /* The sorted keys of isect_tiles.cu:170-224 (cub sort of the keys' low
  * 32 + tile_bits + camera_bits bits, stable) without a 64-bit key sort:
  *   tgs_isect_depth_order   order[] = the n = C*N Gaussians stably sorted
- *                           by their depth bits (unsigned);
- *   tgs_isect_write_ordered each Gaussian's tiles in that order, at the
- *                           inclusive prefix sums cum_tiles of
- *                           tiles_per_gauss[order[]], as 32-bit keys
+ *                           by their depth bits (unsigned), and cum_tiles[]
+ *                           = inclusive prefix sums of
+ *                           tiles_per_gauss[order[]] (int64);
+ *   tgs_isect_write_ordered each Gaussian's tiles in that order as keys
  *                           camera << tile_bits | tile (all ones for a
  *                           negative depth, as the sign-extended reference
  *                           key has) and flat Gaussian ids;
  *   tgs_isect_sort_tiles    stable sort of those keys (tile_bits +
  *                           camera_bits bits);
  *   tgs_isect_expand_ids    the reference's 64-bit keys from the sorted
- *                           32-bit keys and the depths.
- * Keys, flatten ids and their order equal the reference's. Scratch is the
- * caller's device memory of the size the *_scratch_bytes calls return. */
+ *                           keys and the depths.
+ * Keys are tgs_isect_key_bytes(...) wide: 2 (uint16) when tile_bits +
+ * camera_bits <= 16, else 4 (uint32); 0 means the ids need more than 32
+ * bits. Keys, flatten ids and their order equal the reference's. Scratch
+ * is the caller's device memory of the size the *_scratch_bytes calls
+ * return; expand wants its arrays on 16-byte boundaries. */
+TGS_API int32_t tgs_isect_key_bytes(int32_t n_cameras, int32_t tile_width, int32_t tile_height);
 TGS_API int tgs_isect_depth_order_scratch_bytes(int64_t n, size_t* bytes);
-TGS_API int tgs_isect_depth_order(const float* depths, int64_t n, int32_t* order, void* scratch,
+TGS_API int tgs_isect_depth_order(const float* depths, const int32_t* tiles_per_gauss, int64_t n,
+                          int32_t* order, int64_t* cum_tiles, void* scratch,
                           size_t scratch_bytes, void* stream);
 TGS_API int tgs_isect_write_ordered(const float* means2d, const int32_t* radii,
                             const float* depths, const int32_t* order, int64_t n,
                             int64_t n_per_camera, int32_t tile_size, int32_t tile_width,
-                            int32_t tile_height, const int64_t* cum_tiles,
-                            uint32_t* tile_keys, int32_t* flatten_ids, void* stream);
+                            int32_t tile_height, const int64_t* cum_tiles, void* tile_keys,
+                            int32_t* flatten_ids, void* stream);
 TGS_API int tgs_isect_sort_tiles_scratch_bytes(int64_t n_isects, int32_t n_cameras,
                                        int32_t tile_width, int32_t tile_height,
                                        size_t* bytes);
-TGS_API int tgs_isect_sort_tiles(const uint32_t* tile_keys_in, const int32_t* flatten_in,
+TGS_API int tgs_isect_sort_tiles(const void* tile_keys_in, const int32_t* flatten_in,
                          int64_t n_isects, int32_t n_cameras, int32_t tile_width,
-                         int32_t tile_height, uint32_t* tile_keys_out, int32_t* flatten_out,
+                         int32_t tile_height, void* tile_keys_out, int32_t* flatten_out,
                          void* scratch, size_t scratch_bytes, void* stream);
-TGS_API int tgs_isect_expand_ids(const uint32_t* tile_keys, const int32_t* flatten_ids,
-                         const float* depths, int64_t n_isects, int64_t* isect_ids,
-                         void* stream);
+TGS_API int tgs_isect_expand_ids(const void* tile_keys, int32_t key_bytes,
+                         const int32_t* flatten_ids, const float* depths, int64_t n_isects,
+                         int64_t* isect_ids, void* stream);
 /* offsets[c, tile] = index of the first sorted key of (c, tile)
  * (isect_offset_encode, isect_tiles.cu:227-280). */
 TGS_API int tgs_isect_offsets(const int64_t* isect_ids, int64_t n_isects, int32_t n_cameras,

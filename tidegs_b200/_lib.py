@@ -231,14 +231,15 @@ SIGNATURES = {
     "tgs_isect_write": (C.c_int, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp,
                                   _vp]),
     "tgs_isect_depth_order_scratch_bytes": (C.c_int, [_i64, C.POINTER(C.c_size_t)]),
-    "tgs_isect_depth_order": (C.c_int, [_vp, _i64, _vp, _vp, C.c_size_t, _vp]),
+    "tgs_isect_key_bytes": (_i32, [_i32, _i32, _i32]),
+    "tgs_isect_depth_order": (C.c_int, [_vp, _vp, _i64, _vp, _vp, _vp, C.c_size_t, _vp]),
     "tgs_isect_write_ordered": (C.c_int, [_vp, _vp, _vp, _vp, _i64, _i64, _i32, _i32, _i32, _vp,
                                           _vp, _vp, _vp]),
     "tgs_isect_sort_tiles_scratch_bytes": (C.c_int, [_i64, _i32, _i32, _i32,
                                                      C.POINTER(C.c_size_t)]),
     "tgs_isect_sort_tiles": (C.c_int, [_vp, _vp, _i64, _i32, _i32, _i32, _vp, _vp, _vp,
                                        C.c_size_t, _vp]),
-    "tgs_isect_expand_ids": (C.c_int, [_vp, _vp, _vp, _i64, _vp, _vp]),
+    "tgs_isect_expand_ids": (C.c_int, [_vp, _i32, _vp, _vp, _i64, _vp, _vp]),
     "tgs_isect_offsets": (C.c_int, [_vp, _i64, _i32, _i32, _i32, _vp, _vp]),
     "tgs_rasterize_fwd": (C.c_int, [C.POINTER(RasterArgs), _vp]),
     "tgs_rasterize_bwd": (C.c_int, [C.POINTER(RasterBwdArgs), _vp]),
@@ -294,8 +295,8 @@ KERNELS_PER_CALL = {
     "tgs_project_fwd": 1, "tgs_project_bwd": 1, "tgs_isect_count": 1, "tgs_isect_write": 1,
     "tgs_isect_offsets": 1, "tgs_rasterize_fwd": 1, "tgs_rasterize_bwd": 1,
     "tgs_isect_write_ordered": 1, "tgs_isect_expand_ids": 1,
-    # iota + the library radix sort (histogram, one pass per 8 key bits; the
-    # count depends on the library version and is not counted here)
+    # iota + the library radix sort and scan (their kernel counts depend on
+    # the library version and are not counted here)
     "tgs_isect_depth_order": 1, "tgs_isect_sort_tiles": 0,
 }
 launch_counter = {"kernels": 0}

@@ -25,9 +25,24 @@
 
 #include "tgs_common.cuh"
 
+#include <algorithm>
+
 #include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
+#include <thrust/iterator/counting_iterator.h>
+#include <thrust/iterator/transform_iterator.h>
 
 namespace tgs {
+// Tiles of the j-th Gaussian in depth order, as a 64-bit value for the scan
+// (a named namespace: it is a template argument of the library's kernels).
+struct OrderedTileCount {
+  const int32_t* tiles;
+  const int32_t* order;
+  __host__ __device__ int64_t operator()(int64_t j) const {
+    return static_cast<int64_t>(tiles[order[j]]);
+  }
+};
+
 namespace {
 
 constexpr int kProjThreads = 256;
@@ -149,7 +164,8 @@ __global__ void __launch_bounds__(kProjThreads) project_fwd_kernel(const TgsProj
   // cov2d = J cov_c J^T (J is 2x3 with J01 = J10 = 0)
   const float* C3 = G.cov_c;
   const float a0 = J00 * C3[0] + J02 * C3[6], a1 = J00 * C3[1] + J02 * C3[7], a2 = J00 * C3[2] + J02 * C3[8];
-  const float b0 = J11 * C3[3] + J12 * C3[6], b1 = J11 * C3[4] + J12 * C3[7], b2 = J11 * C3[5] + J12 * C3[8];
+  // (the (1, 0) entry equals the (0, 1) entry: cov2d is symmetric)
+  const float b1 = J11 * C3[4] + J12 * C3[7], b2 = J11 * C3[5] + J12 * C3[8];
   float c00 = a0 * J00 + a2 * J02;
   const float c01 = a1 * J11 + a2 * J12;
   float c11 = b1 * J11 + b2 * J12;
@@ -379,8 +395,9 @@ __global__ void isect_write_kernel(const float* __restrict__ means2d, const int3
 // the entries come by the depth's bits (as an unsigned number), then in
 // write order (Gaussian index). The same order results from
 //   1. a stable sort of all C*N Gaussians by the depth bits (C*N items),
-//   2. emitting each Gaussian's tiles in that order with the 32-bit key
-//      bits [32, 32 + tile_bits + camera_bits) of its reference key,
+//   2. emitting each Gaussian's tiles in that order with the key bits
+//      [32, 32 + tile_bits + camera_bits) of its reference key (16-bit keys
+//      when those are at most 16 bits, else 32-bit),
 //   3. a stable sort of those keys (tile_bits + camera_bits bits),
 // after which the reference's 64-bit keys are put back (expand). A negative
 // depth sign-extends into the reference key, whose bits 32 and up are then
@@ -390,6 +407,10 @@ __global__ void iota_kernel(int32_t* __restrict__ out, int64_t n) {
   if (i < n) out[i] = static_cast<int32_t>(i);
 }
 
+// One warp writes the tiles of its 32 Gaussians one Gaussian after another,
+// the lanes covering consecutive entries (coalesced, and a Gaussian with
+// many tiles is spread over the warp instead of one thread).
+template <typename KeyT>
 __global__ void isect_write_ordered_kernel(const float* __restrict__ means2d,
                                            const int32_t* __restrict__ radii,
                                            const float* __restrict__ depths,
@@ -397,37 +418,93 @@ __global__ void isect_write_ordered_kernel(const float* __restrict__ means2d,
                                            int64_t per_camera, int tile_size, int tile_width,
                                            int tile_height, int tile_bits, uint32_t key_mask,
                                            const int64_t* __restrict__ cum,
-                                           uint32_t* __restrict__ tile_keys,
+                                           KeyT* __restrict__ tile_keys,
                                            int32_t* __restrict__ flatten) {
+  constexpr unsigned kAll = 0xffffffffu;
   const int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  if (j >= n) return;
-  const int32_t i = order[j];
-  const int32_t r = radii[i];
-  if (r <= 0) return;
-  const TileRect t = tile_rect(means2d[2 * static_cast<int64_t>(i)],
-                               means2d[2 * static_cast<int64_t>(i) + 1], static_cast<float>(r),
-                               tile_size, tile_width, tile_height);
-  const bool negative = __float_as_int(depths[i]) < 0;
-  const uint32_t hi = static_cast<uint32_t>(i / per_camera) << tile_bits;
-  int64_t out = j == 0 ? 0 : cum[j - 1];
-  for (int y = t.y0; y < t.y1; ++y)
-    for (int x = t.x0; x < t.x1; ++x) {
-      tile_keys[out] = negative ? key_mask : (hi | static_cast<uint32_t>(y * tile_width + x));
-      flatten[out] = i;
-      ++out;
+  const int lane = threadIdx.x & 31;
+  int32_t i = 0;
+  int count = 0, x0 = 0, y0 = 0, w = 1;
+  uint32_t hi = 0;
+  int64_t out = 0;
+  if (j < n) {
+    i = order[j];
+    const int32_t r = radii[i];
+    if (r > 0) {
+      const TileRect t = tile_rect(means2d[2 * static_cast<int64_t>(i)],
+                                   means2d[2 * static_cast<int64_t>(i) + 1],
+                                   static_cast<float>(r), tile_size, tile_width, tile_height);
+      count = (t.y1 - t.y0) * (t.x1 - t.x0);
+      x0 = t.x0;
+      y0 = t.y0;
+      w = max(t.x1 - t.x0, 1);
+      // all ones for a negative depth (the sign-extended reference key)
+      hi = __float_as_int(depths[i]) < 0 ? key_mask
+                                         : static_cast<uint32_t>(i / per_camera) << tile_bits;
+      out = j == 0 ? 0 : cum[j - 1];
     }
+  }
+  unsigned todo = __ballot_sync(kAll, count > 0);
+  while (todo) {
+    const int src = __ffs(todo) - 1;
+    todo &= todo - 1;
+    const int c = __shfl_sync(kAll, count, src);
+    const int sw = __shfl_sync(kAll, w, src);
+    const int sx = __shfl_sync(kAll, x0, src);
+    const int sy = __shfl_sync(kAll, y0, src);
+    const uint32_t sh = __shfl_sync(kAll, hi, src);
+    const int32_t sg = __shfl_sync(kAll, i, src);
+    const int64_t so = __shfl_sync(kAll, out, src);
+    const bool all_ones = sh == key_mask;
+    for (int e = lane; e < c; e += 32) {
+      const int row = e / sw;
+      const uint32_t tile = static_cast<uint32_t>((sy + row) * tile_width + sx + (e - row * sw));
+      tile_keys[so + e] = static_cast<KeyT>(all_ones ? key_mask : (sh | tile));
+      flatten[so + e] = sg;
+    }
+  }
 }
 
-__global__ void isect_expand_kernel(const uint32_t* __restrict__ tile_keys,
+template <typename KeyT>
+__device__ __forceinline__ int64_t expand_key(KeyT key, int32_t d) {
+  return d < 0 ? static_cast<int64_t>(d)
+               : static_cast<int64_t>((static_cast<uint64_t>(key) << 32) | static_cast<uint32_t>(d));
+}
+
+// Four entries per thread (vector loads of keys and ids, two 16-byte stores).
+template <typename KeyT>
+__global__ void isect_expand_kernel(const KeyT* __restrict__ tile_keys,
                                     const int32_t* __restrict__ flatten,
                                     const float* __restrict__ depths, int64_t n,
                                     int64_t* __restrict__ keys) {
-  const int64_t k = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+  const int64_t k = 4 * q;
   if (k >= n) return;
-  const int32_t d = __float_as_int(depths[flatten[k]]);
-  keys[k] = d < 0 ? static_cast<int64_t>(d)
-                  : static_cast<int64_t>((static_cast<uint64_t>(tile_keys[k]) << 32) |
-                                         static_cast<uint32_t>(d));
+  if (k + 4 <= n) {
+    const int4 f = *reinterpret_cast<const int4*>(flatten + k);
+    KeyT kk[4];
+    if constexpr (sizeof(KeyT) == 2) {
+      const uint2 v = *reinterpret_cast<const uint2*>(tile_keys + k);
+      kk[0] = static_cast<KeyT>(v.x & 0xffffu);
+      kk[1] = static_cast<KeyT>(v.x >> 16);
+      kk[2] = static_cast<KeyT>(v.y & 0xffffu);
+      kk[3] = static_cast<KeyT>(v.y >> 16);
+    } else {
+      const uint4 v = *reinterpret_cast<const uint4*>(tile_keys + k);
+      kk[0] = v.x;
+      kk[1] = v.y;
+      kk[2] = v.z;
+      kk[3] = v.w;
+    }
+    const int32_t d0 = __float_as_int(depths[f.x]), d1 = __float_as_int(depths[f.y]);
+    const int32_t d2 = __float_as_int(depths[f.z]), d3 = __float_as_int(depths[f.w]);
+    longlong2* dst = reinterpret_cast<longlong2*>(keys + k);
+    dst[0] = make_longlong2(expand_key(kk[0], d0), expand_key(kk[1], d1));
+    dst[1] = make_longlong2(expand_key(kk[2], d2), expand_key(kk[3], d3));
+  } else {
+    for (int64_t e = k; e < n; ++e)
+      keys[e] = expand_key(tile_keys[e], __float_as_int(depths[flatten[e]]));
+  }
 }
 
 // offsets[k] = number of keys whose (camera, tile) index is below k.
@@ -534,10 +611,26 @@ __global__ void raster_fwd_kernel(const TgsRasterArgs a) {
   }
 }
 
-__device__ __forceinline__ float warp_sum(float v) {
+// Warp reduce-scatter of 16 values: afterwards lane L holds the warp total
+// of value L >> 1 (lanes L and L ^ 1 hold the same total). Each halving
+// step sends half of the lane's values to its partner and keeps the other
+// half: 8 + 4 + 2 + 1 + 1 = 16 shuffles for all 16 totals, where 16
+// separate butterfly sums take 80.
+__device__ __forceinline__ float warp_reduce_scatter16(const float (&v)[16], int lane) {
+  constexpr unsigned kAll = 0xffffffffu;
+  float w8[8], w4[4], w2[2];
+  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4, u2 = lane & 2;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
+  for (int k = 0; k < 8; ++k)
+    w8[k] = (u16 ? v[k + 8] : v[k]) + __shfl_xor_sync(kAll, u16 ? v[k] : v[k + 8], 16);
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    w4[k] = (u8 ? w8[k + 4] : w8[k]) + __shfl_xor_sync(kAll, u8 ? w8[k] : w8[k + 4], 8);
+#pragma unroll
+  for (int k = 0; k < 2; ++k)
+    w2[k] = (u4 ? w4[k + 2] : w4[k]) + __shfl_xor_sync(kAll, u4 ? w4[k] : w4[k + 2], 4);
+  float w1 = (u2 ? w2[1] : w2[0]) + __shfl_xor_sync(kAll, u2 ? w2[0] : w2[1], 2);
+  return w1 + __shfl_xor_sync(kAll, w1, 1);
 }
 
 template <int D>
@@ -546,6 +639,7 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
   // per-Gaussian gradient: means2d (2), conic (3), colors (D), opacity,
   // |means2d| (2)
   constexpr int K = 2 + 3 + D + 1 + 2;
+  static_assert(K <= 16, "one reduce-scatter holds 16 values");
   extern __shared__ __align__(16) unsigned char raster_smem[];
   const int nthreads = blockDim.x * blockDim.y;
   int32_t* ids = reinterpret_cast<int32_t*>(raster_smem);
@@ -621,9 +715,9 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
         if (sigma < 0.f || alpha < 1.f / 255.f) valid = false;
       }
       if (!__any_sync(0xffffffffu, valid)) continue;
-      float gv[K];
+      float gv[16];
 #pragma unroll
-      for (int k = 0; k < K; ++k) gv[k] = 0.f;
+      for (int k = 0; k < 16; ++k) gv[k] = 0.f;
       if (valid) {
         // fast reciprocal (the render path is compared within tolerance)
         const float ra = __fdividef(1.f, 1.f - alpha);
@@ -651,22 +745,19 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
 #pragma unroll
         for (int k = 0; k < D; ++k) buffer[k] += rgb[t * D + k] * fac;
       }
-      float sv[K];
-#pragma unroll
-      for (int k = 0; k < K; ++k) sv[k] = (k >= 6 + D && !absgrad) ? 0.f : warp_sum(gv[k]);
-      if (lane == 0) {
+      // lane 2k holds the warp total of gradient component k; the lanes
+      // of the components in use add them to global memory together
+      const float total = warp_reduce_scatter16(gv, lane);
+      const int k = lane >> 1;
+      if ((lane & 1) == 0 && k < (absgrad ? K : K - 2)) {
         const int64_t g = ids[t];
-        atomicAdd(b.v_means2d + 2 * g, sv[0]);
-        atomicAdd(b.v_means2d + 2 * g + 1, sv[1]);
-#pragma unroll
-        for (int k = 0; k < 3; ++k) atomicAdd(b.v_conics + 3 * g + k, sv[2 + k]);
-#pragma unroll
-        for (int k = 0; k < D; ++k) atomicAdd(b.v_colors + D * g + k, sv[5 + k]);
-        atomicAdd(b.v_opacities + g, sv[5 + D]);
-        if (absgrad) {
-          atomicAdd(b.v_means2d_abs + 2 * g, sv[6 + D]);
-          atomicAdd(b.v_means2d_abs + 2 * g + 1, sv[7 + D]);
-        }
+        float* dst;
+        if (k < 2) dst = b.v_means2d + 2 * g + k;
+        else if (k < 5) dst = b.v_conics + 3 * g + (k - 2);
+        else if (k < 5 + D) dst = b.v_colors + D * g + (k - 5);
+        else if (k == 5 + D) dst = b.v_opacities + g;
+        else dst = b.v_means2d_abs + 2 * g + (k - 6 - D);
+        atomicAdd(dst, total);
       }
     }
   }
@@ -800,43 +891,74 @@ int isect_key_bits(int64_t n_cameras, int32_t n_tiles) {
   return tgs_isect_tile_bits(n_tiles) + tgs_isect_tile_bits(static_cast<int32_t>(n_cameras));
 }
 
-// cub's scratch for a stable (uint32 key, int32 value) sort of n items over `bits` bits.
+// cub's scratch for a stable (key, int32 value) sort of n items over `bits` bits.
+template <typename KeyT>
 cudaError_t pair_sort_temp_bytes(int64_t n, int bits, size_t* bytes) {
   *bytes = 0;
-  return cub::DeviceRadixSort::SortPairs(nullptr, *bytes, static_cast<const uint32_t*>(nullptr),
-                                         static_cast<uint32_t*>(nullptr),
+  return cub::DeviceRadixSort::SortPairs(nullptr, *bytes, static_cast<const KeyT*>(nullptr),
+                                         static_cast<KeyT*>(nullptr),
                                          static_cast<const int32_t*>(nullptr),
                                          static_cast<int32_t*>(nullptr), static_cast<int>(n), 0,
                                          bits);
 }
+
+cudaError_t ordered_scan_temp_bytes(int64_t n, size_t* bytes) {
+  *bytes = 0;
+  const auto it = thrust::make_transform_iterator(thrust::counting_iterator<int64_t>(0),
+                                                  OrderedTileCount{nullptr, nullptr});
+  return cub::DeviceScan::InclusiveSum(nullptr, *bytes, it, static_cast<int64_t*>(nullptr),
+                                       static_cast<int>(n));
+}
+
+// Layout of tgs_isect_depth_order's scratch: [temp | keys out (n u32) | iota (n i32)].
+int depth_order_layout(int64_t n, size_t* temp, size_t* total) {
+  size_t sort_temp = 0, scan_temp = 0;
+  TGS_CUDA(pair_sort_temp_bytes<uint32_t>(n, 32, &sort_temp));
+  TGS_CUDA(ordered_scan_temp_bytes(n, &scan_temp));
+  *temp = align_up(std::max(sort_temp, scan_temp));
+  *total = *temp + 2 * align_up(static_cast<size_t>(n) * 4);
+  return TGS_OK;
+}
 }  // namespace
+
+extern "C" int32_t tgs_isect_key_bytes(int32_t n_cameras, int32_t tile_width,
+                                       int32_t tile_height) {
+  if (n_cameras <= 0 || tile_width <= 0 || tile_height <= 0) return 0;
+  const int bits = isect_key_bits(n_cameras, tile_width * tile_height);
+  return bits <= 16 ? 2 : bits <= 32 ? 4 : 0;
+}
 
 extern "C" int tgs_isect_depth_order_scratch_bytes(int64_t n, size_t* bytes) {
   TGS_CHECK_ARG(bytes && n >= 0 && n < (1ll << 31), "tgs_isect_depth_order_scratch_bytes: bad n");
   size_t temp = 0;
-  TGS_CUDA(pair_sort_temp_bytes(n, 32, &temp));
-  *bytes = align_up(temp) + 2 * align_up(static_cast<size_t>(n) * 4);
-  return TGS_OK;
+  return depth_order_layout(n, &temp, bytes);
 }
 
-extern "C" int tgs_isect_depth_order(const float* depths, int64_t n, int32_t* order, void* scratch,
+extern "C" int tgs_isect_depth_order(const float* depths, const int32_t* tiles_per_gauss,
+                                     int64_t n, int32_t* order, int64_t* cum_tiles, void* scratch,
                                      size_t scratch_bytes, void* stream) {
   TGS_CHECK_ARG(n >= 0 && n < (1ll << 31), "tgs_isect_depth_order: bad n");
   if (n == 0) return TGS_OK;
-  TGS_CHECK_ARG(depths && order && scratch, "tgs_isect_depth_order: NULL pointer");
-  size_t temp = 0;
-  TGS_CUDA(pair_sort_temp_bytes(n, 32, &temp));
-  const size_t need = align_up(temp) + 2 * align_up(static_cast<size_t>(n) * 4);
+  TGS_CHECK_ARG(depths && tiles_per_gauss && order && cum_tiles && scratch,
+                "tgs_isect_depth_order: NULL pointer");
+  size_t temp = 0, need = 0;
+  if (depth_order_layout(n, &temp, &need) != TGS_OK) return TGS_ERR_CUDA;
   TGS_CHECK_ARG(scratch_bytes >= need, "tgs_isect_depth_order: scratch holds %zu bytes, needs %zu",
                 scratch_bytes, need);
   char* base = static_cast<char*>(scratch);
-  uint32_t* keys_out = reinterpret_cast<uint32_t*>(base + align_up(temp));
-  int32_t* iota = reinterpret_cast<int32_t*>(base + align_up(temp) + align_up(static_cast<size_t>(n) * 4));
+  uint32_t* keys_out = reinterpret_cast<uint32_t*>(base + temp);
+  int32_t* iota = reinterpret_cast<int32_t*>(base + temp + align_up(static_cast<size_t>(n) * 4));
   cudaStream_t s = as_stream(stream);
   iota_kernel<<<static_cast<unsigned>(ceil_div<int64_t>(n, 256)), 256, 0, s>>>(iota, n);
   TGS_LAUNCH_CHECK();
-  TGS_CUDA(cub::DeviceRadixSort::SortPairs(base, temp, reinterpret_cast<const uint32_t*>(depths),
-                                           keys_out, iota, order, static_cast<int>(n), 0, 32, s));
+  size_t sort_temp = temp;
+  TGS_CUDA(cub::DeviceRadixSort::SortPairs(base, sort_temp,
+                                           reinterpret_cast<const uint32_t*>(depths), keys_out,
+                                           iota, order, static_cast<int>(n), 0, 32, s));
+  size_t scan_temp = temp;
+  const auto it = thrust::make_transform_iterator(thrust::counting_iterator<int64_t>(0),
+                                                  OrderedTileCount{tiles_per_gauss, order});
+  TGS_CUDA(cub::DeviceScan::InclusiveSum(base, scan_temp, it, cum_tiles, static_cast<int>(n), s));
   return TGS_OK;
 }
 
@@ -844,7 +966,7 @@ extern "C" int tgs_isect_write_ordered(const float* means2d, const int32_t* radi
                                        const float* depths, const int32_t* order, int64_t n,
                                        int64_t n_per_camera, int32_t tile_size, int32_t tile_width,
                                        int32_t tile_height, const int64_t* cum_tiles,
-                                       uint32_t* tile_keys, int32_t* flatten_ids, void* stream) {
+                                       void* tile_keys, int32_t* flatten_ids, void* stream) {
   TGS_CHECK_ARG(n >= 0 && n_per_camera > 0 && tile_size > 0 && tile_width > 0 && tile_height > 0,
                 "tgs_isect_write_ordered: bad sizes");
   TGS_CHECK_ARG(n < (1ll << 31), "tgs_isect_write_ordered: more than 2^31 projected Gaussians");
@@ -852,13 +974,23 @@ extern "C" int tgs_isect_write_ordered(const float* means2d, const int32_t* radi
   TGS_CHECK_ARG(means2d && radii && depths && order && cum_tiles && tile_keys && flatten_ids,
                 "tgs_isect_write_ordered: NULL pointer");
   const int n_tiles = tile_width * tile_height;
-  const int bits = isect_key_bits(ceil_div<int64_t>(n, n_per_camera), n_tiles);
+  const int64_t n_cameras = ceil_div<int64_t>(n, n_per_camera);
+  TGS_CHECK_ARG(n_cameras <= 65535, "tgs_isect_write_ordered: too many cameras");
+  const int bits = isect_key_bits(n_cameras, n_tiles);
   TGS_CHECK_ARG(bits <= 32, "tgs_isect_write_ordered: camera and tile ids need %d bits", bits);
   const uint32_t mask = static_cast<uint32_t>((1ull << bits) - 1);
-  isect_write_ordered_kernel<<<static_cast<unsigned>(ceil_div<int64_t>(n, 256)), 256, 0,
-                               as_stream(stream)>>>(
-      means2d, radii, depths, order, n, n_per_camera, tile_size, tile_width, tile_height,
-      tgs_isect_tile_bits(n_tiles), mask, cum_tiles, tile_keys, flatten_ids);
+  const unsigned grid = static_cast<unsigned>(ceil_div<int64_t>(n, 256));
+  cudaStream_t s = as_stream(stream);
+  if (bits <= 16)
+    isect_write_ordered_kernel<uint16_t><<<grid, 256, 0, s>>>(
+        means2d, radii, depths, order, n, n_per_camera, tile_size, tile_width, tile_height,
+        tgs_isect_tile_bits(n_tiles), mask, cum_tiles, static_cast<uint16_t*>(tile_keys),
+        flatten_ids);
+  else
+    isect_write_ordered_kernel<uint32_t><<<grid, 256, 0, s>>>(
+        means2d, radii, depths, order, n, n_per_camera, tile_size, tile_width, tile_height,
+        tgs_isect_tile_bits(n_tiles), mask, cum_tiles, static_cast<uint32_t*>(tile_keys),
+        flatten_ids);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }
@@ -866,47 +998,68 @@ extern "C" int tgs_isect_write_ordered(const float* means2d, const int32_t* radi
 extern "C" int tgs_isect_sort_tiles_scratch_bytes(int64_t n_isects, int32_t n_cameras,
                                                   int32_t tile_width, int32_t tile_height,
                                                   size_t* bytes) {
-  TGS_CHECK_ARG(bytes && n_isects >= 0 && n_isects < (1ll << 31) && n_cameras > 0 &&
-                    tile_width > 0 && tile_height > 0,
+  const int32_t key_bytes = tgs_isect_key_bytes(n_cameras, tile_width, tile_height);
+  TGS_CHECK_ARG(bytes && n_isects >= 0 && n_isects < (1ll << 31) && key_bytes > 0,
                 "tgs_isect_sort_tiles_scratch_bytes: bad sizes");
-  size_t temp = 0;
-  TGS_CUDA(pair_sort_temp_bytes(n_isects, isect_key_bits(n_cameras, tile_width * tile_height),
-                                &temp));
-  *bytes = temp;
+  const int bits = isect_key_bits(n_cameras, tile_width * tile_height);
+  if (key_bytes == 2) TGS_CUDA(pair_sort_temp_bytes<uint16_t>(n_isects, bits, bytes));
+  else TGS_CUDA(pair_sort_temp_bytes<uint32_t>(n_isects, bits, bytes));
   return TGS_OK;
 }
 
-extern "C" int tgs_isect_sort_tiles(const uint32_t* tile_keys_in, const int32_t* flatten_in,
+extern "C" int tgs_isect_sort_tiles(const void* tile_keys_in, const int32_t* flatten_in,
                                     int64_t n_isects, int32_t n_cameras, int32_t tile_width,
-                                    int32_t tile_height, uint32_t* tile_keys_out,
+                                    int32_t tile_height, void* tile_keys_out,
                                     int32_t* flatten_out, void* scratch, size_t scratch_bytes,
                                     void* stream) {
-  TGS_CHECK_ARG(n_isects >= 0 && n_isects < (1ll << 31) && n_cameras > 0 && tile_width > 0 &&
-                    tile_height > 0,
+  const int32_t key_bytes = tgs_isect_key_bytes(n_cameras, tile_width, tile_height);
+  TGS_CHECK_ARG(n_isects >= 0 && n_isects < (1ll << 31) && key_bytes > 0,
                 "tgs_isect_sort_tiles: bad sizes");
   if (n_isects == 0) return TGS_OK;
   TGS_CHECK_ARG(tile_keys_in && flatten_in && tile_keys_out && flatten_out && scratch,
                 "tgs_isect_sort_tiles: NULL pointer");
   const int bits = isect_key_bits(n_cameras, tile_width * tile_height);
-  TGS_CHECK_ARG(bits <= 32, "tgs_isect_sort_tiles: camera and tile ids need %d bits", bits);
   size_t temp = 0;
-  TGS_CUDA(pair_sort_temp_bytes(n_isects, bits, &temp));
-  TGS_CHECK_ARG(scratch_bytes >= temp, "tgs_isect_sort_tiles: scratch holds %zu bytes, needs %zu",
-                scratch_bytes, temp);
-  TGS_CUDA(cub::DeviceRadixSort::SortPairs(scratch, temp, tile_keys_in, tile_keys_out, flatten_in,
-                                           flatten_out, static_cast<int>(n_isects), 0, bits,
-                                           as_stream(stream)));
+  cudaStream_t s = as_stream(stream);
+  if (key_bytes == 2) {
+    TGS_CUDA(pair_sort_temp_bytes<uint16_t>(n_isects, bits, &temp));
+    TGS_CHECK_ARG(scratch_bytes >= temp, "tgs_isect_sort_tiles: scratch holds %zu bytes, needs %zu",
+                  scratch_bytes, temp);
+    TGS_CUDA(cub::DeviceRadixSort::SortPairs(
+        scratch, temp, static_cast<const uint16_t*>(tile_keys_in),
+        static_cast<uint16_t*>(tile_keys_out), flatten_in, flatten_out,
+        static_cast<int>(n_isects), 0, bits, s));
+  } else {
+    TGS_CUDA(pair_sort_temp_bytes<uint32_t>(n_isects, bits, &temp));
+    TGS_CHECK_ARG(scratch_bytes >= temp, "tgs_isect_sort_tiles: scratch holds %zu bytes, needs %zu",
+                  scratch_bytes, temp);
+    TGS_CUDA(cub::DeviceRadixSort::SortPairs(
+        scratch, temp, static_cast<const uint32_t*>(tile_keys_in),
+        static_cast<uint32_t*>(tile_keys_out), flatten_in, flatten_out,
+        static_cast<int>(n_isects), 0, bits, s));
+  }
   return TGS_OK;
 }
 
-extern "C" int tgs_isect_expand_ids(const uint32_t* tile_keys, const int32_t* flatten_ids,
-                                    const float* depths, int64_t n_isects, int64_t* isect_ids,
-                                    void* stream) {
-  TGS_CHECK_ARG(n_isects >= 0, "tgs_isect_expand_ids: bad n_isects");
+extern "C" int tgs_isect_expand_ids(const void* tile_keys, int32_t key_bytes,
+                                    const int32_t* flatten_ids, const float* depths,
+                                    int64_t n_isects, int64_t* isect_ids, void* stream) {
+  TGS_CHECK_ARG(n_isects >= 0 && (key_bytes == 2 || key_bytes == 4),
+                "tgs_isect_expand_ids: bad sizes");
   if (n_isects == 0) return TGS_OK;
   TGS_CHECK_ARG(tile_keys && flatten_ids && depths && isect_ids, "tgs_isect_expand_ids: NULL pointer");
-  isect_expand_kernel<<<static_cast<unsigned>(ceil_div<int64_t>(n_isects, 256)), 256, 0,
-                        as_stream(stream)>>>(tile_keys, flatten_ids, depths, n_isects, isect_ids);
+  TGS_CHECK_ARG(reinterpret_cast<uintptr_t>(tile_keys) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(flatten_ids) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(isect_ids) % 16 == 0,
+                "tgs_isect_expand_ids: arrays must start on 16-byte boundaries");
+  const unsigned grid = static_cast<unsigned>(ceil_div<int64_t>(ceil_div<int64_t>(n_isects, 4), 256));
+  cudaStream_t s = as_stream(stream);
+  if (key_bytes == 2)
+    isect_expand_kernel<uint16_t><<<grid, 256, 0, s>>>(static_cast<const uint16_t*>(tile_keys),
+                                                       flatten_ids, depths, n_isects, isect_ids);
+  else
+    isect_expand_kernel<uint32_t><<<grid, 256, 0, s>>>(static_cast<const uint32_t*>(tile_keys),
+                                                       flatten_ids, depths, n_isects, isect_ids);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

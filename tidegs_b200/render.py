@@ -159,15 +159,20 @@ def isect_tiles(means2d: torch.Tensor, radii: torch.Tensor, depths: torch.Tensor
     # sorted: Gaussians in depth order, their tiles emitted in that order with
     # 32-bit (camera, tile) keys, a stable sort of those, 64-bit keys put back
     order = torch.empty(n, dtype=torch.int32, device=dev)
+    cum = torch.empty(n, dtype=torch.int64, device=dev)
     scratch = _scratch(dev, "tgs_isect_depth_order_scratch_bytes", n)
-    _lib.call("tgs_isect_depth_order", depths_.data_ptr(), n, order.data_ptr(),
-              scratch.data_ptr(), scratch.numel(), s)
-    cum = torch.cumsum(tiles.view(-1)[order], 0)
+    _lib.call("tgs_isect_depth_order", depths_.data_ptr(), tiles.data_ptr(), n, order.data_ptr(),
+              cum.data_ptr(), scratch.data_ptr(), scratch.numel(), s)
+    del scratch
     n_isects = int(cum[-1].item())
     isect_ids = torch.empty(n_isects, dtype=torch.int64, device=dev)
     flatten_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
     if n_isects:
-        keys = torch.empty(n_isects, dtype=torch.int32, device=dev)
+        key_bytes = int(_lib.load().tgs_isect_key_bytes(C, int(tile_width), int(tile_height)))
+        if key_bytes == 0:
+            raise RuntimeError("isect_tiles: camera and tile ids need more than 32 bits")
+        key_dtype = torch.int16 if key_bytes == 2 else torch.int32
+        keys = torch.empty(n_isects, dtype=key_dtype, device=dev)
         unsorted_ids = torch.empty(n_isects, dtype=torch.int32, device=dev)
         _lib.call("tgs_isect_write_ordered", means2d_.data_ptr(), radii_.data_ptr(),
                   depths_.data_ptr(), order.data_ptr(), n, N, int(tile_size), int(tile_width),
@@ -178,8 +183,8 @@ def isect_tiles(means2d: torch.Tensor, radii: torch.Tensor, depths: torch.Tensor
         _lib.call("tgs_isect_sort_tiles", keys.data_ptr(), unsorted_ids.data_ptr(), n_isects, C,
                   int(tile_width), int(tile_height), sorted_keys.data_ptr(),
                   flatten_ids.data_ptr(), scratch.data_ptr(), scratch.numel(), s)
-        _lib.call("tgs_isect_expand_ids", sorted_keys.data_ptr(), flatten_ids.data_ptr(),
-                  depths_.data_ptr(), n_isects, isect_ids.data_ptr(), s)
+        _lib.call("tgs_isect_expand_ids", sorted_keys.data_ptr(), key_bytes,
+                  flatten_ids.data_ptr(), depths_.data_ptr(), n_isects, isect_ids.data_ptr(), s)
     return tiles, isect_ids, flatten_ids
 
 

@@ -540,35 +540,45 @@ __device__ __forceinline__ TileSpan tile_span(const TgsRasterArgs& a, int cam, i
   return s;
 }
 
-template <int D>
+// Forward, front to back; each thread composites P vertically adjacent
+// pixels of its column, reading each staged Gaussian once for them.
+template <int D, int P>
 __global__ void raster_fwd_kernel(const TgsRasterArgs a) {
   extern __shared__ __align__(16) unsigned char raster_smem[];
   const int nthreads = blockDim.x * blockDim.y;
   int32_t* ids = reinterpret_cast<int32_t*>(raster_smem);
   float3* xyo = reinterpret_cast<float3*>(ids + nthreads);
   float3* con = xyo + nthreads;
+  float* rgb = reinterpret_cast<float*>(con + nthreads);
 
   const int cam = blockIdx.x;
   const int tile_id = blockIdx.y * a.tile_width + blockIdx.z;
-  const int i = blockIdx.y * a.tile_size + threadIdx.y;
   const int j = blockIdx.z * a.tile_size + threadIdx.x;
   const int tr = threadIdx.y * blockDim.x + threadIdx.x;
   const int64_t pix_base = static_cast<int64_t>(cam) * a.image_height * a.image_width;
-  const float px = static_cast<float>(j) + 0.5f, py = static_cast<float>(i) + 0.5f;
-  const bool inside = i < a.image_height && j < a.image_width;
-  bool done = !inside;
+  const float px = static_cast<float>(j) + 0.5f;
+  bool done[P];
+  float py[P], T[P], acc[P][D];
+  int cur[P];
+#pragma unroll
+  for (int q = 0; q < P; ++q) {
+    const int i = blockIdx.y * a.tile_size + threadIdx.y * P + q;
+    done[q] = !(i < a.image_height && j < a.image_width);
+    py[q] = static_cast<float>(i) + 0.5f;
+    T[q] = 1.f;
+    cur[q] = 0;
+#pragma unroll
+    for (int k = 0; k < D; ++k) acc[q][k] = 0.f;
+  }
 
   const TileSpan span = tile_span(a, cam, tile_id);
   const int n_batches = (span.end - span.start + nthreads - 1) / nthreads;
 
-  float T = 1.f;
-  int cur = 0;
-  float acc[D];
-#pragma unroll
-  for (int k = 0; k < D; ++k) acc[k] = 0.f;
-
   for (int b = 0; b < n_batches; ++b) {
-    if (__syncthreads_count(done) >= nthreads) break;
+    bool all_done = true;
+#pragma unroll
+    for (int q = 0; q < P; ++q) all_done &= done[q];
+    if (__syncthreads_count(all_done) >= nthreads) break;
     const int batch_start = span.start + b * nthreads;
     const int idx = batch_start + tr;
     if (idx < span.end) {
@@ -578,36 +588,51 @@ __global__ void raster_fwd_kernel(const TgsRasterArgs a) {
                             a.opacities[g]);
       con[tr] = make_float3(a.conics[3 * static_cast<int64_t>(g)], a.conics[3 * static_cast<int64_t>(g) + 1],
                             a.conics[3 * static_cast<int64_t>(g) + 2]);
+#pragma unroll
+      for (int k = 0; k < D; ++k) rgb[tr * D + k] = a.colors[static_cast<int64_t>(g) * D + k];
     }
     __syncthreads();
     const int batch_size = min(nthreads, span.end - batch_start);
-    for (int t = 0; t < batch_size && !done; ++t) {
+    for (int t = 0; t < batch_size && !all_done; ++t) {
       const float3 c = con[t];
       const float3 xo = xyo[t];
-      const float dx = xo.x - px, dy = xo.y - py;
-      const float sigma = 0.5f * (c.x * dx * dx + c.z * dy * dy) + c.y * dx * dy;
-      const float alpha = fminf(0.999f, xo.z * __expf(-sigma));
-      if (sigma < 0.f || alpha < 1.f / 255.f) continue;
-      const float next_T = T * (1.f - alpha);
-      if (next_T <= 1e-4f) {
-        done = true;
-        break;
-      }
-      const float vis = alpha * T;
-      const float* col = a.colors + static_cast<int64_t>(ids[t]) * D;
+      const float dx = xo.x - px;
+      all_done = true;
 #pragma unroll
-      for (int k = 0; k < D; ++k) acc[k] += col[k] * vis;
-      cur = batch_start + t;
-      T = next_T;
+      for (int q = 0; q < P; ++q) {
+        if (!done[q]) {
+          const float dy = xo.y - py[q];
+          const float sigma = 0.5f * (c.x * dx * dx + c.z * dy * dy) + c.y * dx * dy;
+          const float alpha = fminf(0.999f, xo.z * __expf(-sigma));
+          if (sigma >= 0.f && alpha >= 1.f / 255.f) {
+            const float next_T = T[q] * (1.f - alpha);
+            if (next_T <= 1e-4f) {
+              done[q] = true;
+            } else {
+              const float vis = alpha * T[q];
+#pragma unroll
+              for (int k = 0; k < D; ++k) acc[q][k] += rgb[t * D + k] * vis;
+              cur[q] = batch_start + t;
+              T[q] = next_T;
+            }
+          }
+        }
+        all_done &= done[q];
+      }
     }
   }
-  if (inside) {
-    const int64_t pix = pix_base + static_cast<int64_t>(i) * a.image_width + j;
-    a.render_alphas[pix] = 1.f - T;
-    const float* bg = a.backgrounds != nullptr ? a.backgrounds + cam * D : nullptr;
 #pragma unroll
-    for (int k = 0; k < D; ++k) a.render_colors[pix * D + k] = bg ? acc[k] + T * bg[k] : acc[k];
-    a.last_ids[pix] = cur;
+  for (int q = 0; q < P; ++q) {
+    const int i = blockIdx.y * a.tile_size + threadIdx.y * P + q;
+    if (i < a.image_height && j < a.image_width) {
+      const int64_t pix = pix_base + static_cast<int64_t>(i) * a.image_width + j;
+      a.render_alphas[pix] = 1.f - T[q];
+      const float* bg = a.backgrounds != nullptr ? a.backgrounds + cam * D : nullptr;
+#pragma unroll
+      for (int k = 0; k < D; ++k)
+        a.render_colors[pix * D + k] = bg ? acc[q][k] + T[q] * bg[k] : acc[q][k];
+      a.last_ids[pix] = cur[q];
+    }
   }
 }
 
@@ -633,7 +658,12 @@ __device__ __forceinline__ float warp_reduce_scatter16(const float (&v)[16], int
   return w1 + __shfl_xor_sync(kAll, w1, 1);
 }
 
-template <int D>
+// Backward, back to front. Each thread handles P vertically adjacent pixels
+// of its column (a warp covers a 16 x (2P) patch of a 16-pixel tile): the
+// Gaussian is read from shared memory once for the P pixels, its per-pixel
+// gradients are added in registers, and one warp reduce-scatter plus one
+// set of atomics serves 32 P pixels.
+template <int D, int P>
 __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
   const TgsRasterArgs& a = b.fwd;
   // per-Gaussian gradient: means2d (2), conic (3), colors (D), opacity,
@@ -649,38 +679,60 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
 
   const int cam = blockIdx.x;
   const int tile_id = blockIdx.y * a.tile_width + blockIdx.z;
-  const int i = blockIdx.y * a.tile_size + threadIdx.y;
   const int j = blockIdx.z * a.tile_size + threadIdx.x;
   const int tr = threadIdx.y * blockDim.x + threadIdx.x;
   const int lane = tr & 31;
-  const bool inside = i < a.image_height && j < a.image_width;
   const int64_t plane = static_cast<int64_t>(a.image_height) * a.image_width;
-  const int64_t pix = static_cast<int64_t>(cam) * plane +
-                      min(static_cast<int64_t>(i) * a.image_width + j, plane - 1);
-  const float px = static_cast<float>(j) + 0.5f, py = static_cast<float>(i) + 0.5f;
+  const float px = static_cast<float>(j) + 0.5f;
   const bool absgrad = b.v_means2d_abs != nullptr;
+
+  // the gradient component this lane adds to global memory after the
+  // reduce-scatter (lane 2k holds component k)
+  const int comp = lane >> 1;
+  const bool adds = (lane & 1) == 0 && comp < (absgrad ? K : K - 2);
+  float* comp_base = nullptr;
+  int comp_stride = 0;
+  if (adds) {
+    if (comp < 2) comp_base = b.v_means2d + comp, comp_stride = 2;
+    else if (comp < 5) comp_base = b.v_conics + (comp - 2), comp_stride = 3;
+    else if (comp < 5 + D) comp_base = b.v_colors + (comp - 5), comp_stride = D;
+    else if (comp == 5 + D) comp_base = b.v_opacities, comp_stride = 1;
+    else comp_base = b.v_means2d_abs + (comp - 6 - D), comp_stride = 2;
+  }
 
   const TileSpan span = tile_span(a, cam, tile_id);
   const int n_batches = (span.end - span.start + nthreads - 1) / nthreads;
 
-  const float T_final = 1.f - a.render_alphas[pix];
-  float T = T_final;
-  float buffer[D];
+  bool inside[P];
+  float py[P], T_final[P], T[P], buffer[P][D], v_out[P][D], v_alpha_out[P], bg_dot[P];
+  int bin_final[P];
+  int warp_bin_final = 0;
 #pragma unroll
-  for (int k = 0; k < D; ++k) buffer[k] = 0.f;
-  const int bin_final = inside ? a.last_ids[pix] : 0;
-  float v_out[D];
+  for (int q = 0; q < P; ++q) {
+    const int i = blockIdx.y * a.tile_size + threadIdx.y * P + q;
+    inside[q] = i < a.image_height && j < a.image_width;
+    py[q] = static_cast<float>(i) + 0.5f;
+    const int64_t pix = static_cast<int64_t>(cam) * plane +
+                        min(static_cast<int64_t>(i) * a.image_width + j, plane - 1);
+    T_final[q] = 1.f - a.render_alphas[pix];
+    T[q] = T_final[q];
+    bin_final[q] = inside[q] ? a.last_ids[pix] : 0;
+    warp_bin_final = max(warp_bin_final, bin_final[q]);
 #pragma unroll
-  for (int k = 0; k < D; ++k) v_out[k] = b.v_render_colors[pix * D + k];
-  const float v_alpha_out = b.v_render_alphas[pix];
-  float bg_dot = 0.f;
-  if (a.backgrounds != nullptr) {
+    for (int k = 0; k < D; ++k) {
+      buffer[q][k] = 0.f;
+      v_out[q][k] = b.v_render_colors[pix * D + k];
+    }
+    v_alpha_out[q] = b.v_render_alphas[pix];
+    bg_dot[q] = 0.f;
+    if (a.backgrounds != nullptr) {
 #pragma unroll
-    for (int k = 0; k < D; ++k) bg_dot += a.backgrounds[cam * D + k] * v_out[k];
+      for (int k = 0; k < D; ++k) bg_dot[q] += a.backgrounds[cam * D + k] * v_out[q][k];
+    }
   }
-  int warp_bin_final = bin_final;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) warp_bin_final = max(warp_bin_final, __shfl_xor_sync(0xffffffffu, warp_bin_final, o));
+  for (int o = 16; o > 0; o >>= 1)
+    warp_bin_final = max(warp_bin_final, __shfl_xor_sync(0xffffffffu, warp_bin_final, o));
 
   for (int bt = 0; bt < n_batches; ++bt) {
     __syncthreads();
@@ -700,90 +752,90 @@ __global__ void raster_bwd_kernel(const TgsRasterBwdArgs b) {
     }
     __syncthreads();
     for (int t = max(0, batch_end - warp_bin_final); t < batch_size; ++t) {
-      bool valid = inside && (batch_end - t <= bin_final);
-      float alpha = 0.f, opac = 0.f, vis = 0.f, dx = 0.f, dy = 0.f;
-      float3 c = make_float3(0.f, 0.f, 0.f);
-      if (valid) {
-        c = con[t];
-        const float3 xo = xyo[t];
-        opac = xo.z;
-        dx = xo.x - px;
-        dy = xo.y - py;
-        const float sigma = 0.5f * (c.x * dx * dx + c.z * dy * dy) + c.y * dx * dy;
-        vis = __expf(-sigma);
-        alpha = fminf(0.999f, opac * vis);
-        if (sigma < 0.f || alpha < 1.f / 255.f) valid = false;
+      const float3 c = con[t];
+      const float3 xo = xyo[t];
+      const float opac = xo.z;
+      const float dx = xo.x - px;
+      bool valid[P];
+      float vis[P], alpha[P], dy[P];
+      bool any = false;
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        dy[q] = xo.y - py[q];
+        const float sigma = 0.5f * (c.x * dx * dx + c.z * dy[q] * dy[q]) + c.y * dx * dy[q];
+        vis[q] = __expf(-sigma);
+        alpha[q] = fminf(0.999f, opac * vis[q]);
+        valid[q] = inside[q] && (batch_end - t <= bin_final[q]) && sigma >= 0.f &&
+                   alpha[q] >= 1.f / 255.f;
+        any |= valid[q];
       }
-      if (!__any_sync(0xffffffffu, valid)) continue;
+      if (!__any_sync(0xffffffffu, any)) continue;
       float gv[16];
 #pragma unroll
       for (int k = 0; k < 16; ++k) gv[k] = 0.f;
-      if (valid) {
+      float col[D];
+#pragma unroll
+      for (int k = 0; k < D; ++k) col[k] = rgb[t * D + k];
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        if (!valid[q]) continue;
         // fast reciprocal (the render path is compared within tolerance)
-        const float ra = __fdividef(1.f, 1.f - alpha);
-        T *= ra;
-        const float fac = alpha * T;
+        const float ra = __fdividef(1.f, 1.f - alpha[q]);
+        T[q] *= ra;
+        const float fac = alpha[q] * T[q];
         float v_alpha = 0.f;
 #pragma unroll
         for (int k = 0; k < D; ++k) {
-          gv[5 + k] = fac * v_out[k];
-          v_alpha += (rgb[t * D + k] * T - buffer[k] * ra) * v_out[k];
+          gv[5 + k] += fac * v_out[q][k];
+          v_alpha += (col[k] * T[q] - buffer[q][k] * ra) * v_out[q][k];
         }
-        v_alpha += T_final * ra * v_alpha_out;
-        if (a.backgrounds != nullptr) v_alpha += -T_final * ra * bg_dot;
-        if (opac * vis <= 0.999f) {
-          const float v_sigma = -opac * vis * v_alpha;
-          gv[2] = 0.5f * v_sigma * dx * dx;
-          gv[3] = v_sigma * dx * dy;
-          gv[4] = 0.5f * v_sigma * dy * dy;
-          gv[0] = v_sigma * (c.x * dx + c.y * dy);
-          gv[1] = v_sigma * (c.y * dx + c.z * dy);
-          gv[5 + D] = vis * v_alpha;
-          gv[6 + D] = fabsf(gv[0]);
-          gv[7 + D] = fabsf(gv[1]);
+        v_alpha += T_final[q] * ra * v_alpha_out[q];
+        if (a.backgrounds != nullptr) v_alpha += -T_final[q] * ra * bg_dot[q];
+        if (opac * vis[q] <= 0.999f) {
+          const float v_sigma = -opac * vis[q] * v_alpha;
+          const float gx = v_sigma * (c.x * dx + c.y * dy[q]);
+          const float gy = v_sigma * (c.y * dx + c.z * dy[q]);
+          gv[0] += gx;
+          gv[1] += gy;
+          gv[2] += 0.5f * v_sigma * dx * dx;
+          gv[3] += v_sigma * dx * dy[q];
+          gv[4] += 0.5f * v_sigma * dy[q] * dy[q];
+          gv[5 + D] += vis[q] * v_alpha;
+          gv[6 + D] += fabsf(gx);
+          gv[7 + D] += fabsf(gy);
         }
 #pragma unroll
-        for (int k = 0; k < D; ++k) buffer[k] += rgb[t * D + k] * fac;
+        for (int k = 0; k < D; ++k) buffer[q][k] += col[k] * fac;
       }
-      // lane 2k holds the warp total of gradient component k; the lanes
-      // of the components in use add them to global memory together
       const float total = warp_reduce_scatter16(gv, lane);
-      const int k = lane >> 1;
-      if ((lane & 1) == 0 && k < (absgrad ? K : K - 2)) {
-        const int64_t g = ids[t];
-        float* dst;
-        if (k < 2) dst = b.v_means2d + 2 * g + k;
-        else if (k < 5) dst = b.v_conics + 3 * g + (k - 2);
-        else if (k < 5 + D) dst = b.v_colors + D * g + (k - 5);
-        else if (k == 5 + D) dst = b.v_opacities + g;
-        else dst = b.v_means2d_abs + 2 * g + (k - 6 - D);
-        atomicAdd(dst, total);
-      }
+      if (adds) atomicAdd(comp_base + static_cast<int64_t>(comp_stride) * ids[t], total);
     }
   }
 }
 
 template <int D>
-size_t raster_smem_bytes(int nthreads, bool bwd) {
-  size_t s = nthreads * (sizeof(int32_t) + 2 * sizeof(float3));
-  if (bwd) s += nthreads * sizeof(float) * D;
-  return s;
+size_t raster_smem_bytes(int nthreads) {
+  // per staged Gaussian: id, (x, y, opacity), conic, D colors
+  return nthreads * (sizeof(int32_t) + 2 * sizeof(float3) + sizeof(float) * D);
 }
 
 template <int D>
 int launch_raster(const TgsRasterArgs& a, const TgsRasterBwdArgs* bwd, cudaStream_t s) {
   const int nthreads = a.tile_size * a.tile_size;
   const dim3 grid(a.n_cameras, a.tile_height, a.tile_width);
-  const dim3 block(a.tile_size, a.tile_size, 1);
-  const size_t smem = raster_smem_bytes<D>(nthreads, bwd != nullptr);
+  // two pixels per thread: tile_size^2 is a multiple of 32, so tile_size
+  // is a multiple of 8 and half a tile is whole warps
+  const size_t smem2 = raster_smem_bytes<D>(nthreads / 2);
   if (bwd == nullptr) {
-    TGS_CUDA(cudaFuncSetAttribute(raster_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(smem)));
-    raster_fwd_kernel<D><<<grid, block, smem, s>>>(a);
+    TGS_CUDA(cudaFuncSetAttribute(raster_fwd_kernel<D, 2>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem2)));
+    raster_fwd_kernel<D, 2><<<grid, dim3(a.tile_size, a.tile_size / 2, 1), smem2, s>>>(a);
   } else {
-    TGS_CUDA(cudaFuncSetAttribute(raster_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  static_cast<int>(smem)));
-    raster_bwd_kernel<D><<<grid, block, smem, s>>>(*bwd);
+    TGS_CUDA(cudaFuncSetAttribute(raster_bwd_kernel<D, 2>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem2)));
+    raster_bwd_kernel<D, 2><<<grid, dim3(a.tile_size, a.tile_size / 2, 1), smem2, s>>>(*bwd);
   }
   TGS_LAUNCH_CHECK();
   return TGS_OK;

@@ -49,11 +49,56 @@ SLOTS = 2048
 TURNOVER = 512
 
 
+# scene blocks a rank owns = POOL_MULT * SLOTS (4: BASELINE configs[3]'s
+# pinned pool); lowered by plan_host_pool when the box's memory cannot hold
+# every rank's page-locked host tier
+POOL_MULT = 4
+BLOCK_BYTES = B * 59 * 4
+
+
 def set_slots(slots: int) -> None:
     """Resident slots per GPU; the turnover stays at 25 % of them."""
     global SLOTS, TURNOVER
     SLOTS = int(slots)
     TURNOVER = max(1, SLOTS // 4)
+
+
+def host_memory_limit() -> int:
+    """Bytes of host memory the job may use: MemTotal, or the cgroup limit
+    when that is lower (the same value on every rank of the box)."""
+    limit = None
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemTotal:"):
+                    limit = int(line.split()[1]) * 1024
+                    break
+    except OSError:
+        pass
+    for path in ("/sys/fs/cgroup/memory.max", "/sys/fs/cgroup/memory/memory.limit_in_bytes"):
+        try:
+            with open(path) as f:
+                v = f.read().strip()
+        except OSError:
+            continue
+        if v.isdigit() and int(v) > 0:
+            limit = int(v) if limit is None else min(limit, int(v))
+    return limit if limit is not None else 0
+
+
+def plan_host_pool(world: int, host_tier: str, pool_blocks: int, limit: int):
+    """(pool multiple, host tier) that fit every rank's host tier into 60 %
+    of the box's memory: the cache holds POOL_MULT * SLOTS + TURNOVER
+    page-locked entries plus pool_blocks seeded source blocks per rank; the
+    scene shrinks to 3 or 2 x SLOTS blocks per rank before the cache gives
+    way to the small fixed pool (pool_blocks page-locked blocks)."""
+    budget = 0.6 * limit / world
+    if host_tier == "cache":
+        for mult in (4, 3, 2):
+            if (mult * SLOTS + TURNOVER + pool_blocks) * BLOCK_BYTES <= budget:
+                return mult, "cache"
+        return 4, "pool"
+    return 4, host_tier
 
 
 WIDTHS = {"xyz": 3, "opacity": 1, "scaling": 3, "rotation": 4, "features_dc": 3,
@@ -175,8 +220,8 @@ class Schedule:
         self.rng = np.random.default_rng(seed + 1000 * rank)
         self.world = world
         self.rank = rank
-        # owned block ids: rank + k*world; 8192 candidate blocks per rank
-        self.pool_ids = np.arange(rank, rank + world * 4 * SLOTS, world, dtype=np.int64)
+        # owned block ids: rank + k*world; POOL_MULT * SLOTS per rank
+        self.pool_ids = np.arange(rank, rank + world * POOL_MULT * SLOTS, world, dtype=np.int64)
         self.slot_block = self.rng.choice(self.pool_ids, SLOTS, replace=False)
         self.n_sets = n_cameras_sets
 
@@ -627,8 +672,8 @@ class ApiStep:
         gen = torch.Generator().manual_seed(99 + rank)
         self.cache = None
         if host_tier == "cache":
-            # the host tier holds every scene block of this rank (4 x SLOTS
-            # blocks, BASELINE configs[3]'s pinned pool): pool_blocks distinct
+            # the host tier holds every scene block of this rank (POOL_MULT x
+            # SLOTS blocks, BASELINE configs[3]'s pinned pool): pool_blocks distinct
             # seeded blocks, block b holding distinct[b % pool_blocks], read
             # into the cache's page-locked slab through its prefetch; room
             # for one write-back batch of fresh entries on top
@@ -1293,6 +1338,9 @@ def main(argv=None):
     from tidegs_b200 import _lib
 
     device = torch.device("cuda", torch.cuda.current_device())
+    global POOL_MULT
+    POOL_MULT, args.host_tier = plan_host_pool(world, args.host_tier, args.pool_blocks,
+                                               host_memory_limit())
     n_trace = max(args.warmup + args.steps + 3, args.e2e_warmup + args.e2e_steps + 1)
     trace = ScheduleTrace(world, rank, n_trace)
     scheds = [Schedule(o, world) for o in range(world)]
@@ -1370,7 +1418,7 @@ def main(argv=None):
                "d2h_bytes_per_step": int(api.d2h_bytes / args.e2e_steps),
                "ms_per_step": e_ms / args.e2e_steps, "steps": args.e2e_steps,
                "host_pool_blocks": args.pool_blocks,
-               "host_tier": (f"PinnedBlockCache of the rank's {4 * SLOTS} scene blocks "
+               "host_tier": (f"PinnedBlockCache of the rank's {POOL_MULT * SLOTS} scene blocks "
                              f"(+{TURNOVER} write-back entries); write-back DMA into it"
                              if args.host_tier == "cache" else
                              f"PinnedBlockPool of {args.pool_blocks} blocks (block id mod pool)")}
@@ -1401,6 +1449,7 @@ def main(argv=None):
                                    "Gaussians per GPU, 16-camera contiguous block runs (~30% "
                                    "visible), 25% slot turnover, Bernoulli(0.5) dirty evictions",
                        "slots_per_gpu": SLOTS, "block_size": B, "turnover_blocks": TURNOVER,
+                       "scene_blocks_per_gpu": POOL_MULT * SLOTS,
                        "rows_updated_per_step": rows / args.steps,
                        "parallelism": f"block ownership, rank = block_id mod {world}",
                        "exchange_rows_per_step": exchange_rows / (args.warmup + args.steps),

@@ -1028,11 +1028,13 @@ def cull_probe(args):
 def render_probe(args):
     """Not the bench line. The engine's render path for one camera batch
     (strategies/tide_engine/engine.py:481-561): projection, tile intersection,
-    rasterization forward and the two backward kernels, tidegs_b200 against
+    SH colors (degree 3), rasterization forward and the three backward
+    kernels, tidegs_b200 against
     the reference's gsplat 1.0.0 kernels compiled from its sources
     (oracle/_ref/gsplat) on the same inputs. Seeded scene: 2 M Gaussians in
     a box in front of a 1920 x 1080 camera, log-normal scales, uniform
-    opacities and colors. One JSON line per implementation (CUDA events,
+    opacities, N(0, 0.2) degree-3 SH coefficients (colors evaluated from them,
+    as the engine does). One JSON line per implementation (CUDA events,
     median over --steps after --warmup)."""
     from oracle import build_ref
     from oracle import render as orc
@@ -1047,12 +1049,15 @@ def render_probe(args):
     quats = torch.randn((n, 4), generator=g, device=dev)
     scales = torch.exp(torch.randn((n, 3), generator=g, device=dev) * 0.5 - 3.2)
     opac = torch.rand((1, n), generator=g, device=dev) * 0.9 + 0.05
-    colors = torch.rand((1, n, 3), generator=g, device=dev)
+    # degree-3 SH coefficients (16 per channel), colors evaluated per camera
+    coeffs = torch.randn((1, n, 16, 3), generator=g, device=dev) * 0.2
+    dirs = (means - torch.tensor([0.0, 0.0, -1.0], device=dev))[None].contiguous()
     view = orc.look_at((0.0, 0.0, -1.0), (0.0, 0.0, 10.0), up=(0.0, -1.0, 0.0))[None].float().to(dev)
     K = orc.intrinsics(Wd, Hd, 70.0)[None].float().to(dev)
     tw, th = (Wd + tile - 1) // tile, (Hd + tile - 1) // tile
     ref = build_ref.load_prebuilt_gsplat()
     means_g, quats_g, scales_g = (t.clone().requires_grad_(True) for t in (means, quats, scales))
+    coeffs_g = coeffs.clone().requires_grad_(True)
 
     def run_ours():
         marks = {}
@@ -1060,6 +1065,10 @@ def render_probe(args):
                                                       0.3, 0.01, 1e10, 0.0, False)
         marks["projection"] = torch.cuda.Event(enable_timing=True)
         marks["projection"].record()
+        sh_out = tr.spherical_harmonics(3, dirs, coeffs_g)
+        colors = sh_out.detach()
+        marks["sh"] = torch.cuda.Event(enable_timing=True)
+        marks["sh"].record()
         _, ids, flat = tr.isect_tiles(m2, radii, dep, tile, tw, th)
         offs = tr.isect_offset_encode(ids, 1, tw, th)
         marks["intersect"] = torch.cuda.Event(enable_timing=True)
@@ -1070,12 +1079,19 @@ def render_probe(args):
                                                   offs, flat)
         marks["raster_fwd"] = torch.cuda.Event(enable_timing=True)
         marks["raster_fwd"].record()
-        _, vm, vc, _, _ = tr.rasterize_to_pixels_bwd(m2d, cond, colors, opac, None, Wd, Hd, tile,
-                                                     offs, flat, ra, last, torch.ones_like(rc),
-                                                     torch.ones_like(ra), False)
+        _, vm, vc, vcol, _ = tr.rasterize_to_pixels_bwd(m2d, cond, colors, opac, None, Wd, Hd,
+                                                        tile, offs, flat, ra, last,
+                                                        torch.ones_like(rc), torch.ones_like(ra),
+                                                        False)
         marks["raster_bwd"] = torch.cuda.Event(enable_timing=True)
         marks["raster_bwd"].record()
-        torch.autograd.backward([m2, dep, con], [vm, torch.zeros_like(dep), vc])
+        # autograd.grad: the gradients are returned, not added into the
+        # leaves' .grad (an extra pass over them the reference arm does not do)
+        torch.autograd.grad([sh_out], [coeffs_g], [vcol])
+        marks["sh_bwd"] = torch.cuda.Event(enable_timing=True)
+        marks["sh_bwd"].record()
+        torch.autograd.grad([m2, dep, con], [means_g, quats_g, scales_g],
+                            [vm, torch.zeros_like(dep), vc])
         marks["projection_bwd"] = torch.cuda.Event(enable_timing=True)
         marks["projection_bwd"].record()
         return marks, int(flat.numel())
@@ -1086,6 +1102,9 @@ def render_probe(args):
                                                                 Wd, Hd, 0.3, 0.01, 1e10, 0.0, False)
         marks["projection"] = torch.cuda.Event(enable_timing=True)
         marks["projection"].record()
+        colors = ref.compute_sh_fwd(3, dirs, coeffs, None)
+        marks["sh"] = torch.cuda.Event(enable_timing=True)
+        marks["sh"].record()
         _, ids, flat = ref.isect_tiles(m2, radii, dep, None, None, 1, tile, tw, th, True, True)
         offs = ref.isect_offset_encode(ids, 1, tw, th)
         marks["intersect"] = torch.cuda.Event(enable_timing=True)
@@ -1098,6 +1117,9 @@ def render_probe(args):
                                                           torch.ones_like(ra), False)
         marks["raster_bwd"] = torch.cuda.Event(enable_timing=True)
         marks["raster_bwd"].record()
+        ref.compute_sh_bwd(16, 3, dirs, coeffs, None, vcol, False)
+        marks["sh_bwd"] = torch.cuda.Event(enable_timing=True)
+        marks["sh_bwd"].record()
         ref.fully_fused_projection_bwd(means, None, quats, scales, view, K, Wd, Hd, 0.3, radii, con,
                                        None, vm, torch.zeros_like(dep), vc, None, False)
         marks["projection_bwd"] = torch.cuda.Event(enable_timing=True)

@@ -730,6 +730,33 @@ typedef struct {
  * per Gaussian and tile, one set of global additions. */
 TGS_API int tgs_rasterize_bwd(const TgsRasterBwdArgs* args, void* stream);
 
+/* Spherical-harmonics colors (gsplat compute_sh_fwd.cu / compute_sh_bwd.cu,
+ * spherical_harmonics.cuh; the engine's call engine.py:508-520):
+ * colors[n] = sum_{k < (degree+1)^2} coeffs[n, k, :] Y_k(dirs[n] / |dirs[n]|),
+ * real SH of degree <= 4 in 3D Gaussian splatting's order and signs. */
+typedef struct {
+  const float* dirs;          /* [n, 3] (need not be unit length) */
+  const float* coeffs;        /* [n, K, 3] */
+  const uint8_t* masks;       /* [n] bool, or NULL: masked rows give 0 */
+  int64_t n;
+  int32_t K;                  /* coefficients per row, 1..25 */
+  int32_t degree;             /* degrees_to_use, (degree + 1)^2 <= K */
+  float* colors;              /* [n, 3] out (forward) */
+} TgsShArgs;
+
+TGS_API int tgs_sh_fwd(const TgsShArgs* args, void* stream);
+
+typedef struct {
+  TgsShArgs fwd;              /* colors unused */
+  const float* v_colors;      /* [n, 3] */
+  float* v_coeffs;            /* [n, K, 3] out, every entry written */
+  float* v_dirs;              /* [n, 3] out, or NULL (not computed) */
+} TgsShBwdArgs;
+
+/* dL/dcoeffs[n, k, c] = v_colors[n, c] Y_k; dL/ddirs through the
+ * normalization (compute_sh_bwd.cu; v_dirs only when not NULL). */
+TGS_API int tgs_sh_bwd(const TgsShBwdArgs* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -51,7 +51,8 @@ GSPLAT_OUT = OUT / "gsplat"
 # the kernels of the engine's render path (projection, tile intersection,
 # rasterization), compiled with gsplat's own nvcc flags (its setup.py:79-94)
 GSPLAT_SOURCES = ("fully_fused_projection_fwd.cu", "fully_fused_projection_bwd.cu",
-                  "isect_tiles.cu", "rasterize_to_pixels_fwd.cu", "rasterize_to_pixels_bwd.cu")
+                  "isect_tiles.cu", "rasterize_to_pixels_fwd.cu", "rasterize_to_pixels_bwd.cu",
+                  "compute_sh_fwd.cu", "compute_sh_bwd.cu")
 
 
 def build_gsplat(root: Path, verbose: bool = False):

@@ -11,6 +11,8 @@ exact derivatives of the same forward:
   rasterize  rasterize_to_pixels_fwd.cu:15-158 (front-to-back compositing,
              alpha = min(0.999, o exp(-sigma)), skipped below 1/255, a pixel
              stops when its transmittance would reach 1e-4)
+  sh_colors  compute_sh_fwd.cu, spherical_harmonics.cuh:11-90 (real SH of
+             degree <= 4 at the normalized direction)
 Pinning: gsplat's Python reference (gsplat/cuda/_torch_impl.py) is not part
 of the reference checkout, and its CUDA kernels run only on a GPU; the GPU
 tests compare this oracle, tidegs_b200 and the reference kernels (compiled
@@ -135,6 +137,52 @@ def rasterize(means2d, conics, colors, opacities, width: int, height: int, tile_
         out_rows.append(full)
         alpha_rows.append(fa)
     return torch.stack(out_rows), torch.stack(alpha_rows)
+
+
+def sh_basis(degree: int, dirs: torch.Tensor) -> torch.Tensor:
+    """[..., (degree + 1)^2] real SH basis at dirs / |dirs| (float64), in the
+    order and signs 3D Gaussian splatting and gsplat use
+    (spherical_harmonics.cuh:11-90); the forms follow the reference's own
+    Sloan-style recurrences (products of z-polynomials with the cos / sin
+    multiple-angle terms C_m, S_m of (x, y)), not the closed polynomials the
+    CUDA kernel uses, so the two are independent restatements."""
+    n = dirs / dirs.norm(dim=-1, keepdim=True)
+    x, y, z = n.unbind(-1)
+    out = [torch.full_like(x, 0.28209479177387814)]
+    if degree >= 1:
+        out += [-0.48860251190292 * y, 0.48860251190292 * z, -0.48860251190292 * x]
+    if degree >= 2:
+        z2 = z * z
+        c1, s1 = x * x - y * y, 2 * x * y
+        t0b = -1.092548430592079 * z
+        sh6 = 0.9461746957575601 * z2 - 0.3153915652525201
+        out += [0.5462742152960395 * s1, t0b * y, sh6, t0b * x, 0.5462742152960395 * c1]
+    if degree >= 3:
+        c2, s2 = x * c1 - y * s1, x * s1 + y * c1
+        t0c = -2.285228997322329 * z2 + 0.4570457994644658
+        t1b = 1.445305721320277 * z
+        sh12 = z * (1.865881662950577 * z2 - 1.119528997770346)
+        out += [-0.5900435899266435 * s2, t1b * s1, t0c * y, sh12, t0c * x, t1b * c1,
+                -0.5900435899266435 * c2]
+    if degree >= 4:
+        c3, s3 = x * c2 - y * s2, x * s2 + y * c2
+        t0d = z * (-4.683325804901025 * z2 + 2.007139630671868)
+        t1c = 3.31161143515146 * z2 - 0.47308734787878
+        t2b = -1.770130769779931 * z
+        sh20 = 1.984313483298443 * z * sh12 - 1.006230589874905 * sh6
+        out += [0.6258357354491763 * s3, t2b * s2, t1c * s1, t0d * y, sh20, t0d * x, t1c * c1,
+                t2b * c2, 0.6258357354491763 * c3]
+    return torch.stack(out, dim=-1)
+
+
+def sh_colors(degree: int, dirs: torch.Tensor, coeffs: torch.Tensor, masks=None) -> torch.Tensor:
+    """[..., 3] = sum_k coeffs[..., k, :] Y_k (compute_sh_fwd.cu), zero where
+    masks is False; differentiable (autograd gives the reference backward)."""
+    K = (degree + 1) ** 2
+    col = (sh_basis(degree, dirs)[..., None] * coeffs[..., :K, :]).sum(dim=-2)
+    if masks is not None:
+        col = torch.where(masks[..., None], col, torch.zeros_like(col))
+    return col
 
 
 def look_at(eye, target, up=(0.0, 0.0, 1.0)) -> torch.Tensor:

@@ -262,3 +262,60 @@ def test_render_chain_against_oracle():
         _close(s.grad, ss.grad, 2e-3, "v_scales vs oracle")
     finally:
         W, H = w0, h0
+
+
+@pytest.mark.parametrize("degree,K", [(0, 1), (1, 4), (2, 16), (3, 16), (4, 25)])
+def test_spherical_harmonics_against_reference_and_oracle(degree, K):
+    from tidegs_b200.render import spherical_harmonics
+
+    g = torch.Generator().manual_seed(40 + degree)
+    N = 3000
+    dirs64 = torch.randn(2, N, 3, generator=g, dtype=torch.float64) * 5.0
+    coeffs64 = torch.randn(2, N, K, 3, generator=g, dtype=torch.float64) * 0.3
+    v64 = torch.randn(2, N, 3, generator=g, dtype=torch.float64)
+    dirs, coeffs, v = _cuda32(dirs64, coeffs64, v64)
+    d = dirs.clone().requires_grad_(True)
+    c = coeffs.clone().requires_grad_(True)
+    colors = spherical_harmonics(degree, d, c)
+    colors.backward(v)
+    # float64 oracle with autograd
+    d64 = dirs.double().cpu().requires_grad_(True)
+    c64 = coeffs.double().cpu().requires_grad_(True)
+    ocol = orc.sh_colors(degree, d64, c64)
+    ocol.backward(v.double().cpu())
+    _close(colors.detach(), ocol.detach(), 1e-5, "SH colors vs oracle")
+    _close(c.grad, c64.grad, 1e-5, "v_coeffs vs oracle")
+    # degree 0 is constant in the direction: no gradient reaches dirs
+    d64_grad = d64.grad if d64.grad is not None else torch.zeros_like(d64)
+    _close(d.grad, d64_grad, 1e-4, "v_dirs vs oracle", atol=0.0 if degree == 0 else None)
+    if K > (degree + 1) ** 2:
+        assert torch.all(c.grad[..., (degree + 1) ** 2:, :] == 0)
+    ref = _ref()
+    if ref is None or not hasattr(ref, "compute_sh_fwd"):
+        pytest.skip("reference gsplat SH kernels not built")
+    r_col = ref.compute_sh_fwd(degree, dirs, coeffs, None)
+    _close(colors.detach(), r_col, 1e-5, "SH colors vs reference")
+    r_vc, r_vd = ref.compute_sh_bwd(K, degree, dirs, coeffs, None, v, True)
+    _close(c.grad, r_vc, 1e-5, "v_coeffs vs reference")
+    _close(d.grad, r_vd, 1e-4, "v_dirs vs reference")
+
+
+def test_spherical_harmonics_masks_and_no_dir_gradient():
+    from tidegs_b200.render import spherical_harmonics
+
+    g = torch.Generator().manual_seed(5)
+    dirs, coeffs, v = _cuda32(torch.randn(1000, 3, generator=g), torch.randn(1000, 16, 3, generator=g),
+                              torch.randn(1000, 3, generator=g))
+    masks = (torch.rand(1000, generator=g) < 0.6).cuda()
+    c = coeffs.clone().requires_grad_(True)
+    colors = spherical_harmonics(3, dirs, c, masks)  # dirs without grad: no v_dirs
+    colors.backward(v)
+    assert torch.all(colors[~masks] == 0) and torch.all(c.grad[~masks] == 0)
+    full = spherical_harmonics(3, dirs, coeffs)
+    assert torch.equal(colors[masks], full[masks])
+    ref = _ref()
+    if ref is None or not hasattr(ref, "compute_sh_bwd"):
+        pytest.skip("reference gsplat SH kernels not built")
+    r_vc, _ = ref.compute_sh_bwd(16, 3, dirs, coeffs, masks, v, False)
+    _close(c.grad, r_vc, 1e-5, "masked v_coeffs vs reference")
+

@@ -183,6 +183,15 @@ class RasterBwdArgs(C.Structure):
     ]
 
 
+class ShArgs(C.Structure):
+    _fields_ = [("dirs", _vp), ("coeffs", _vp), ("masks", _vp), ("n", _i64), ("K", _i32),
+                ("degree", _i32), ("colors", _vp)]
+
+
+class ShBwdArgs(C.Structure):
+    _fields_ = [("fwd", ShArgs), ("v_colors", _vp), ("v_coeffs", _vp), ("v_dirs", _vp)]
+
+
 # name -> (restype, argtypes). Keep in sync with include/tidegs_b200.h.
 SIGNATURES = {
     "tgs_version": (C.c_int, []),
@@ -243,6 +252,8 @@ SIGNATURES = {
     "tgs_isect_offsets": (C.c_int, [_vp, _i64, _i32, _i32, _i32, _vp, _vp]),
     "tgs_rasterize_fwd": (C.c_int, [C.POINTER(RasterArgs), _vp]),
     "tgs_rasterize_bwd": (C.c_int, [C.POINTER(RasterBwdArgs), _vp]),
+    "tgs_sh_fwd": (C.c_int, [C.POINTER(ShArgs), _vp]),
+    "tgs_sh_bwd": (C.c_int, [C.POINTER(ShBwdArgs), _vp]),
 }
 
 _lock = threading.Lock()
@@ -294,7 +305,7 @@ KERNELS_PER_CALL = {
     "tgs_sparse_grad_accumulate": 1, "tgs_block_spheres": 1, "tgs_frustum_cull": 2,
     "tgs_project_fwd": 1, "tgs_project_bwd": 1, "tgs_isect_count": 1, "tgs_isect_write": 1,
     "tgs_isect_offsets": 1, "tgs_rasterize_fwd": 1, "tgs_rasterize_bwd": 1,
-    "tgs_isect_write_ordered": 1, "tgs_isect_expand_ids": 1,
+    "tgs_isect_write_ordered": 1, "tgs_isect_expand_ids": 1, "tgs_sh_fwd": 1, "tgs_sh_bwd": 1,
     # iota + the library radix sort and scan (their kernel counts depend on
     # the library version and are not counted here)
     "tgs_isect_depth_order": 1, "tgs_isect_sort_tiles": 0,

@@ -25,7 +25,7 @@ LIB_DIR = PKG_DIR / "lib"
 LIB_PATH = LIB_DIR / "libtidegs_b200.so"
 
 SOURCES = ("tgs_abi.cu", "tgs_adam.cu", "tgs_blocks.cu", "tgs_dirty.cu", "tgs_exchange.cu",
-           "tgs_sparse.cu", "tgs_cull.cu", "tgs_render.cu")
+           "tgs_sparse.cu", "tgs_cull.cu", "tgs_render.cu", "tgs_sh.cu")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",
@@ -45,7 +45,7 @@ _IEEE_FLAGS = ("-prec-div=true", "-prec-sqrt=true", "-ftz=false")
 # The render path is compared with the reference within tolerance and the
 # reference builds it with fast math (gsplat setup.py:81); every other file
 # keeps IEEE rounding (bit-exact parity).
-FAST_MATH_SOURCES = ("tgs_render.cu",)
+FAST_MATH_SOURCES = ("tgs_render.cu", "tgs_sh.cu")
 
 
 def _flags(name: str) -> list[str]:

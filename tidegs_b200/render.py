@@ -1,10 +1,11 @@
 """Render path before the optimizer, with gsplat 1.0.0's Python interface for
-the four calls the engine makes (strategies/tide_engine/engine.py:481-561):
-`fully_fused_projection`, `isect_tiles`, `isect_offset_encode` and
-`rasterize_to_pixels`, the first and last differentiable (autograd), so that
+the five calls the engine makes (strategies/tide_engine/engine.py:481-561):
+`fully_fused_projection`, `spherical_harmonics`, `isect_tiles`,
+`isect_offset_encode` and `rasterize_to_pixels`, the projection, the SH
+colors and the rasterization differentiable (autograd), so that
 `from tidegs_b200.render import ...` replaces `from gsplat import ...`.
 
-Kernels: tgs_project_fwd/bwd, tgs_isect_count/write/offsets,
+Kernels: tgs_project_fwd/bwd, tgs_sh_fwd/bwd, tgs_isect_count/write/offsets,
 tgs_rasterize_fwd/bwd (libtidegs_b200.so). The sorted intersections come
 from a stable sort of the Gaussians by depth and a stable sort of 32-bit
 (camera, tile) keys (cub radix sorts, as gsplat sorts with cub) instead of
@@ -24,7 +25,7 @@ import torch
 from . import _lib
 
 __all__ = ["fully_fused_projection", "isect_tiles", "isect_offset_encode", "rasterize_to_pixels",
-           "rasterize_to_pixels_fwd", "rasterize_to_pixels_bwd"]
+           "rasterize_to_pixels_fwd", "rasterize_to_pixels_bwd", "spherical_harmonics"]
 
 
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
@@ -327,3 +328,57 @@ def rasterize_to_pixels(means2d: torch.Tensor, conics: torch.Tensor, colors: tor
         raise ValueError("rasterize_to_pixels: inputs must be [C, N, ...] with C cameras")
     return _Rasterize.apply(means2d, conics, colors, opacities, backgrounds, int(image_width),
                             int(image_height), int(tile_size), isect_offsets, flatten_ids, absgrad)
+
+
+class _SphericalHarmonics(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, degree, dirs, coeffs, masks):
+        dirs_, coeffs_ = _f32(dirs, "dirs"), _f32(coeffs, "coeffs")
+        masks_ = None if masks is None else masks.detach().to(torch.bool).contiguous()
+        colors = torch.empty(dirs_.shape, dtype=torch.float32, device=dirs_.device)
+        a = _sh_args(degree, dirs_, coeffs_, masks_)
+        a.colors = colors.data_ptr()
+        _lib.call("tgs_sh_fwd", a, _stream(dirs_))
+        ctx.save_for_backward(dirs_, coeffs_, masks_)
+        ctx.degree = degree
+        return colors
+
+    @staticmethod
+    def backward(ctx, v_colors):
+        dirs, coeffs, masks = ctx.saved_tensors
+        v_colors = v_colors.to(torch.float32).contiguous()
+        v_coeffs = torch.empty_like(coeffs)
+        v_dirs = torch.empty_like(dirs) if ctx.needs_input_grad[1] else None
+        b = _lib.ShBwdArgs()
+        b.fwd = _sh_args(ctx.degree, dirs, coeffs, masks)
+        b.v_colors, b.v_coeffs, b.v_dirs = v_colors.data_ptr(), v_coeffs.data_ptr(), _ptr(v_dirs)
+        _lib.call("tgs_sh_bwd", b, _stream(dirs))
+        return None, v_dirs, v_coeffs, None
+
+
+def _sh_args(degree, dirs, coeffs, masks) -> "_lib.ShArgs":
+    a = _lib.ShArgs()
+    a.dirs, a.coeffs, a.masks = dirs.data_ptr(), coeffs.data_ptr(), _ptr(masks)
+    a.n, a.K, a.degree = dirs.numel() // 3, int(coeffs.shape[-2]), int(degree)
+    return a
+
+
+def spherical_harmonics(degrees_to_use: int, dirs: torch.Tensor, coeffs: torch.Tensor,
+                        masks: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """[..., 3] colors from SH coefficients [..., K, 3] evaluated at the
+    directions [..., 3] (normalized inside), using the first
+    (degrees_to_use + 1)^2 coefficients; differentiable in dirs and coeffs
+    (gsplat 1.0.0 spherical_harmonics). Masked-out entries (masks [...]
+    False) give zero colors and zero gradients."""
+    if dirs.shape[-1] != 3 or coeffs.shape[-1] != 3:
+        raise ValueError("spherical_harmonics: dirs and coeffs must have last dimension 3")
+    if coeffs.shape[:-2] != dirs.shape[:-1]:
+        raise ValueError(f"spherical_harmonics: coeffs {tuple(coeffs.shape)} and dirs "
+                         f"{tuple(dirs.shape)} do not share their leading dimensions")
+    if not 0 <= degrees_to_use <= 4 or (degrees_to_use + 1) ** 2 > coeffs.shape[-2]:
+        raise ValueError(f"spherical_harmonics: degree {degrees_to_use} needs "
+                         f"{(degrees_to_use + 1) ** 2} coefficients, coeffs has "
+                         f"{coeffs.shape[-2]}")
+    if masks is not None and masks.shape != dirs.shape[:-1]:
+        raise ValueError("spherical_harmonics: masks must have dirs' leading shape")
+    return _SphericalHarmonics.apply(int(degrees_to_use), dirs, coeffs, masks)

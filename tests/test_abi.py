@@ -53,6 +53,29 @@ def test_empty_work_is_a_no_op_without_device():
     assert lib.tgs_block_bounds(None, None, None, 0, None, None) == 0
     assert lib.tgs_compact_scratch_words(0) == 1
     assert lib.tgs_compact_scratch_words(2049) == 3
+    sh = _lib.ShArgs()
+    sh.n, sh.K, sh.degree = 0, 16, 3
+    assert lib.tgs_sh_fwd(ctypes.byref(sh), None) == 0
+    assert lib.tgs_isect_depth_order(None, None, 0, None, None, None, 0, None) == 0
+    assert lib.tgs_isect_expand_ids(None, 2, None, None, 0, None, None) == 0
+
+
+def test_render_argument_checks_without_device():
+    lib = _lib.load()
+    sh = _lib.ShArgs()
+    sh.n, sh.K, sh.degree = 5, 9, 3  # degree 3 needs 16 coefficients
+    assert lib.tgs_sh_fwd(ctypes.byref(sh), None) == 1
+    assert "degree 3" in _lib.last_error()
+    sh.K, sh.degree = 26, 4  # at most 25 coefficients
+    assert lib.tgs_sh_fwd(ctypes.byref(sh), None) == 1
+    # key widths: 13 bits (one camera, 120 x 68 tiles) fit 16-bit keys; 70
+    # cameras at 4K (240 x 135 tiles) need 32-bit keys; beyond 32 bits: none
+    assert lib.tgs_isect_key_bytes(1, 120, 68) == 2
+    assert lib.tgs_isect_key_bytes(70, 240, 135) == 4
+    assert lib.tgs_isect_key_bytes(65535, 65535, 2) == 0
+    assert lib.tgs_isect_sort_tiles(None, None, 10, 65535, 65535, 2, None, None, None, 0,
+                                    None) == 1
+    assert lib.tgs_isect_tile_bits(8160) == 13
 
 
 def test_struct_layouts_match_the_header_sizes():
@@ -76,7 +99,7 @@ def test_struct_offsets_match_the_c_compiler(tmp_path):
         "ResidentCountArgs", "ResidentAdamArgs", "DenseGroup", "DenseArgs", "UnpackArgs",
         "CopyBlocksArgs", "PackArgs", "BlockSumArgs", "GradPushArgs", "PeerHandle",
         "ResidentAdamSumArgs", "SparseAccumArgs", "CullArgs", "ProjectArgs",
-        "ProjectBwdArgs", "RasterArgs", "RasterBwdArgs")}
+        "ProjectBwdArgs", "RasterArgs", "RasterBwdArgs", "ShArgs", "ShBwdArgs")}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "tidegs_b200.h"',
              'int main(void) {']
     expect = []

@@ -407,26 +407,31 @@ __global__ void iota_kernel(int32_t* __restrict__ out, int64_t n) {
   if (i < n) out[i] = static_cast<int32_t>(i);
 }
 
-// One warp writes the tiles of its 32 Gaussians one Gaussian after another,
-// the lanes covering consecutive entries (coalesced, and a Gaussian with
-// many tiles is spread over the warp instead of one thread).
+// One warp per 32 consecutive Gaussians in depth order. Their entries are
+// one contiguous output range (cum is the prefix sum in that order), so the
+// lanes write entries lane, lane + 32, ... of the range (coalesced, every
+// lane busy whatever the Gaussians' sizes); an entry's Gaussian is found by
+// binary search over the warp's inclusive entry counts in shared memory.
+constexpr int kWriteThreads = 256;
 template <typename KeyT>
-__global__ void isect_write_ordered_kernel(const float* __restrict__ means2d,
-                                           const int32_t* __restrict__ radii,
-                                           const float* __restrict__ depths,
-                                           const int32_t* __restrict__ order, int64_t n,
-                                           int64_t per_camera, int tile_size, int tile_width,
-                                           int tile_height, int tile_bits, uint32_t key_mask,
-                                           const int64_t* __restrict__ cum,
-                                           KeyT* __restrict__ tile_keys,
-                                           int32_t* __restrict__ flatten) {
+__global__ void __launch_bounds__(kWriteThreads) isect_write_ordered_kernel(
+    const float* __restrict__ means2d, const int32_t* __restrict__ radii,
+    const float* __restrict__ depths, const int32_t* __restrict__ order, int64_t n,
+    int64_t per_camera, int tile_size, int tile_width, int tile_height, int tile_bits,
+    uint32_t key_mask, const int64_t* __restrict__ cum, KeyT* __restrict__ tile_keys,
+    int32_t* __restrict__ flatten) {
   constexpr unsigned kAll = 0xffffffffu;
-  const int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-  const int lane = threadIdx.x & 31;
+  constexpr int kWarps = kWriteThreads / 32;
+  __shared__ int s_end[kWarps][32];
+  __shared__ int s_x0[kWarps][32], s_y0[kWarps][32], s_w[kWarps][32];
+  __shared__ uint32_t s_hi[kWarps][32];
+  __shared__ int32_t s_id[kWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t j = blockIdx.x * static_cast<int64_t>(kWriteThreads) + threadIdx.x;
+  const int64_t j0 = j - lane;
   int32_t i = 0;
   int count = 0, x0 = 0, y0 = 0, w = 1;
   uint32_t hi = 0;
-  int64_t out = 0;
   if (j < n) {
     i = order[j];
     const int32_t r = radii[i];
@@ -441,27 +446,38 @@ __global__ void isect_write_ordered_kernel(const float* __restrict__ means2d,
       // all ones for a negative depth (the sign-extended reference key)
       hi = __float_as_int(depths[i]) < 0 ? key_mask
                                          : static_cast<uint32_t>(i / per_camera) << tile_bits;
-      out = j == 0 ? 0 : cum[j - 1];
     }
   }
-  unsigned todo = __ballot_sync(kAll, count > 0);
-  while (todo) {
-    const int src = __ffs(todo) - 1;
-    todo &= todo - 1;
-    const int c = __shfl_sync(kAll, count, src);
-    const int sw = __shfl_sync(kAll, w, src);
-    const int sx = __shfl_sync(kAll, x0, src);
-    const int sy = __shfl_sync(kAll, y0, src);
-    const uint32_t sh = __shfl_sync(kAll, hi, src);
-    const int32_t sg = __shfl_sync(kAll, i, src);
-    const int64_t so = __shfl_sync(kAll, out, src);
-    const bool all_ones = sh == key_mask;
-    for (int e = lane; e < c; e += 32) {
-      const int row = e / sw;
-      const uint32_t tile = static_cast<uint32_t>((sy + row) * tile_width + sx + (e - row * sw));
-      tile_keys[so + e] = static_cast<KeyT>(all_ones ? key_mask : (sh | tile));
-      flatten[so + e] = sg;
-    }
+  int incl = count;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(kAll, incl, o);
+    if (lane >= o) incl += v;
+  }
+  s_end[warp][lane] = incl;
+  s_x0[warp][lane] = x0;
+  s_y0[warp][lane] = y0;
+  s_w[warp][lane] = w;
+  s_hi[warp][lane] = hi;
+  s_id[warp][lane] = i;
+  __syncwarp();
+  const int total = __shfl_sync(kAll, incl, 31);
+  if (j0 >= n || total == 0) return;
+  const int64_t base = j0 == 0 ? 0 : cum[j0 - 1];
+  for (int e = lane; e < total; e += 32) {
+    // owner: the number of Gaussians whose entries end at or before e
+    int g = 0;
+#pragma unroll
+    for (int step = 16; step >= 1; step >>= 1)
+      if (s_end[warp][g + step - 1] <= e) g += step;
+    const int local = e - (g == 0 ? 0 : s_end[warp][g - 1]);
+    const int sw = s_w[warp][g];
+    const int row = local / sw;
+    const uint32_t tile = static_cast<uint32_t>((s_y0[warp][g] + row) * tile_width +
+                                                s_x0[warp][g] + (local - row * sw));
+    const uint32_t sh = s_hi[warp][g];
+    tile_keys[base + e] = static_cast<KeyT>(sh == key_mask ? key_mask : (sh | tile));
+    flatten[base + e] = s_id[warp][g];
   }
 }
 
@@ -1031,15 +1047,15 @@ extern "C" int tgs_isect_write_ordered(const float* means2d, const int32_t* radi
   const int bits = isect_key_bits(n_cameras, n_tiles);
   TGS_CHECK_ARG(bits <= 32, "tgs_isect_write_ordered: camera and tile ids need %d bits", bits);
   const uint32_t mask = static_cast<uint32_t>((1ull << bits) - 1);
-  const unsigned grid = static_cast<unsigned>(ceil_div<int64_t>(n, 256));
+  const unsigned grid = static_cast<unsigned>(ceil_div<int64_t>(n, kWriteThreads));
   cudaStream_t s = as_stream(stream);
   if (bits <= 16)
-    isect_write_ordered_kernel<uint16_t><<<grid, 256, 0, s>>>(
+    isect_write_ordered_kernel<uint16_t><<<grid, kWriteThreads, 0, s>>>(
         means2d, radii, depths, order, n, n_per_camera, tile_size, tile_width, tile_height,
         tgs_isect_tile_bits(n_tiles), mask, cum_tiles, static_cast<uint16_t*>(tile_keys),
         flatten_ids);
   else
-    isect_write_ordered_kernel<uint32_t><<<grid, 256, 0, s>>>(
+    isect_write_ordered_kernel<uint32_t><<<grid, kWriteThreads, 0, s>>>(
         means2d, radii, depths, order, n, n_per_camera, tile_size, tile_width, tile_height,
         tgs_isect_tile_bits(n_tiles), mask, cum_tiles, static_cast<uint32_t*>(tile_keys),
         flatten_ids);

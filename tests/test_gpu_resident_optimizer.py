@@ -163,6 +163,61 @@ def test_large_random_steps_bit_exact_with_oracle():
     assert opt.get_stats()["state_evictions"] == oracle.stats["state_evictions"]
 
 
+def test_full_resident_set_sampled_blocks_bit_exact():
+    """BASELINE configs[3] size: 2048 resident blocks x 16,384 rows (33.5 M
+    Gaussians, parameters and moments ~24 GB on the device), Bernoulli(0.3)
+    touched rows, two steps. The update of a row depends only on its own
+    values and its block's slot tables, so the oracle replaying 12 sampled
+    blocks alone (same rows, same gradients) must match the full-size GPU
+    result on those blocks bit for bit."""
+    from tidegs_b200 import GPUResidentAdam
+
+    B, nb = 16384, 2048
+    rows = B * nb
+    rng = np.random.default_rng(17)
+    order = rng.permutation(nb * 4)[:nb].tolist()
+    layout = [(int(b), slice(i * B, (i + 1) * B)) for i, b in enumerate(order)]
+    lrs = [1.6e-4, 0.05, 5e-3, 1e-3, 2.5e-3, 1.25e-4]
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    manager = _Manager(layout)
+    gaussians = _Gaussians.__new__(_Gaussians)
+    gaussians.gpu_working_set_manager = manager
+    gaussians.optimizer = types.SimpleNamespace(
+        columns_lr=torch.tensor(lrs, dtype=torch.float32),
+        param_groups=[{"betas": (0.9, 0.999), "eps": 1e-15}])
+    for n in NAMES:
+        setattr(gaussians, ATTRS[n], torch.nn.Parameter(
+            torch.randn((rows, WIDTHS[n]), generator=gen, device="cuda")))
+    sample = np.sort(rng.choice(nb, 12, replace=False))
+    sub_rows = np.concatenate([np.arange(k * B, (k + 1) * B) for k in sample])
+    sub_rows_t = torch.as_tensor(sub_rows, device="cuda")
+    ref = {n: getattr(gaussians, ATTRS[n]).detach()[sub_rows_t].cpu().numpy() for n in NAMES}
+    sub_layout = [(order[k], slice(i * B, (i + 1) * B)) for i, k in enumerate(sample)]
+    opt = GPUResidentAdam(batch_size=16, block_size=B, capacity_blocks=nb, device="cuda")
+    oracle = ResidentAdamOracle(batch_size=16, block_size=B, capacity_blocks=len(sample))
+    opt.set_resident_blocks([b for b, _ in layout])
+    oracle.set_resident_blocks([b for b, _ in sub_layout])
+    for step in range(2):
+        ids = torch.nonzero(torch.rand(rows, generator=gen, device="cuda") < 0.3).view(-1)
+        grads = {n: torch.randn((ids.numel(), w), generator=gen, device="cuda") * 1e-3
+                 for n, w in WIDTHS.items()}
+        stats = opt.step(step, gaussians, ids, grads)
+        assert stats["touched_rows"] == ids.numel()
+        # the sampled blocks' share of this step, renumbered into the subset
+        ids_h = ids.cpu().numpy()
+        blk = ids_h // B
+        keep = np.isin(blk, sample)
+        pos = np.nonzero(keep)[0]
+        sub_ids = np.searchsorted(sample, blk[keep]) * B + ids_h[keep] % B
+        pos_t = torch.as_tensor(pos, device="cuda")
+        sub_grads = {n: g[pos_t].cpu().numpy() for n, g in grads.items()}
+        oracle.step(ref, sub_ids, sub_grads, sub_layout, lrs, (0.9, 0.999), 1e-15)
+        for n in NAMES:
+            got = getattr(gaussians, ATTRS[n]).detach()[sub_rows_t].cpu().numpy()
+            np.testing.assert_array_equal(got, ref[n], err_msg=f"{n} step {step}")
+        del grads
+
+
 def _small_setup():
     from tidegs_b200 import GPUResidentAdam
 

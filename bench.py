@@ -101,6 +101,11 @@ def plan_host_pool(world: int, host_tier: str, pool_blocks: int, limit: int):
     return 4, host_tier
 
 
+WORKLOAD_CONFIG = {
+    "workload": "configs[3]: full resident-set step, 2048 slots x 16384 Gaussians per GPU, "
+                "16-camera contiguous block runs (~30% visible), 25% slot turnover, "
+                "Bernoulli(0.5) dirty evictions"}
+
 WIDTHS = {"xyz": 3, "opacity": 1, "scaling": 3, "rotation": 4, "features_dc": 3,
           "features_rest": 45}
 NAMES = tuple(WIDTHS)
@@ -1278,6 +1283,8 @@ def cpu_baseline(seconds_budget: float = 12.0):
     elapsed = time.perf_counter() - t0
     return {
         "value": done_rows / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
+        # one full-size step (SLOTS slots) at the sample's rate
+        "ms_per_step": 1e3 * (n * SLOTS / slots) / (done_rows / elapsed),
         "sample": (f"{slots} slots x {Bs} rows (1/32 of a GPU's resident set), 30% blocks "
                    f"visible ({n} rows), 25% turnover, {steps} steps in {elapsed:.1f} s: "
                    "reference torch CPU step (gpu_resident_optimizer.py:339-364 ported), "
@@ -1294,9 +1301,13 @@ def run_reference_arm(args, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": base["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded, BASELINE configs[3] shapes)",
-        "config": {"workload": "configs[3] full resident-set step (sampled on the host CPU)"},
+        "data": "synthetic (seeded, BASELINE configs[3] shapes and distributions)",
+        "config": dict(WORKLOAD_CONFIG, slots_per_gpu=SLOTS, block_size=B,
+                       turnover_blocks=TURNOVER,
+                       run="the reference's CPU step on a bounded sample of this workload "
+                           "(cpu_baseline.sample), all host threads, rank 0 only"),
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -1467,9 +1478,7 @@ def main(argv=None):
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded, BASELINE configs[3] shapes and distributions)",
-            "config": {"workload": "configs[3]: full resident-set step, 2048 slots x 16384 "
-                                   "Gaussians per GPU, 16-camera contiguous block runs (~30% "
-                                   "visible), 25% slot turnover, Bernoulli(0.5) dirty evictions",
+            "config": {**WORKLOAD_CONFIG,
                        "slots_per_gpu": SLOTS, "block_size": B, "turnover_blocks": TURNOVER,
                        "scene_blocks_per_gpu": POOL_MULT * SLOTS,
                        "rows_updated_per_step": rows / args.steps,

@@ -132,3 +132,18 @@ def test_no_cpu_fallback_without_cuda():
         GPUResidentAdam(device="cuda")
     with pytest.raises(RuntimeError, match="no CPU path"):
         GPUResidentAdam(device="cpu")
+
+
+def test_nvtx_ranges_wrap_calls_when_enabled(monkeypatch):
+    calls = []
+    monkeypatch.setattr(_lib, "NVTX", True)
+    import torch
+
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda n: calls.append(("push", n)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: calls.append(("pop",)))
+    _lib.call("tgs_fill_global_ids", None, 0, None, 0, 4, None)  # no work: no device needed
+    with pytest.raises(RuntimeError, match="tgs_copy_blocks"):
+        _lib.call("tgs_copy_blocks", None, None)
+    assert calls == [("push", "tgs_fill_global_ids"), ("pop",), ("push", "tgs_copy_blocks"),
+                     ("pop",)]
+

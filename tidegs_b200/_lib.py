@@ -313,10 +313,22 @@ KERNELS_PER_CALL = {
 launch_counter = {"kernels": 0}
 
 
+# TIDEGS_NVTX=1: every entry point call is an NVTX range named after it (for
+# Nsight timelines; off by default, a push/pop costs about a microsecond).
+NVTX = os.environ.get("TIDEGS_NVTX", "0") not in ("", "0")
+
+
 def call(name: str, *args) -> None:
     """Calls entry point `name`; raises RuntimeError with the library message."""
     lib = load()
-    status = getattr(lib, name)(*args)
+    if NVTX:
+        torch.cuda.nvtx.range_push(name)
+        try:
+            status = getattr(lib, name)(*args)
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        status = getattr(lib, name)(*args)
     if status != 0:
         raise RuntimeError(f"[tidegs_b200] {name} failed (status {status}): {last_error()}")
     launch_counter["kernels"] += KERNELS_PER_CALL.get(name, 0)

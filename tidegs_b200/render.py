@@ -158,7 +158,8 @@ def isect_tiles(means2d: torch.Tensor, radii: torch.Tensor, depths: torch.Tensor
                       flatten_ids.data_ptr(), s)
         return tiles, isect_ids, flatten_ids
     # sorted: Gaussians in depth order, their tiles emitted in that order with
-    # 32-bit (camera, tile) keys, a stable sort of those, 64-bit keys put back
+    # 16- or 32-bit (camera, tile) keys, a stable sort of those, the 64-bit
+    # keys put back
     order = torch.empty(n, dtype=torch.int32, device=dev)
     cum = torch.empty(n, dtype=torch.int64, device=dev)
     scratch = _scratch(dev, "tgs_isect_depth_order_scratch_bytes", n)

@@ -1,15 +1,20 @@
 /*
  * tidegs_b200.h -- C ABI of libtidegs_b200.so, the sm_100a implementation of
- * TideGS's resident-block optimizer / materialization / write-back hot path.
+ * TideGS's resident-block optimizer / materialization / write-back hot path,
+ * and of the steps either side of it: touched-only gradient accumulation,
+ * per-block host DMAs, block frustum culling, and the gsplat render kernels
+ * (projection, SH colors, tile intersection, rasterization).
  *
  * Conventions shared by every entry point:
  *   - Plain pointers and sizes only. Every pointer named dev_* / inside an args
  *     struct is a DEVICE pointer unless its comment says "host".
  *   - The library allocates nothing and keeps no per-call state: every buffer,
  *     including scratch words, is owned by the caller. Calls are re-entrant and
- *     may come from several host threads on different streams. The one
- *     exception is tgs_peer_buffer_alloc, which allocates the exportable
- *     buffer its caller asks for and hands its ownership to that caller.
+ *     may come from several host threads on different streams. Two
+ *     exceptions: tgs_peer_buffer_alloc allocates the exportable buffer its
+ *     caller asks for and hands its ownership to that caller, and
+ *     tgs_global_to_local_compact_noalloc keeps fixed per-device scratch
+ *     inside the library (see its declaration).
  *   - `stream` is a cudaStream_t passed as void* (0 = legacy default stream).
  *     All work is enqueued on it; no entry point synchronizes the device.
  *   - Return value: 0 (TGS_OK) or a TGS_ERR_* code. The message of the last

@@ -176,30 +176,26 @@ def _updated_recency(previous, accessed: np.ndarray, decay: float):
         out = RecencyScores(vals)
         return out, out.lookup
     prev = previous or {}
-    try:
-        keys = np.fromiter(prev.keys(), np.int64, len(prev))
-        vals = np.fromiter(prev.values(), np.float64, len(prev))
-    except (TypeError, ValueError):
-        keys = np.fromiter((int(k) for k in prev.keys()), np.int64, len(prev))
-        vals = np.fromiter((float(v) for v in prev.values()), np.float64, len(prev))
-    vals = vals * float(decay)
-    keep = vals > _DROP_BELOW
-    keys, vals = keys[keep], vals[keep]
-    updated = dict(zip(keys.tolist(), vals.tolist()))
+    decay = float(decay)
+    if type(prev) is dict and _last_returned[0] == id(prev) and _last_returned[1] == len(prev):
+        # the dict this function returned last (int keys, float values
+        # already): no per-entry conversions
+        updated = {b: d for b, s in prev.items() if (d := s * decay) > _DROP_BELOW}
+    else:
+        updated = {int(b): d for b, s in prev.items() if (d := float(s) * decay) > _DROP_BELOW}
     updated.update(dict.fromkeys(accessed.tolist(), 1.0))
-    order = np.argsort(keys, kind="stable")
-    sk, sv = keys[order], vals[order]
+    _last_returned[:] = [id(updated), len(updated)]
+    get = updated.get
 
     def lookup(ids: np.ndarray) -> np.ndarray:
-        out = np.zeros(ids.size, np.float64)
-        if sk.size:
-            pos = np.minimum(np.searchsorted(sk, ids), sk.size - 1)
-            hit = sk[pos] == ids
-            out[hit] = sv[pos[hit]]
-        out[_member(ids, accessed)] = 1.0
-        return out
+        return np.fromiter((get(b, 0.0) for b in ids.tolist()), np.float64, ids.size)
 
     return updated, lookup
+
+
+# (id, length) of the last recency dict _updated_recency returned: the
+# runtime passes it back as the next transition's previous scores
+_last_returned: list = [None, -1]
 
 
 def _normalized_cameras(camera_blocks, allowed: Optional[np.ndarray]) -> List[Tuple[int, np.ndarray]]:

@@ -60,3 +60,20 @@ def test_recency_scores_mapping():
     assert dict(tr.updated_recency_scores) == {1: 1.0, 2: 1.0, 5: 0.25}
     empty = rp.compute_topc_resident_transition([], [], resident_capacity_blocks=4)
     assert empty.next_resident_blocks == [] and empty.topc_cutoff_score == 0.0
+
+
+def test_recency_update_fast_path_equals_converting_path():
+    """The returned dict passed back (no per-entry conversions) and a copy of
+    it (converted like the reference converts foreign dicts) give the same
+    scores; foreign key / value types are converted to int / float."""
+    import numpy as np
+
+    prev = {np.int64(5): np.float64(0.5), 7: 1e-6, "9": 0.3, 11: np.float32(0.25)}
+    upd, look = rp._updated_recency(prev, np.array([3, 5]), 0.9)
+    assert upd == {5: 1.0, 9: 0.27, 11: np.float32(0.25) * 0.9, 3: 1.0}
+    assert all(type(k) is int for k in upd) and all(type(v) is float for v in upd.values())
+    np.testing.assert_array_equal(look(np.array([3, 100, 9])), [1.0, 0.0, 0.27])
+    fast, _ = rp._updated_recency(upd, np.array([100]), 0.5)     # the dict returned last
+    slow, _ = rp._updated_recency(dict(upd), np.array([100]), 0.5)  # a foreign copy
+    assert fast == slow and list(fast.items()) == list(slow.items())
+

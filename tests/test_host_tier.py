@@ -328,3 +328,41 @@ def test_cache_over_block_log_round_trip(tmp_path):
     finally:
         cache.shutdown()
         st.close()
+
+
+def test_tail_block_round_trip(tmp_path):
+    """A scene whose last block is short (total rows not a multiple of the
+    block size): its write-back entry holds only its rows, the patch stores
+    only those rows, and the block comes back with that shape from the cache
+    and from the log; the reader packs it with its real row count."""
+    B, NB, tail = 8, 5, 3
+    st = BlockLogStore(str(tmp_path), B, NB, point_dim=G.POINT_DIM, verbose=False)
+    base = torch.cat([G.block_data(60_000 + b, B) for b in range(NB)])
+    st.file_paths[0].write_bytes(base.numpy().tobytes())
+    cache = PinnedBlockCache(st, max_ram_gb=1.0, block_size=B, point_dim=G.POINT_DIM,
+                             verbose=False, capacity_blocks=8, pin_memory=False)
+    try:
+        plans = [(1, B), (NB - 1, tail)]
+        views = cache.reserve_writeback(plans)
+        new = {b: G.block_data(70_000 + b, rows) for b, rows in plans}
+        for (b, _), v in zip(plans, views):
+            assert v.shape == new[b].shape
+            v.copy_(new[b])
+        cache.commit_writeback(plans, views)
+        got = cache.prefetch([NB - 1, 1])
+        assert torch.equal(got[NB - 1], new[NB - 1]) and torch.equal(got[1], new[1])
+        with pytest.raises(ValueError, match="rows"):
+            cache.reserve_writeback([(2, B + 1)])
+        cache.flush_all_dirty()
+        cache.drain()
+        assert st.index[NB - 1].size == tail * G.POINT_DIM * 4
+        back = st.read_blocks([NB - 1, 1, 0])
+        assert torch.equal(back[NB - 1], new[NB - 1]) and torch.equal(back[1], new[1])
+        assert torch.equal(back[0], base[:B])
+        reader = CachedBlockReader(cache, (NB - 1) * B + tail, B)
+        batch = reader.read_batch([NB - 1, 1])
+        assert torch.equal(batch.tensor, torch.cat([new[NB - 1], new[1]]))
+    finally:
+        cache.shutdown()
+        st.close()
+

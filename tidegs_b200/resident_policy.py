@@ -177,14 +177,14 @@ def _updated_recency(previous, accessed: np.ndarray, decay: float):
         return out, out.lookup
     prev = previous or {}
     decay = float(decay)
-    if type(prev) is dict and _last_returned[0] == id(prev) and _last_returned[1] == len(prev):
+    if prev is _last_returned[0] and len(prev) == _last_returned[1]:
         # the dict this function returned last (int keys, float values
         # already): no per-entry conversions
         updated = {b: d for b, s in prev.items() if (d := s * decay) > _DROP_BELOW}
     else:
         updated = {int(b): d for b, s in prev.items() if (d := float(s) * decay) > _DROP_BELOW}
     updated.update(dict.fromkeys(accessed.tolist(), 1.0))
-    _last_returned[:] = [id(updated), len(updated)]
+    _last_returned[:] = [updated, len(updated)]
     get = updated.get
 
     def lookup(ids: np.ndarray) -> np.ndarray:
@@ -193,8 +193,10 @@ def _updated_recency(previous, accessed: np.ndarray, decay: float):
     return updated, lookup
 
 
-# (id, length) of the last recency dict _updated_recency returned: the
-# runtime passes it back as the next transition's previous scores
+# The last recency dict _updated_recency returned and its length (held, so
+# that the identity test cannot match a different dict at a reused
+# address): the runtime passes it back as the next transition's previous
+# scores.
 _last_returned: list = [None, -1]
 
 

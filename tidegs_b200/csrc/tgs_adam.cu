@@ -187,6 +187,32 @@ struct __align__(16) RowScale {
   uint32_t pad;
 };
 
+// Resolves the chunk's rows (lane l: row row0 + l) into the warp's tables and
+// returns, uniformly across the warp, whether the chunk is contiguous: 32 rows
+// whose ids AND state rows both advance by one from lane to lane. Every lane
+// checks its own row; ends alone do not decide it, because with blocks
+// shorter than 32 rows consecutive ids can sit in slots out of order (slots
+// 0,5,2,.. of 4-row blocks) while the first and last rows still line up.
+__device__ __forceinline__ bool resolve_chunk_rows(const ResidentApplyParams& a, int64_t row0,
+                                                   int nr, int lane, RowAddr* addr,
+                                                   RowScale* scale) {
+  int64_t id = 0, sr = 0;
+  if (lane < nr) {
+    id = a.ids[row0 + lane];
+    const int p = find_position(a.pos_start, a.pos_end, a.n_pos, a.block_size, id);
+    const int s = __ldg(a.pos_slot + p);
+    const float2 bb = a.slot_bias[s];
+    sr = static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p));
+    addr[lane] = {id, sr};
+    scale[lane] = {bb.x, bb.y, __ldg(a.slot_stamp + s), 0u};
+  }
+  const unsigned full = 0xffffffffu;
+  const int64_t id0 = __shfl_sync(full, id, 0);
+  const int64_t sr0 = __shfl_sync(full, sr, 0);
+  __syncwarp();
+  return __all_sync(full, nr == 32 && id == id0 + lane && sr == sr0 + lane) != 0;
+}
+
 // Contiguous chunks (32 consecutive ids whose state rows are consecutive,
 // e.g. all rows of visible blocks) take a staged path: lane 0 copies the state
 // rows of the warp's next kStateBatch-row batches with one non-multicast bulk
@@ -261,20 +287,13 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
     const int64_t row0 = chunk * 32;
     const int nr = static_cast<int>(min64(32, a.n - row0));
 
-    if (lane < nr) {
-      const int64_t id = a.ids[row0 + lane];
-      const int p = find_position(a.pos_start, a.pos_end, a.n_pos, a.block_size, id);
-      const int s = __ldg(a.pos_slot + p);
-      const float2 bb = a.slot_bias[s];
-      s_addr[warp][lane] = {id, static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p))};
-      s_scale[warp][lane] = {bb.x, bb.y, __ldg(a.slot_stamp + s), 0u};
-    }
+    const bool contiguous = resolve_chunk_rows(a, row0, nr, lane, s_addr[warp], s_scale[warp]);
     __syncwarp();
 
     const float* gptr0 = gbase[0] + row0 * width[0];
     const float* gptr1 = gbase[1] + row0 * width[1];
     const RowAddr first = s_addr[warp][0];
-    if (nr == 32 && s_addr[warp][31].id == first.id + 31 && s_addr[warp][31].sr == first.sr + 31) {
+    if (contiguous) {
       // staged path: state rows first.sr .. first.sr + 31 are contiguous
       const float4* src = a.state + first.sr * 32;
       if (lane == 0) {
@@ -525,14 +544,7 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
     const int64_t row0 = chunk * 32;
     const int nr = static_cast<int>(min64(32, a.n - row0));
 
-    if (lane < nr) {
-      const int64_t id = a.ids[row0 + lane];
-      const int p = find_position(a.pos_start, a.pos_end, a.n_pos, a.block_size, id);
-      const int s = __ldg(a.pos_slot + p);
-      const float2 bb = a.slot_bias[s];
-      s_addr[warp][lane] = {id, static_cast<int64_t>(s) * a.block_size + (id - __ldg(a.pos_start + p))};
-      s_scale[warp][lane] = {bb.x, bb.y, __ldg(a.slot_stamp + s), 0u};
-    }
+    const bool contiguous = resolve_chunk_rows(a, row0, nr, lane, s_addr[warp], s_scale[warp]);
     // Segment of the chunk's first row (first s with seg_begin[s + 1] > row0),
     // resolved by lane 0; the chunk takes the fast path when its last row is
     // in the same segment.
@@ -587,8 +599,7 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
         }
       };
       const RowAddr first = s_addr[warp][0];
-      if (nr == 32 && s_addr[warp][31].id == first.id + 31 &&
-          s_addr[warp][31].sr == first.sr + 31) {
+      if (contiguous) {
         // Contiguous chunk: state rows staged by bulk copies as in kernel C;
         // the next batch's parameters and contributions load into registers
         // while the current batch updates.

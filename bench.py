@@ -49,10 +49,6 @@ SLOTS = 2048
 TURNOVER = 512
 
 
-# scene blocks a rank owns = POOL_MULT * SLOTS (4: BASELINE configs[3]'s
-# pinned pool); lowered by plan_host_pool when the box's memory cannot hold
-# every rank's page-locked host tier
-POOL_MULT = 4
 BLOCK_BYTES = B * 59 * 4
 
 
@@ -86,25 +82,25 @@ def host_memory_limit() -> int:
     return limit if limit is not None else 0
 
 
-def plan_host_pool(world: int, host_tier: str, pool_blocks: int, limit: int):
-    """(pool multiple, host tier) that fit every rank's host tier into 60 %
-    of the box's memory: the cache holds POOL_MULT * SLOTS + TURNOVER
-    page-locked entries plus pool_blocks seeded source blocks per rank; the
-    scene shrinks to 3 or 2 x SLOTS blocks per rank before the cache gives
-    way to the small fixed pool (pool_blocks page-locked blocks)."""
+def plan_host_tier(world: int, host_tier: str, pool_blocks: int, host_blocks: int,
+                   limit: int) -> str:
+    """The e2e leg's host tier: a page-locked cache of every block the rank
+    holds during the e2e steps (plus one write-back batch and the seeded
+    source blocks) while all ranks' caches fit in 60 % of the box's memory,
+    else the small fixed page-locked pool (block id mod pool_blocks)."""
     budget = 0.6 * limit / world
-    if host_tier == "cache":
-        for mult in (4, 3, 2):
-            if (mult * SLOTS + TURNOVER + pool_blocks) * BLOCK_BYTES <= budget:
-                return mult, "cache"
-        return 4, "pool"
-    return 4, host_tier
+    if host_tier == "cache" and (host_blocks + TURNOVER + pool_blocks) * BLOCK_BYTES > budget:
+        return "pool"
+    return host_tier
 
 
 WORKLOAD_CONFIG = {
-    "workload": "configs[3]: full resident-set step, 2048 slots x 16384 Gaussians per GPU, "
-                "16-camera contiguous block runs (~30% visible), 25% slot turnover, "
-                "Bernoulli(0.5) dirty evictions"}
+    "workload": "configs[4] block schedule: 61,036-block scene (1.0 B Gaussians), owner = "
+                "block_id mod N, 2048 resident slots x 16384 Gaussians per GPU, one 16-camera "
+                "batch per step split across the ranks on a smooth trajectory (neighbouring "
+                "cameras share 70% of their blocks; the batch sees ~30% of every owner's "
+                "slots), 25% slot turnover per step, dirty blocks written back; at N=1 this "
+                "is configs[3]'s full resident-set step"}
 
 WIDTHS = {"xyz": 3, "opacity": 1, "scaling": 3, "rotation": 4, "features_dc": 3,
           "features_rest": 45}
@@ -216,57 +212,144 @@ def measured_peak():
 
 
 # ---------------------------------------------------------------------------
-# Workload generation (seeded; shapes/distributions of BASELINE configs[3])
+# Workload generation: BASELINE configs[4]'s block schedule (seeded)
 # ---------------------------------------------------------------------------
-class Schedule:
-    """Block ids, camera visibility and slot turnover for one rank."""
+SCENE_BLOCKS = 61036   # 1,000,013,824 Gaussians in 16,384-row blocks
+CAMERAS = 16           # camera batch per step, split across the ranks
+VISIBLE_FRAC = 0.30    # the batch sees ~30 % of every owner's resident slots
+OVERLAP = 0.70         # neighbouring cameras share 70 % of their blocks
 
-    def __init__(self, rank: int, world: int, seed: int = 4, n_cameras_sets: int = 4):
-        self.rng = np.random.default_rng(seed + 1000 * rank)
+
+class Trajectory:
+    """The camera schedule all ranks share. Blocks are numbered along the
+    scene's space-filling order, so a camera sees a contiguous run of block
+    ids. Each step one batch of CAMERAS cameras sits on a smooth path: camera
+    i's run starts (1 - OVERLAP) of a run after camera i-1's, so neighbours
+    share OVERLAP of their blocks, and the batch's union covers VISIBLE_FRAC
+    of the resident window. The resident window (SLOTS * world consecutive
+    block ids, SLOTS of them owned by each rank under owner = id mod world)
+    follows the batch by TURNOVER * world ids a step, bouncing at the ends of
+    the scene, so every owner turns over exactly TURNOVER slots a step.
+    Rank r renders cameras [CAMERAS*r/world, CAMERAS*(r+1)/world)."""
+
+    def __init__(self, world: int, seed: int = 4):
+        if CAMERAS % world:
+            raise ValueError(f"{CAMERAS} cameras do not split across {world} ranks")
         self.world = world
-        self.rank = rank
-        # owned block ids: rank + k*world; POOL_MULT * SLOTS per rank
-        self.pool_ids = np.arange(rank, rank + world * POOL_MULT * SLOTS, world, dtype=np.int64)
-        self.slot_block = self.rng.choice(self.pool_ids, SLOTS, replace=False)
-        self.n_sets = n_cameras_sets
+        self.span = SLOTS * world
+        self.shift = TURNOVER * world
+        if self.span > SCENE_BLOCKS:
+            raise ValueError("resident window larger than the scene")
+        self.union = max(CAMERAS, int(round(VISIBLE_FRAC * self.span)))
+        # union = cam + (CAMERAS - 1) * (1 - OVERLAP) * cam
+        self.cam = max(1, int(round(self.union / (1 + (CAMERAS - 1) * (1 - OVERLAP)))))
+        self.stride = max(1, int(round((1 - OVERLAP) * self.cam)))
+        self.extent = self.cam + (CAMERAS - 1) * self.stride
+        self.n_pos = (SCENE_BLOCKS - self.span) // self.shift  # window positions 0..n_pos
+        self.seed = seed
 
-    _vis_cache: dict = {}
+    def start(self, k: int) -> int:
+        """First block id of the resident window at step k (back and forth)."""
+        if self.n_pos == 0:
+            return 0
+        j = k % (2 * self.n_pos)
+        return self.shift * (j if j <= self.n_pos else 2 * self.n_pos - j)
 
-    def visible_positions(self, step: int) -> np.ndarray:
-        """Union over 16 cameras of contiguous runs of slots, ~30 % visible
-        (the same runs for every owner; cached per camera set)."""
-        key = (SLOTS, step % self.n_sets)
-        hit = Schedule._vis_cache.get(key)
-        if hit is not None:
-            return hit
-        rng = np.random.default_rng(10_000 + step % self.n_sets)
-        vis = np.zeros(SLOTS, bool)
-        scale = SLOTS / 2048.0
-        for _ in range(16):
-            length = max(1, int(rng.integers(24, 56) * scale))
-            start = int(rng.integers(0, max(1, SLOTS - length)))
-            vis[start:start + length] = True
-        out = np.nonzero(vis)[0]
-        out.setflags(write=False)
-        Schedule._vis_cache[key] = out
-        return out
+    def cameras(self, k: int):
+        """[lo, hi) block-id runs of the batch's cameras at step k."""
+        slack = self.span - self.extent
+        # the batch drifts smoothly inside the window around its centre
+        off = slack // 2 + int(round(0.25 * slack * math.sin(0.37 * k + self.seed)))
+        lo0 = self.start(k) + max(0, min(slack, off))
+        return [(lo0 + i * self.stride, lo0 + i * self.stride + self.cam) for i in range(CAMERAS)]
 
-    def turnover(self, step: int):
-        rng = np.random.default_rng(20_000 + step)
-        evict_pos = np.sort(rng.choice(SLOTS, TURNOVER, replace=False))
-        # pool blocks not resident, ascending (pool_ids is ascending)
-        resident = np.zeros(self.pool_ids.size, bool)
-        resident[(self.slot_block - self.rank) // self.world] = True
-        candidates = self.pool_ids[~resident]
-        incoming = np.sort(rng.choice(candidates, TURNOVER, replace=False))
-        dirty = rng.random(TURNOVER) < 0.5
-        return evict_pos, incoming, dirty
+    def rendered(self, k: int, rank: int) -> np.ndarray:
+        """Block ids rank `rank`'s cameras see at step k (ascending)."""
+        per = CAMERAS // self.world
+        runs = self.cameras(k)[rank * per:(rank + 1) * per]
+        return np.arange(runs[0][0], runs[-1][1], dtype=np.int64)
+
+    def visible(self, k: int) -> np.ndarray:
+        runs = self.cameras(k)
+        return np.arange(runs[0][0], runs[-1][1], dtype=np.int64)
+
+    def max_owned_visible(self) -> int:
+        """Upper bound of one owner's visible blocks in any step."""
+        return -(-self.extent // self.world) + 1
+
+
+class Schedule:
+    """One owner's resident slots along the trajectory: slot position i
+    holds block slot_block[i]; incoming blocks (ascending) take the freed
+    positions (ascending), the persistent-slot plan's rule."""
+
+    def __init__(self, rank: int, world: int, traj: "Trajectory" = None):
+        self.traj = traj if traj is not None else Trajectory(world)
+        self.world, self.rank = world, rank
+        a = self.traj.start(0)
+        self.slot_block = self.owned(a, a + self.traj.span)
+        assert self.slot_block.size == SLOTS
+        self.num_blocks = SCENE_BLOCKS
+
+    def owned(self, lo: int, hi: int) -> np.ndarray:
+        first = lo + (self.rank - lo) % self.world
+        return np.arange(first, hi, self.world, dtype=np.int64)
 
     def slot_table(self) -> np.ndarray:
         """Dense block id -> slot position table (-1: not resident)."""
-        table = np.full(int(self.pool_ids[-1]) + 1, -1, np.int64)
-        table[self.slot_block] = np.arange(SLOTS, dtype=np.int64)
+        table = np.full(SCENE_BLOCKS, -1, np.int64)
+        table[self.slot_block] = np.arange(self.slot_block.size, dtype=np.int64)
         return table
+
+    def visible_blocks(self, k: int) -> np.ndarray:
+        """This owner's blocks the batch of step k sees (ascending id)."""
+        v = self.traj.visible(k)
+        return v[v % self.world == self.rank]
+
+    def visible_positions(self, k: int) -> np.ndarray:
+        """Slot positions of this owner's visible blocks at step k, ascending
+        (the owner's row ids are all rows of these positions)."""
+        pos = self.slot_table()[self.visible_blocks(k)]
+        if pos.size and pos.min() < 0:
+            raise RuntimeError("a visible block is not resident")
+        return np.sort(pos)
+
+    def turnover(self, k: int):
+        """(evicted positions ascending, incoming block ids ascending, None)
+        between steps k and k+1; the blocks' dirty state decides the
+        write-back."""
+        a0, a1 = self.traj.start(k), self.traj.start(k + 1)
+        span = self.traj.span
+        if a1 >= a0:
+            leaving, entering = self.owned(a0, a1), self.owned(a0 + span, a1 + span)
+        else:
+            leaving, entering = self.owned(a1 + span, a0 + span), self.owned(a1, a0)
+        evict_pos = np.sort(self.slot_table()[leaving])
+        return evict_pos, entering, None
+
+    def touched_blocks(self, n_steps: int) -> np.ndarray:
+        """Every block this owner holds during steps [0, n_steps]."""
+        starts = [self.traj.start(k) for k in range(n_steps + 1)]
+        return self.owned(min(starts), max(starts) + self.traj.span)
+
+
+class RandomTurnover:
+    """configs[2]'s materialization schedule over one owner's slot map: each
+    iteration TURNOVER random slots take random non-resident blocks of a
+    host pool (random block-id -> slot remap), Bernoulli(0.5) dirty flags on
+    the evicted blocks."""
+
+    def __init__(self, slot_block: np.ndarray, pool_ids: np.ndarray, seed: int = 3):
+        self.slot_block = slot_block
+        self.pool_ids = np.sort(np.asarray(pool_ids, np.int64))
+        self.seed = seed
+
+    def turnover(self, k: int):
+        rng = np.random.default_rng(self.seed * 100_003 + k)
+        evict_pos = np.sort(rng.choice(self.slot_block.size, TURNOVER, replace=False))
+        resident = np.isin(self.pool_ids, self.slot_block, assume_unique=True)
+        incoming = np.sort(rng.choice(self.pool_ids[~resident], TURNOVER, replace=False))
+        return evict_pos, incoming, rng.random(TURNOVER) < 0.5
 
 
 def fill_params(comps, gen):
@@ -284,58 +367,43 @@ def fill_params(comps, gen):
 # ---------------------------------------------------------------------------
 # Device leg: library entry points, inputs resident in HBM
 # ---------------------------------------------------------------------------
-def rank_visible_positions(sched: "Schedule", step: int, world: int, rank: int) -> np.ndarray:
-    """Slot positions of `sched`'s owner whose blocks rank `rank` renders at
-    `step`: the owner's visible runs (~30 % of its slots, as on one GPU) split
-    into `world` contiguous parts, each widened by 15 % of a part on both
-    sides so that neighbouring ranks' cameras overlap."""
-    pos = sched.visible_positions(step)
-    if world == 1:
-        return pos
-    part = -(-pos.size // world)
-    margin = int(0.15 * part)
-    lo = max(0, rank * part - margin)
-    hi = min(pos.size, (rank + 1) * part + margin)
-    return pos[lo:hi]
+def rendered_blocks(traj: "Trajectory", step: int, world: int):
+    """Block ids whose gradients each rank renders at `step`."""
+    return [traj.rendered(step, r) for r in range(world)]
 
 
-def rendered_blocks(scheds, step: int, world: int):
-    """Block ids whose gradients each rank renders at `step` (every owner's
-    share for that rank)."""
-    return [np.concatenate([o.slot_block[rank_visible_positions(o, step, world, r)]
-                            for o in scheds]) for r in range(world)]
-
-
-def exchange_capacity(sched: "Schedule", scheds, world: int):
-    """(blocks a rank renders, tiles an owner receives): the largest over the
-    periodic camera sets."""
+def exchange_capacity(sched: "Schedule", world: int, n_steps: int):
+    """(blocks a rank renders, tiles an owner receives): the largest over
+    the steps of the trace."""
     send_max = recv_max = 0
-    for s_ in range(sched.n_sets):
-        mine = sum(rank_visible_positions(o, s_, world, sched.rank).size for o in scheds)
-        theirs = sum(rank_visible_positions(sched, s_, world, r).size for r in range(world))
-        send_max, recv_max = max(send_max, mine), max(recv_max, theirs)
+    for k in range(n_steps):
+        ren = rendered_blocks(sched.traj, k, world)
+        send_max = max(send_max, ren[sched.rank].size)
+        recv_max = max(recv_max, sum(int(np.count_nonzero(r % world == sched.rank))
+                                     for r in ren))
     return send_max, recv_max
 
 
 class ScheduleTrace:
-    """Every owner's synthetic schedule simulated ahead of the timed region
-    (workload generation, not the measured path): for step k, the blocks
-    each rank renders (vis[k], world > 1) and this rank's slot turnover
-    (turn[k] = evicted slot positions, incoming block ids, dirty pattern)."""
+    """The synthetic schedule simulated ahead of the timed region (workload
+    generation, not the measured path): for step k, the blocks each rank
+    renders (vis[k], world > 1) and this rank's slot turnover (turn[k] =
+    evicted slot positions, incoming block ids, dirty pattern or None)."""
 
     def __init__(self, world: int, rank: int, n_steps: int):
-        scheds = [Schedule(o, world) for o in range(world)]
+        traj = Trajectory(world)
+        sched = Schedule(rank, world, traj)
+        self.n_steps = n_steps
         self.vis, self.turn = [], []
         for k in range(n_steps):
-            self.vis.append(rendered_blocks(scheds, k, world) if world > 1 else None)
-            turns = [o.turnover(k) for o in scheds]
-            self.turn.append(turns[rank])
-            for o, (ev, inc, _) in zip(scheds, turns):
-                o.slot_block[ev] = inc
+            self.vis.append(rendered_blocks(traj, k, world) if world > 1 else None)
+            ev, inc, dirty = sched.turnover(k)
+            self.turn.append((ev, inc, dirty))
+            sched.slot_block[ev] = inc
 
 
 class DeviceStep:
-    def __init__(self, device, sched: Schedule, trace: ScheduleTrace, scheds=None, world: int = 1,
+    def __init__(self, device, sched: Schedule, trace: ScheduleTrace, world: int = 1,
                  exchange: str = "pull"):
         from tidegs_b200 import _lib, _ops
 
@@ -344,7 +412,6 @@ class DeviceStep:
         self.sched = sched
         self.trace = trace
         self.world = world
-        self.scheds = scheds if scheds is not None else [sched]
         gen = torch.Generator(device=device).manual_seed(1234 + sched.rank)
         rows = SLOTS * B
         self.arena = {n: torch.empty((rows, w), device=device) for n, w in WIDTHS.items()}
@@ -370,20 +437,19 @@ class DeviceStep:
         self.table = torch.tensor(table, dtype=torch.float32, device=device)
         self.err = torch.zeros(4, dtype=torch.int32, device=device)
         self.pos_count = torch.zeros(SLOTS, dtype=torch.int32, device=device)
+        self.chunk_table = torch.empty(2 * sched.traj.max_owned_visible() * B // 32,
+                                       dtype=torch.int64, device=device)
         starts = np.arange(SLOTS, dtype=np.int64) * B
         self.pos_start = _ops.i64_to_device(starts, device)
         self.pos_end = _ops.i64_to_device(starts + B, device)
         self.pos_slot = torch.arange(SLOTS, dtype=torch.int32, device=device)
-        self.bitmap = torch.zeros(_ops.bitmap_words(int(sched.pool_ids.max()) + 1),
-                                  dtype=torch.int32, device=device)
-        # visible rows per camera set (all rows of visible blocks), grads
-        self.vis_sets = []
-        max_rows = 0
-        for s in range(sched.n_sets):
-            pos = sched.visible_positions(s)
-            ids = (pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)
-            self.vis_sets.append((pos, _ops.i64_to_device(ids, device)))
-            max_rows = max(max_rows, ids.size)
+        self.bitmap = torch.zeros(_ops.bitmap_words(SCENE_BLOCKS), dtype=torch.int32,
+                                  device=device)
+        # the owner's row ids of a step (all rows of its visible positions)
+        # are expanded on the device from the positions; gradients of the
+        # largest step
+        max_rows = sched.traj.max_owned_visible() * B
+        self.ids_buf = torch.empty(max_rows, dtype=torch.int64, device=device)
         self.grads = {n: torch.empty((max_rows, w), device=device).normal_(0, 1e-3, generator=gen)
                       for n, w in WIDTHS.items()}
         self.exchange_mode = exchange if world > 1 else None
@@ -393,7 +459,7 @@ class DeviceStep:
         if world > 1:
             # gradients this rank renders for blocks of every owner, and the
             # exchange buffers (sizes: the largest of the periodic camera sets)
-            send_max, recv_max = exchange_capacity(sched, self.scheds, world)
+            send_max, recv_max = exchange_capacity(sched, world, trace.n_steps)
             self.rank_grads = {n: torch.empty((send_max * B, w), device=device).normal_(
                 0, 1e-3, generator=gen) for n, w in WIDTHS.items()}
             if exchange == "pull":
@@ -446,19 +512,27 @@ class DeviceStep:
             self.exchange.reduce(plan, recv, out=self.grads, err=self.err)
             self.exchange_rows += int(send.shape[0])
         pos = slot_of[plan.out_blocks]
-        # the owner's visible slots are its camera set's positions: reuse the
-        # device row ids prepared for that set
-        set_pos, set_ids = self.vis_sets[k % self.sched.n_sets]
-        if not np.array_equal(pos, set_pos):
+        # the plan's output blocks are the owner's visible blocks in slot order
+        if not np.array_equal(pos, self.sched.visible_positions(k)):
             raise RuntimeError("exchange plan and owner visibility disagree")
-        return pos, set_ids
+        return pos, self.row_ids(pos)
+
+    def row_ids(self, pos: np.ndarray) -> torch.Tensor:
+        """All rows of slot positions `pos` (ascending), expanded on the
+        device from the positions."""
+        n = int(pos.size) * B
+        if n > self.ids_buf.numel():
+            raise RuntimeError(f"{pos.size} visible positions exceed the row-id buffer")
+        ids = self.ids_buf[:n]
+        self._ops.fill_global_ids(ids, 0, self._ops.i64_to_device(pos, self.device), n, B)
+        return ids
 
     def _make_plan(self, k: int, slot_block: np.ndarray):
         """Exchange plan of step k for the slot map `slot_block` (and, for the
         pull exchange, its device tables)."""
         from tidegs_b200.sharded import make_plan
 
-        table = np.full(int(self.sched.pool_ids[-1]) + 1, -1, np.int64)
+        table = np.full(SCENE_BLOCKS, -1, np.int64)
         table[slot_block] = np.arange(slot_block.size, dtype=np.int64)
         plan = make_plan(self.trace.vis[k], self.world, self.sched.rank, B, out_order=table)
         tables = self.pull.tables(plan) if self.pull is not None else None
@@ -488,7 +562,8 @@ class DeviceStep:
             slot_step=self.slot_step.data_ptr(), slot_stamp=self.slot_stamp.data_ptr(),
             slot_bias=self.slot_bias.data_ptr(), step_table=self.table.data_ptr(),
             step_table_len=self.table.shape[0], n_slots=SLOTS,
-            pos_count=self.pos_count.data_ptr(), err=self.err.data_ptr())
+            pos_count=self.pos_count.data_ptr(), err=self.err.data_ptr(),
+            chunk_table=self.chunk_table.data_ptr())
         tables = self.pull_tables
         _lib.call("tgs_resident_adam_count", c, stream)
         self._phase("count")
@@ -506,6 +581,7 @@ class DeviceStep:
         a.local_ids, a.n_rows = ids.data_ptr(), n
         a.state, a.slot_stamp = self.state.data_ptr(), self.slot_stamp.data_ptr()
         a.slot_bias, a.err = self.slot_bias.data_ptr(), self.err.data_ptr()
+        a.chunk_table = self.chunk_table.data_ptr()
         if self.pull is not None:
             self.pull.barrier()  # every rank's gradients of this step are written
             self._phase("acquire")
@@ -554,7 +630,8 @@ class DeviceStep:
             pos, ids = self.exchange_grads(k)
             self._phase("exchange")
         else:
-            pos, ids = self.vis_sets[k % sched.n_sets]
+            pos = sched.visible_positions(k)
+            ids = self.row_ids(pos)
         # 1. optimizer over the visible rows
         self.adam(ids, timed)
         self.plan_ahead(k)
@@ -564,13 +641,13 @@ class DeviceStep:
         _ops.block_bounds(self.arena["xyz"], (pos * B).tolist(), [B] * pos.size,
                           self.bounds[: pos.size])
         self._phase("dirty_bounds")
-        # 3. evict 512 slots: write back the dirty ones
+        # 3. evict TURNOVER slots: write back the dirty ones
         evict_pos, incoming, dirty = self.trace.turn[k]
-        # half of the evicted blocks were never touched before: mark a random
-        # dirty pattern so that the compaction has work of the configured mix
         evicted_blocks = sched.slot_block[evict_pos]
-        _ops.dirty_mark(self.bitmap, evicted_blocks[dirty].tolist(), True)
-        _ops.dirty_mark(self.bitmap, evicted_blocks[~dirty].tolist(), False)
+        if dirty is not None:
+            # a schedule with a prescribed dirty pattern
+            _ops.dirty_mark(self.bitmap, evicted_blocks[dirty].tolist(), True)
+            _ops.dirty_mark(self.bitmap, evicted_blocks[~dirty].tolist(), False)
         order = np.argsort(evicted_blocks, kind="stable")
         selection = _ops.dirty_select_async(self.bitmap, evicted_blocks[order].tolist())
         self._phase("dirty_select")
@@ -609,6 +686,107 @@ class DeviceStep:
             if obj is not None:
                 obj.close()
                 setattr(self, attr, None)
+
+    def parity_check(self, k: int, blocks_per_owner: int = 2, rows: int = 256) -> dict:
+        """Checker, run after the timed region (not part of any measured
+        number): step k runs as usual while sampled rows of `blocks_per_owner`
+        of each owner's updated blocks are replayed on the CPU through the
+        kernel-order Adam restatement (oracle/resident_adam.py, pinned to the
+        reference's update, gpu_resident_optimizer.py:339-364) on the
+        rank-order sum of every rank's gradient contribution to the block.
+        Parameters, both moments and the row stamps must match bit for bit.
+        A row's update depends only on its own values and its slot's step, so
+        a window of `rows` rows of a block stands for the block. Every rank
+        takes the same collective steps (two object all-gathers and a final
+        one for the counts)."""
+        from oracle.resident_adam import bias_pair, kernel_update
+
+        W, me, sched = self.world, self.sched.rank, self.sched
+        pos_all = sched.visible_positions(k)
+        evict_pos = self.trace.turn[k][0]
+        rng = np.random.default_rng(777 + 31 * k + me)
+        # positions whose parameters survive the step (evicted slots are
+        # overwritten by the incoming blocks at its end)
+        cand = np.setdiff1d(pos_all, evict_pos)
+        pick = np.sort(rng.choice(cand, min(blocks_per_owner, cand.size), replace=False))
+        mine = [(int(sched.slot_block[p]), int(p), int(rng.integers(0, B - rows + 1)))
+                for p in pick]
+
+        def gather(obj):
+            if W == 1:
+                return [obj]
+            import torch.distributed as dist
+
+            out = [None] * W
+            dist.all_gather_object(out, obj)
+            return out
+
+        samples = gather(mine)  # [owner] -> [(block, position, first row)]
+        # this rank's gradient rows for every sampled block it rendered
+        contrib = {}
+        if W == 1:
+            for b, p, r0 in mine:
+                i = int(np.searchsorted(pos_all, p))
+                contrib[(0, b)] = np.concatenate(
+                    [self.grads[n][i * B + r0: i * B + r0 + rows].cpu().numpy()
+                     for n in NAMES], axis=1)
+        else:
+            rendered = np.unique(self.trace.vis[k][me])
+            for o, lst in enumerate(samples):
+                for b, _, r0 in lst:
+                    j = int(np.searchsorted(rendered, b))
+                    if j < rendered.size and rendered[j] == b:
+                        contrib[(o, b)] = np.concatenate(
+                            [self.rank_grads[n][j * B + r0: j * B + r0 + rows].cpu().numpy()
+                             for n in NAMES], axis=1)
+        by_rank = gather(contrib)
+        # snapshot of the owner's rows before the step
+        before = []
+        for b, p, r0 in mine:
+            lo = p * B + r0
+            before.append(dict(
+                params={n: self.arena[n][lo:lo + rows].cpu().numpy() for n in NAMES},
+                state=self.state[lo:lo + rows].cpu().numpy(),
+                step=int(self.slot_step[p].item()), stamp=int(self.stamp_host[p])))
+        self.step(k)
+        torch.cuda.synchronize()
+        checked = mismatched = 0
+        for (b, p, r0), snap in zip(mine, before):
+            parts = [d[(me, b)] for d in by_rank if (me, b) in d]  # rank order
+            g = parts[0].copy()
+            for x in parts[1:]:
+                g = (g + x).astype(np.float32)
+            st = snap["state"]
+            fresh = st[:, 124].view(np.uint32) == np.uint32(snap["stamp"])
+            m0 = np.where(fresh[:, None], st[:, 0:118:2], np.float32(0))
+            v0 = np.where(fresh[:, None], st[:, 1:118:2], np.float32(0))
+            bias1, dscale = bias_pair(0.9, 0.999, snap["step"] + 1)
+            lo = p * B + r0
+            after_state = self.state[lo:lo + rows].cpu().numpy()
+            ok = bool(np.all(after_state[:, 124].view(np.uint32) == np.uint32(snap["stamp"])))
+            col = 0
+            for n in NAMES:
+                w = WIDTHS[n]
+                pn, mn, vn = kernel_update(snap["params"][n], g[:, col:col + w],
+                                           m0[:, col:col + w], v0[:, col:col + w], LRS[n],
+                                           bias1, dscale, 0.9, 0.999, 1e-15, 16)
+                got_p = self.arena[n][lo:lo + rows].cpu().numpy()
+                ok &= np.array_equal(got_p.view(np.uint32), pn.view(np.uint32))
+                ok &= np.array_equal(after_state[:, 2 * col:2 * (col + w):2].view(np.uint32),
+                                     mn.view(np.uint32))
+                ok &= np.array_equal(after_state[:, 2 * col + 1:2 * (col + w):2].view(np.uint32),
+                                     vn.view(np.uint32))
+                col += w
+            checked += 1
+            mismatched += 0 if ok else 1
+        counts = gather((checked, mismatched, sum(len(v) for v in by_rank)))
+        return {"checked_blocks": sum(c for c, _, _ in counts),
+                "rows_per_block": rows, "step": k,
+                "mismatched_blocks": sum(m for _, m, _ in counts),
+                "bit_exact": all(m == 0 for _, m, _ in counts),
+                "contributions": sum(c for _, _, c in counts) // max(1, W),
+                "oracle": "oracle/resident_adam.py kernel_update on the rank-order sum of "
+                          "the contributions (CPU, after the timed region)"}
 
     def adam_stats(self):
         ms = [e0.elapsed_time(e1) for e0, e1, _ in self.adam_ms]
@@ -660,8 +838,9 @@ class ApiStep:
             return now
         return t
 
-    def __init__(self, device, scheds, trace: ScheduleTrace, rank: int, world: int,
-                 pool_blocks: int, exchange: str = "pull", host_tier: str = "cache"):
+    def __init__(self, device, sched: "Schedule", trace: ScheduleTrace, rank: int, world: int,
+                 pool_blocks: int, host_blocks: np.ndarray, exchange: str = "pull",
+                 host_tier: str = "cache"):
         import types
 
         from tidegs_b200 import (BlockLayout, CachedBlockReader, DoubleBufferGPUWorkingSet,
@@ -669,26 +848,26 @@ class ApiStep:
                                  PinnedBlockPool, _ops)
 
         self.device = device
-        self.scheds = scheds
         self.trace = trace
-        self.sched = sched = scheds[rank]
+        self.sched = sched
         self.rank, self.world = rank, world
-        num_total = int(max(int(o.pool_ids.max()) for o in scheds) + 1) * B
+        num_total = SCENE_BLOCKS * B
         gen = torch.Generator().manual_seed(99 + rank)
         self.cache = None
+        self.host_blocks = np.asarray(host_blocks, np.int64)
         if host_tier == "cache":
-            # the host tier holds every scene block of this rank (POOL_MULT x
-            # SLOTS blocks, BASELINE configs[3]'s pinned pool): pool_blocks distinct
-            # seeded blocks, block b holding distinct[b % pool_blocks], read
-            # into the cache's page-locked slab through its prefetch; room
-            # for one write-back batch of fresh entries on top
+            # the host tier holds every block this rank touches in the timed
+            # steps (host_blocks): pool_blocks distinct seeded blocks, scene
+            # block b holding distinct[b % pool_blocks], read into the cache's
+            # page-locked slab through its prefetch; room for one write-back
+            # batch of fresh entries on top
             distinct = torch.empty((pool_blocks, B, 59))
             for i in range(pool_blocks):
                 distinct[i].normal_(0.0, 1.0, generator=gen)
             store = _SceneStore(distinct)
             self.cache = PinnedBlockCache(store, max_ram_gb=1e9, block_size=B, verbose=False,
-                                          capacity_blocks=sched.pool_ids.size + TURNOVER)
-            self.cache.prefetch(sched.pool_ids.tolist())
+                                          capacity_blocks=self.host_blocks.size + TURNOVER)
+            self.cache.prefetch(self.host_blocks.tolist())
             store.sealed = True  # a host-tier miss inside the steps is an error
             self.pool = CachedBlockReader(self.cache, num_total, B)
         else:
@@ -716,19 +895,17 @@ class ApiStep:
                 param_groups=[{"betas": (0.9, 0.999), "eps": 1e-15}]))
         self._activate()
         self.opt.set_resident_blocks(order)
-        # visible rows of each camera set, page-locked (world == 1)
-        self.ids_pinned = []
-        for s_ in range(sched.n_sets):
-            pos = sched.visible_positions(s_)
-            self.ids_pinned.append(
-                torch.from_numpy((pos[:, None] * B + np.arange(B)[None, :]).reshape(-1)).pin_memory())
-        max_rows = max(t.numel() for t in self.ids_pinned)
+        # the step's row ids: all rows of the visible positions, uploaded as
+        # positions from page-locked memory and expanded on the device
+        max_rows = sched.traj.max_owned_visible() * B
+        self.pos_pinned = torch.empty(2 * (max_rows // B), dtype=torch.int64).pin_memory()
+        self.ids_buf = torch.empty(max_rows, dtype=torch.int64, device=device)
         self.grads = {n: torch.empty((max_rows, w), device=device).normal_(0, 1e-3)
                       for n, w in WIDTHS.items()}
         self.peer = None
         self.pull = None
         if world > 1:
-            send_max, recv_max = exchange_capacity(sched, scheds, world)
+            send_max, recv_max = exchange_capacity(sched, world, trace.n_steps)
             self.rank_grads = {n: torch.empty((send_max * B, w), device=device).normal_(0, 1e-3)
                                for n, w in WIDTHS.items()}
             if exchange == "pull":
@@ -774,11 +951,10 @@ class ApiStep:
     def _grads_and_ids(self, k: int):
         """(sparse_grad_local_ids, sparse_grad_components or (pull, plan)) of
         this owner."""
+        pos = self.sched.visible_positions(k)
         if self.world == 1:
-            ids_host = self.ids_pinned[k % self.sched.n_sets]
-            n = ids_host.numel()
-            self.h2d_bytes += n * 8
-            return self._upload_ids(ids_host), {name: g[:n] for name, g in self.grads.items()}
+            ids = self._row_ids(pos, k)
+            return ids, {name: g[:ids.numel()] for name, g in self.grads.items()}
         from tidegs_b200.sharded import make_plan
 
         W, me = self.world, self.rank
@@ -797,15 +973,30 @@ class ApiStep:
             send = self.exchange.pack(plan, self.rank_grads, starts, out=self.send_buf)
             recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
             grads = self.exchange.reduce(plan, recv, out=self.grads)
-        rows = slot_of[plan.out_blocks] * B
-        ids_host = self.ids_pinned[k % self.sched.n_sets]
         slices = self.db.active_buffer.block_to_local_slice
         probe = plan.out_blocks[:: max(1, plan.n_out // 16)]
-        if (not np.array_equal(rows, ids_host[::B].numpy())
+        if (not np.array_equal(slot_of[plan.out_blocks], pos)
                 or any(slices[int(b)].start != slot_of[int(b)] * B for b in probe)):
             raise RuntimeError("exchange plan and owner slices disagree")
-        self.h2d_bytes += ids_host.numel() * 8
-        return self._upload_ids(ids_host), grads
+        return self._row_ids(pos, k), grads
+
+    def _row_ids(self, pos: np.ndarray, k: int) -> torch.Tensor:
+        """All rows of the visible slot positions: the positions go up from
+        page-locked memory (counted as H2D bytes), the rows are expanded on
+        the device. Two host buffers alternate by step."""
+        from tidegs_b200 import _ops
+
+        half = self.pos_pinned.numel() // 2
+        if pos.size > half:
+            raise RuntimeError(f"{pos.size} visible positions exceed the position buffer")
+        host = self.pos_pinned[(k % 2) * half:(k % 2) * half + pos.size]
+        host.numpy()[:] = pos
+        self.h2d_bytes += pos.size * 8
+        dev_pos = self._upload_ids(host)
+        n = int(pos.size) * B
+        ids = self.ids_buf[:n]
+        _ops.fill_global_ids(ids, 0, dev_pos, n, B)
+        return ids
 
     def close(self):
         """Releases the peer mappings (collective over the ranks) and stops
@@ -828,18 +1019,22 @@ class ApiStep:
                   torch.cuda.current_stream(self.device).cuda_stream)
         return out
 
-    def step(self, k: int) -> int:
+    def step(self, k: int, turn=None, optimize: bool = True) -> int:
         """One iteration in the engine's order: the resident plan for k+1 is
         known up front and its N+1 prefetch (H2D of the incoming blocks) runs
         on the worker thread / prefetch stream while the optimizer step and
-        the write-back of iteration k run."""
+        the write-back of iteration k run. `turn` overrides the trace's
+        turnover (evicted positions, incoming blocks, dirty pattern or None);
+        optimize=False leaves out the optimizer and the bounds
+        (materialization only, configs[2]), marking the evicted blocks dirty
+        by the pattern instead."""
         db, ws, sched = self.db, self.ws, self.sched
         t = time.perf_counter()
         if self.profile is not None:
             step_ev = torch.cuda.Event(enable_timing=True)
             step_ev.record()
             db.prefetch_events = {}
-        evict_pos, incoming_arr, _ = self.trace.turn[k]
+        evict_pos, incoming_arr, dirty = turn if turn is not None else self.trace.turn[k]
         evicted_arr = np.sort(sched.slot_block[evict_pos])
         evicted = evicted_arr.tolist()
         incoming = incoming_arr.tolist()
@@ -853,19 +1048,28 @@ class ApiStep:
             # the views of the slots swapped in at the end of the previous
             # step (after the N+1 DMA is queued: it needs only the slot map)
             self._activate()
-            self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
+            if optimize:
+                self.opt.set_resident_blocks(db.active_buffer.loaded_blocks)
             self._pending_activate = False
             t = self._mark("activate", t)
-        ids, grads = self._grads_and_ids(k)
-        t = self._mark("exchange", t)
-        if isinstance(grads, tuple):
-            stats = self.opt.step_pulled(k, self.gaussians, ids, *grads)
-        else:
-            stats = self.opt.step(k, self.gaussians, ids, grads)
-        t = self._mark("adam_step", t)
-        updated = stats["updated_block_ids"]
-        db.mark_dirty_blocks(updated)
-        bounds = ws.stage_block_bounds(updated)
+        rows = 0
+        bounds = None
+        if optimize:
+            ids, grads = self._grads_and_ids(k)
+            rows = int(ids.numel())
+            t = self._mark("exchange", t)
+            if isinstance(grads, tuple):
+                stats = self.opt.step_pulled(k, self.gaussians, ids, *grads)
+            else:
+                stats = self.opt.step(k, self.gaussians, ids, grads)
+            t = self._mark("adam_step", t)
+            updated = stats["updated_block_ids"]
+            db.mark_dirty_blocks(updated)
+            bounds = ws.stage_block_bounds(updated)
+        if dirty is not None:
+            evicted_now = sched.slot_block[evict_pos]
+            db.mark_dirty_blocks(evicted_now[dirty].tolist())
+            db.mark_blocks_written_back(evicted_now[~dirty].tolist())
         t = self._mark("dirty_mark_bounds", t)
         wb_ids = db.dirty_blocks_for_eviction(evicted)
         t = self._mark("dirty_select", t)
@@ -900,414 +1104,327 @@ class ApiStep:
         t = self._mark("swap", t)
         sched.slot_block[evict_pos] = incoming_arr
         self._pending_activate = True
-        self.h2d_bytes += TURNOVER * B * 59 * 4
-        return int(ids.numel())
+        self.h2d_bytes += len(incoming) * B * 59 * 4
+        return rows
 
 
 # ---------------------------------------------------------------------------
-# Diagnostic: the pull kernel with a remote sender, in one process
+# The other configs of BASELINE.json, measured at N = 1 beside the step
 # ---------------------------------------------------------------------------
-def pull_probe(args, modes):
-    """Not the bench line. One owner (GPU 0) of a two-rank schedule updates
-    its visible rows with the pull kernel while the other rank's gradients
-    live on GPU 1 ("remote", read over NVLink) or on GPU 0 ("local"), next to
-    the single-GPU kernel ("plain"). One JSON line per mode (CUDA events)."""
-    from tidegs_b200.sharded import PeerGradPull, make_plan
+def _events():
+    return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    W = 2
-    torch.cuda.set_device(0)
-    d0 = torch.device("cuda", 0)
-    scheds = [Schedule(r, W) for r in range(W)]
-    ds = DeviceStep(d0, scheds[0], None, scheds=scheds, world=1)
-    caps = [exchange_capacity(scheds[r], scheds, W)[0] for r in range(W)]
-    plan = make_plan(rendered_blocks(scheds, 0, W), W, 0, B, out_order=scheds[0].slot_table())
-    pos, ids = ds.vis_sets[0]
-    if not np.array_equal(scheds[0].slot_table()[plan.out_blocks], pos):
-        raise RuntimeError("probe plan and owner visibility disagree")
-    for mode in modes:
-        ds.pull = ds.pull_tables = None
-        if mode != "plain":
-            where = [d0, torch.device("cuda", 1) if mode == "remote" else d0]
-            grads = [{n: torch.empty((caps[r] * B, w), device=where[r]).normal_(0, 1e-3)
-                      for n, w in WIDTHS.items()} for r in range(W)]
-            ds.pull = PeerGradPull.in_process(grads, 0, B, d0)
-            ds.plan, ds.pull_tables = plan, ds.pull.tables(plan)
-        ds.adam_ms = []
-        for k in range(args.warmup + args.steps):
-            ds.adam(ids, timed=k >= args.warmup)
+
+def bench_selective_adam(device, steps: int = 10, warmup: int = 3) -> dict:
+    """SelectiveAdam (optimizer.py:46-87 drop-in, one
+    tgs_selective_adam launch for the six groups) over N = 1,048,576
+    Gaussians, Bernoulli(0.3) visibility, grads N(0, 1e-3) on visible rows,
+    10 steps from zero moments. Inputs (990 MB) exceed L2."""
+    from tidegs_b200 import SelectiveAdam
+
+    N = 1 << 20
+    gen = torch.Generator(device=device).manual_seed(0)
+    comps = {n: torch.empty((N, w), device=device) for n, w in WIDTHS.items()}
+    fill_params(comps, gen)
+    vis = torch.rand(N, generator=gen, device=device) < 0.3
+    params = []
+    for n in NAMES:
+        p = torch.nn.Parameter(comps[n])
+        p.grad = torch.randn(p.shape, generator=gen, device=device).mul_(1e-3) * vis[:, None]
+        params.append(p)
+    opt = SelectiveAdam([{"params": [p], "lr": LRS[n]} for p, n in zip(params, NAMES)],
+                        eps=1e-15, betas=(0.9, 0.999))
+    for _ in range(warmup):
+        opt.step(vis)
+    for p in params:
+        opt.state[p]["exp_avg"].zero_()
+        opt.state[p]["exp_avg_sq"].zero_()
+    torch.cuda.synchronize()
+    e0, e1 = _events()
+    e0.record()
+    for _ in range(steps):
+        opt.step(vis)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    rows = int(vis.sum().item())
+    nbytes = rows * 59 * 4 * 7 + N  # g r, p r/w, m r/w, v r/w per visible element; mask
+    peak, kind = measured_peak()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    return {"config": "configs[0]: SelectiveAdam, N=1,048,576 x 59, Bernoulli(0.3) rows, "
+                      f"{steps} steps", "value": rows / (ms / 1e3), "unit": UNIT,
+            "ms_per_step": ms, "visible_rows": rows,
+            "roofline": {"bound": "hbm", "kernel": "dense_kernel<adam>", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": kind,
+                         "algorithmic_bytes": "28 B per visible element + 1 B mask per row"}}
+
+
+def bench_sophia(device, steps: int = 50, k: int = 10, warmup: int = 3) -> dict:
+    """SelectiveSophia over N = 8,388,608 Gaussians, b1 0.965,
+    b2 0.99, rho 0.04, Hessian EMA refreshed every k = 10 steps from a
+    seeded N(0, 1) noise input, Bernoulli(0.3) visibility, 50 steps."""
+    from tidegs_b200 import SelectiveSophia
+
+    N = 8 * (1 << 20)
+    gen = torch.Generator(device=device).manual_seed(1)
+    comps = {n: torch.empty((N, w), device=device) for n, w in WIDTHS.items()}
+    fill_params(comps, gen)
+    vis = torch.rand(N, generator=gen, device=device) < 0.3
+    params = []
+    for n in NAMES:
+        p = torch.nn.Parameter(comps[n])
+        p.grad = torch.randn(p.shape, generator=gen, device=device).mul_(1e-3) * vis[:, None]
+        params.append(p)
+    noise = [torch.randn(p.shape, generator=gen, device=device) for p in params]
+    groups = [{"params": [p], "lr": LRS[n]} for p, n in zip(params, NAMES)]
+    opt = SelectiveSophia(groups, betas=(0.965, 0.99), rho=0.04, eps=1e-15, k=k)
+    for _ in range(warmup):
+        opt.step(vis, noise=noise)
+    for p in params:
+        st = opt.state[p]
+        st["step"] = 0
+        st["exp_avg"].zero_()
+        st["hessian"].zero_()
+    torch.cuda.synchronize()
+    e0, e1 = _events()
+    e0.record()
+    for _ in range(steps):
+        opt.step(vis, noise=noise)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    rows = int(vis.sum().item())
+    hess_steps = sum(1 for t in range(1, steps + 1) if t % k == 1 % k)
+    per_elem = (24 * steps + 8 * hess_steps) / steps
+    nbytes = rows * 59 * per_elem + N
+    peak, kind = measured_peak()
+    achieved = nbytes / (ms / 1e3) / 1e9
+    return {"config": f"configs[1]: SelectiveSophia, N=8,388,608 x 59, Bernoulli(0.3) rows, "
+                      f"{steps} steps, Hessian every {k}", "value": rows / (ms / 1e3),
+            "unit": UNIT, "ms_per_step": ms, "visible_rows": rows, "hessian_steps": hess_steps,
+            "parity": "unpinned (the reference has no Sophia)",
+            "roofline": {"bound": "hbm", "kernel": "dense_kernel<sophia>", "achieved": achieved,
+                         "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": kind,
+                         "algorithmic_bytes": "24 B per visible element, +8 on Hessian steps, "
+                                              "+1 B mask per row"}}
+
+
+def link_probe(api, device, blocks_in: int, blocks_out: int) -> dict:
+    """Host-link ceiling of this box: one DMA per block between page-locked
+    host-cache entries and device memory, H2D alone, D2H alone, then both at
+    once on two streams (the materialization's traffic pattern)."""
+    from tidegs_b200 import _ops
+
+    slab = api.cache.slab if api.cache is not None else None
+    if slab is None:
+        return {"skipped": "no page-locked host cache"}
+    nb = min(blocks_in, slab.shape[0] // 2)
+    no = min(blocks_out, slab.shape[0] - nb)
+    dev = torch.empty((max(nb, no), B, 59), device=device)
+    bpb = B * 59 * 4
+    h_src = [slab[i].data_ptr() for i in range(nb)]
+    h_dst = [dev[i].data_ptr() for i in range(nb)]
+    d_src = [dev[i].data_ptr() for i in range(no)]
+    d_dst = [slab[nb + i].data_ptr() for i in range(no)]
+    side = torch.cuda.Stream(device)
+
+    def run(h2d, d2h):
         torch.cuda.synchronize()
-        ms = sorted(ms for ms, _ in zip(*ds.adam_stats()))
-        print(json.dumps({"probe": mode, "rows": int(ids.numel()), "median_ms": ms[len(ms) // 2],
-                          "contributions": int(plan.contrib_offsets[-1]), "blocks": plan.n_out,
-                          "remote_blocks": int(sum(plan.recv_counts[1:]))}), flush=True)
-    return 0
-
-
-# ---------------------------------------------------------------------------
-# Diagnostic: touched-only gradient accumulation of a camera batch
-# ---------------------------------------------------------------------------
-def _look_at(eye, target, up=(0.0, 0.0, 1.0)) -> np.ndarray:
-    """OpenGL view matrix (camera looks down -Z)."""
-    eye, target, up = (np.asarray(v, dtype=np.float64) for v in (eye, target, up))
-    f = (target - eye) / np.linalg.norm(target - eye)
-    s = np.cross(f, up)
-    s /= np.linalg.norm(s)
-    m = np.eye(4)
-    m[0, :3], m[1, :3], m[2, :3] = s, np.cross(s, f), -f
-    m[:3, 3] = -m[:3, :3] @ eye
-    return m
-
-
-def _perspective(fovy_deg: float, aspect: float, near: float, far: float) -> np.ndarray:
-    t = 1.0 / np.tan(np.radians(fovy_deg) / 2.0)
-    m = np.zeros((4, 4))
-    m[0, 0], m[1, 1] = t / aspect, t
-    m[2, 2], m[2, 3] = (far + near) / (near - far), 2.0 * far * near / (near - far)
-    m[3, 2] = -1.0
-    return m
-
-
-def cull_probe(args):
-    """Not the bench line. Frustum culling of a configs[4]-sized scene
-    (61,036 block spheres, blocks of 16,384 Gaussians in a 200^3 box) for a
-    16-camera batch: BlockCuller (one launch; device time with CUDA events,
-    and with the per-camera id lists read back to Python lists) against the
-    reference's per-camera numpy evaluation (oracle/culling.py, the same
-    numpy operations) on the host; checks the visible sets are equal."""
-    import warnings
-
-    from oracle import culling as oc
-    from tidegs_b200 import BlockCuller
-
-    warnings.filterwarnings("ignore", message="Suspicious plane orientations")
-    torch.cuda.set_device(0)
-    rng = np.random.default_rng(11)
-    n = 61036
-    centers = rng.uniform(-100.0, 100.0, (n, 3))
-    half = rng.uniform(1.0, 6.0, (n, 3))
-    bounds = np.concatenate([centers - half, centers + half], axis=1).astype(np.float32)
-    cams = []
-    for _ in range(16):
-        ang = rng.uniform(0, 2 * np.pi)
-        eye = np.array([110 * np.cos(ang), 110 * np.sin(ang), rng.uniform(10, 60)])
-        cams.append((_look_at(eye, rng.uniform(-60, 60, 3)),
-                     _perspective(rng.uniform(25, 45), 16 / 9, 0.5, 260.0)))
-    from tidegs_b200.culling import extract_frustum_planes
-
-    cu = BlockCuller(torch.from_numpy(bounds).cuda(), verbose=False)
-    planes_ms, dev_ms, list_ms = [], [], []
-    for k in range(args.warmup + args.steps):
+        a0, a1 = _events()
+        b0, b1 = _events()
+        a0.record()
+        if h2d:
+            _ops.h2d_blocks(h_dst, h_src, [bpb] * nb, device)
+        a1.record()
+        with torch.cuda.stream(side):
+            b0.record(side)
+            if d2h:
+                _ops.d2h_blocks(d_dst, d_src, [bpb] * no, device)
+            b1.record(side)
         torch.cuda.synchronize()
+        return a0.elapsed_time(a1), b0.elapsed_time(b1)
+
+    run(True, True)
+    h_ms, _ = run(True, False)
+    _, d_ms = run(False, True)
+    hc_ms, dc_ms = run(True, True)
+    del dev
+    return {"h2d_GBps": nb * bpb / h_ms / 1e6, "d2h_GBps": no * bpb / d_ms / 1e6,
+            "concurrent_h2d_GBps": nb * bpb / hc_ms / 1e6,
+            "concurrent_d2h_GBps": no * bpb / dc_ms / 1e6,
+            "concurrent_total_GBps": (nb + no) * bpb / max(hc_ms, dc_ms) / 1e6,
+            "blocks": [nb, no]}
+
+
+def bench_materialization(api, device, first_k: int, iterations: int = 240,
+                          warmup: int = 3) -> dict:
+    """materialization only over the e2e leg's host tier: each
+    iteration TURNOVER random slots take random non-resident blocks of the
+    rank's page-locked host cache (random block-id -> slot remap; H2D,
+    unpack, slot swap through DoubleBufferGPUWorkingSet), Bernoulli(0.5)
+    dirty flags on the evicted blocks, compacted and written back into the
+    cache (GPUWorkingSet.stage_updated_blocks, D2H)."""
+    turn = RandomTurnover(api.sched.slot_block, api.host_blocks, seed=3)
+    for i in range(warmup):
+        api.step(first_k + i, turn=turn.turnover(i), optimize=False)
+    torch.cuda.synchronize()
+    api.h2d_bytes = api.d2h_bytes = 0
+    e0, e1 = _events()
+    t0 = time.perf_counter()
+    e0.record()
+    for i in range(warmup, warmup + iterations):
+        api.step(first_k + i, turn=turn.turnover(i), optimize=False)
+    e1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = e0.elapsed_time(e1)
+    link = link_probe(api, device, TURNOVER, TURNOVER // 2)
+    moved = api.h2d_bytes + api.d2h_bytes
+    achieved = moved / (ms / 1e3) / 1e9
+    ceiling = link.get("concurrent_total_GBps")
+    return {"config": f"configs[2]: {SLOTS} slots x {B}, {TURNOVER} random slots replaced per "
+                      f"iteration from the rank's page-locked host tier "
+                      f"({api.host_blocks.size} blocks), Bernoulli(0.5) dirty write-back, "
+                      f"{iterations} iterations",
+            "ms_per_iteration": ms / iterations, "wall_ms_per_iteration": 1e3 * wall / iterations,
+            "h2d_bytes_per_iteration": api.h2d_bytes / iterations,
+            "d2h_bytes_per_iteration": api.d2h_bytes / iterations,
+            "host_link_GBps": achieved, "link_ceiling": link,
+            "frac_of_link_ceiling": (achieved / ceiling) if ceiling else None}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline and reference arm: the reference's torch CPU path of the same
+# step (oracle/cpu_step.py), on the same seeded schedule
+# ---------------------------------------------------------------------------
+def run_cpu_step(slots: int, steps: int, warmup: int, seconds_budget: float = None) -> dict:
+    """Runs the reference's CPU step over `slots` resident slots (the
+    workload's other ratios kept) on this workload's schedule: `warmup`
+    untimed steps, then `steps` timed ones (or, with a budget, as many as fit
+    in `seconds_budget`, at least one). All host threads."""
+    from oracle.cpu_step import ReferenceCpuStep
+
+    # The CPU step allocates its temporaries (index_select results, ~0.2 GB
+    # each) anew every step, as the reference does. Keep freed heap memory
+    # for reuse instead of returning it to the kernel, so that the baseline
+    # is not charged a fresh round of page faults per step.
+    try:
+        import ctypes
+
+        libc = ctypes.CDLL("libc.so.6")
+        libc.mallopt(-3, ctypes.c_int(2 ** 31 - 1))  # M_MMAP_THRESHOLD
+        libc.mallopt(-1, ctypes.c_int(2 ** 31 - 1))  # M_TRIM_THRESHOLD
+    except OSError:
+        pass
+    saved = SLOTS
+    set_slots(slots)
+    try:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        n_trace = warmup + (steps if seconds_budget is None else 10_000) + 1
+        sched = Schedule(0, 1)
+        max_vis = sched.traj.max_owned_visible() * B
+        cpu = ReferenceCpuStep(SLOTS, B, TURNOVER, max_vis, pool_blocks=32,
+                               num_blocks=SCENE_BLOCKS, seed=0)
+        rows_in_block = torch.arange(B, dtype=torch.int64)
+
+        def one(k):
+            pos = sched.visible_positions(k)
+            # the touched rows, as the engine lists them (all rows of the
+            # visible blocks, ascending)
+            ids = (torch.from_numpy(pos)[:, None] * B + rows_in_block[None, :]).reshape(-1)
+            evict_pos, incoming, dirty = sched.turnover(k)
+            n = cpu.step(ids, sched.slot_block[pos].tolist(), pos, evict_pos,
+                         sched.slot_block[evict_pos].copy(), incoming, dirty)
+            sched.slot_block[evict_pos] = incoming
+            return n
+
+        for k in range(warmup):
+            one(k)
+        rows = done = 0
         t0 = time.perf_counter()
-        planes = np.stack([extract_frustum_planes(v, p) for v, p in cams])
-        t1 = time.perf_counter()
-        cu.cull_cameras(None, planes=planes, as_tensors=True)  # uploads stay out of the timing
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        ids, counts = cu.cull_cameras(None, planes=planes, as_tensors=True)
-        e1.record()
-        torch.cuda.synchronize()
-        t2 = time.perf_counter()
-        lists = cu.cull_cameras(cams)
-        t3 = time.perf_counter()
-        if k >= args.warmup:
-            planes_ms.append((t1 - t0) * 1e3)
-            dev_ms.append(e0.elapsed_time(e1))
-            list_ms.append((t3 - t2) * 1e3)
-    c_np, r_np = oc.spheres(bounds)
-    t0 = time.perf_counter()
-    want = [oc.visible(c_np, r_np, oc.planes(v, p)).tolist() for v, p in cams]
-    cpu_ms = (time.perf_counter() - t0) * 1e3
-    if want != lists:
-        raise RuntimeError("cull-probe: visible sets differ from the oracle")
-    vis = sum(len(x) for x in want)
-    print(json.dumps({"probe": "frustum_cull", "blocks": n, "cameras": 16,
-                      "visible_fraction": round(vis / (16 * n), 3),
-                      "host_planes_ms": round(statistics.median(planes_ms), 3),
-                      "gpu_launch_ms": round(statistics.median(dev_ms), 4),
-                      "gpu_with_python_lists_ms": round(statistics.median(list_ms), 3),
-                      "reference_numpy_ms": round(cpu_ms, 2), "equal": True}), flush=True)
+        k = warmup
+        while k < n_trace - 1:
+            rows += one(k)
+            done += 1
+            k += 1
+            if seconds_budget is None:
+                if done == steps:
+                    break
+            elif time.perf_counter() - t0 > seconds_budget:
+                break
+        elapsed = time.perf_counter() - t0
+        return {"value": rows / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
+                "ms_per_step": 1e3 * elapsed / done, "steps": done, "warmup": warmup,
+                "slots": SLOTS, "rows_per_step": rows / done,
+                "sample": (f"{SLOTS} slots x {B} rows ({'a full GPU resident set' if SLOTS == 2048 else f'{SLOTS}/2048 of a GPU resident set'}), "
+                           f"the bench's schedule at one rank (~30% of the slots visible, all "
+                           f"their rows updated; {TURNOVER} blocks turned over, dirty ones "
+                           f"written back), "
+                           f"{done} timed steps after {warmup} warm-up steps in {elapsed:.1f} s: "
+                           "the reference's torch CPU step (oracle/cpu_step.py: optimizer "
+                           "gpu_resident_optimizer.py:266-364, dirty marks, bounds, write-back "
+                           "pack gpu_working_set.py:968-975, block staging, unpack, id fill and "
+                           "slot swap double_buffer_gpu.py:791-837,944-951,1053-1062, moments "
+                           "cleared on admission)")}
+    finally:
+        set_slots(saved)
 
 
-def render_probe(args):
-    """Not the bench line. The engine's render path for one camera batch
-    (strategies/tide_engine/engine.py:481-561): projection, tile intersection,
-    SH colors (degree 3), rasterization forward and the three backward
-    kernels, tidegs_b200 against
-    the reference's gsplat 1.0.0 kernels compiled from its sources
-    (oracle/_ref/gsplat) on the same inputs. Seeded scene: 2 M Gaussians in
-    a box in front of a 1920 x 1080 camera, log-normal scales, uniform
-    opacities, N(0, 0.2) degree-3 SH coefficients (colors evaluated from them,
-    as the engine does). One JSON line per implementation (CUDA events,
-    median over --steps after --warmup)."""
-    from oracle import build_ref
-    from oracle import render as orc
-    from tidegs_b200 import render as tr
-
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
-    Wd, Hd, tile, n = 1920, 1080, 16, 2_000_000
-    g = torch.Generator(device=dev).manual_seed(3)
-    means = (torch.rand((n, 3), generator=g, device=dev) * torch.tensor([16.0, 9.0, 20.0], device=dev)
-             + torch.tensor([-8.0, -4.5, 4.0], device=dev))
-    quats = torch.randn((n, 4), generator=g, device=dev)
-    scales = torch.exp(torch.randn((n, 3), generator=g, device=dev) * 0.5 - 3.2)
-    opac = torch.rand((1, n), generator=g, device=dev) * 0.9 + 0.05
-    # degree-3 SH coefficients (16 per channel), colors evaluated per camera
-    coeffs = torch.randn((1, n, 16, 3), generator=g, device=dev) * 0.2
-    dirs = (means - torch.tensor([0.0, 0.0, -1.0], device=dev))[None].contiguous()
-    view = orc.look_at((0.0, 0.0, -1.0), (0.0, 0.0, 10.0), up=(0.0, -1.0, 0.0))[None].float().to(dev)
-    K = orc.intrinsics(Wd, Hd, 70.0)[None].float().to(dev)
-    tw, th = (Wd + tile - 1) // tile, (Hd + tile - 1) // tile
-    ref = build_ref.load_prebuilt_gsplat()
-    means_g, quats_g, scales_g = (t.clone().requires_grad_(True) for t in (means, quats, scales))
-    coeffs_g = coeffs.clone().requires_grad_(True)
-
-    def run_ours():
-        marks = {}
-        radii, m2, dep, con, _ = tr._Projection.apply(means_g, quats_g, scales_g, view, K, Wd, Hd,
-                                                      0.3, 0.01, 1e10, 0.0, False)
-        marks["projection"] = torch.cuda.Event(enable_timing=True)
-        marks["projection"].record()
-        sh_out = tr.spherical_harmonics(3, dirs, coeffs_g)
-        colors = sh_out.detach()
-        marks["sh"] = torch.cuda.Event(enable_timing=True)
-        marks["sh"].record()
-        _, ids, flat = tr.isect_tiles(m2, radii, dep, tile, tw, th)
-        offs = tr.isect_offset_encode(ids, 1, tw, th)
-        marks["intersect"] = torch.cuda.Event(enable_timing=True)
-        marks["intersect"].record()
-        # the raw kernels, called as the reference arm calls its binding
-        m2d, cond = m2.detach(), con.detach()
-        rc, ra, last = tr.rasterize_to_pixels_fwd(m2d, cond, colors, opac, None, Wd, Hd, tile,
-                                                  offs, flat)
-        marks["raster_fwd"] = torch.cuda.Event(enable_timing=True)
-        marks["raster_fwd"].record()
-        _, vm, vc, vcol, _ = tr.rasterize_to_pixels_bwd(m2d, cond, colors, opac, None, Wd, Hd,
-                                                        tile, offs, flat, ra, last,
-                                                        torch.ones_like(rc), torch.ones_like(ra),
-                                                        False)
-        marks["raster_bwd"] = torch.cuda.Event(enable_timing=True)
-        marks["raster_bwd"].record()
-        # autograd.grad: the gradients are returned, not added into the
-        # leaves' .grad (an extra pass over them the reference arm does not do)
-        torch.autograd.grad([sh_out], [coeffs_g], [vcol])
-        marks["sh_bwd"] = torch.cuda.Event(enable_timing=True)
-        marks["sh_bwd"].record()
-        torch.autograd.grad([m2, dep, con], [means_g, quats_g, scales_g],
-                            [vm, torch.zeros_like(dep), vc])
-        marks["projection_bwd"] = torch.cuda.Event(enable_timing=True)
-        marks["projection_bwd"].record()
-        return marks, int(flat.numel())
-
-    def run_ref():
-        marks = {}
-        radii, m2, dep, con, _ = ref.fully_fused_projection_fwd(means, None, quats, scales, view, K,
-                                                                Wd, Hd, 0.3, 0.01, 1e10, 0.0, False)
-        marks["projection"] = torch.cuda.Event(enable_timing=True)
-        marks["projection"].record()
-        colors = ref.compute_sh_fwd(3, dirs, coeffs, None)
-        marks["sh"] = torch.cuda.Event(enable_timing=True)
-        marks["sh"].record()
-        _, ids, flat = ref.isect_tiles(m2, radii, dep, None, None, 1, tile, tw, th, True, True)
-        offs = ref.isect_offset_encode(ids, 1, tw, th)
-        marks["intersect"] = torch.cuda.Event(enable_timing=True)
-        marks["intersect"].record()
-        rc, ra, last = ref.rasterize_to_pixels_fwd(m2, con, colors, opac, None, Wd, Hd, tile, offs, flat)
-        marks["raster_fwd"] = torch.cuda.Event(enable_timing=True)
-        marks["raster_fwd"].record()
-        _, vm, vc, vcol, vo = ref.rasterize_to_pixels_bwd(m2, con, colors, opac, None, Wd, Hd, tile,
-                                                          offs, flat, ra, last, torch.ones_like(rc),
-                                                          torch.ones_like(ra), False)
-        marks["raster_bwd"] = torch.cuda.Event(enable_timing=True)
-        marks["raster_bwd"].record()
-        ref.compute_sh_bwd(16, 3, dirs, coeffs, None, vcol, False)
-        marks["sh_bwd"] = torch.cuda.Event(enable_timing=True)
-        marks["sh_bwd"].record()
-        ref.fully_fused_projection_bwd(means, None, quats, scales, view, K, Wd, Hd, 0.3, radii, con,
-                                       None, vm, torch.zeros_like(dep), vc, None, False)
-        marks["projection_bwd"] = torch.cuda.Event(enable_timing=True)
-        marks["projection_bwd"].record()
-        return marks, int(flat.numel())
-
-    arms = [("tidegs_b200", run_ours)]
-    if ref is not None:
-        arms.append(("reference_gsplat", run_ref))
-    for name, fn in arms:
-        per = {}
-        for k in range(args.warmup + args.steps):
-            torch.cuda.synchronize()
-            e0 = torch.cuda.Event(enable_timing=True)
-            e0.record()
-            marks, n_isects = fn()
-            torch.cuda.synchronize()
-            if k < args.warmup:
-                continue
-            prev = e0
-            for stage, ev in marks.items():
-                per.setdefault(stage, []).append(prev.elapsed_time(ev))
-                prev = ev
-        out = {"probe": "render", "impl": name, "gaussians": n, "image": [Wd, Hd],
-               "intersections": n_isects}
-        out.update({k + "_ms": round(statistics.median(v), 3) for k, v in per.items()})
-        out["total_ms"] = round(sum(out[k + "_ms"] for k in per), 3)
-        print(json.dumps(out), flush=True)
+def cpu_baseline(seconds_budget: float = 15.0):
+    """The cpu_baseline object of this arm's line: a bounded sample (64 of
+    the 2048 slots, the same ratios) for about `seconds_budget` seconds."""
+    base = run_cpu_step(64, 0, 2, seconds_budget=seconds_budget)
+    return {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "ms_per_step")}
 
 
-def accum_probe(args):
-    """Not the bench line. A camera batch of the configs[3] shape (16 cameras,
-    each seeing a contiguous run of 24-56 resident blocks of 16,384 rows out
-    of 2048) accumulated by SparseGradAccumulator, and by the reference's own
-    torch operations on the same GPU (engine.py:1801-1826: mask, nonzero,
-    zeros; :2434-2471: searchsorted + six scatter_add_ per camera). Checks the
-    two results are equal; prints one JSON line (CUDA events, median)."""
-    from tidegs_b200 import SparseGradAccumulator
+def reference_arm_slots(limit: int) -> int:
+    """Resident slots the reference arm can hold in this host's memory: the
+    full 2048 when the CPU step's buffers fit in 70 % of it, else halved
+    until they do."""
+    from oracle.cpu_step import host_bytes
 
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda", 0)
-    M = SLOTS * B
-    rng = np.random.default_rng(10_000)
-    filters, grads = [], []
-    for _ in range(16):
-        length = max(1, int(rng.integers(24, 56) * SLOTS / 2048))
-        start = int(rng.integers(0, max(1, SLOTS - length)))
-        f = torch.arange(start * B, (start + length) * B, dtype=torch.int64, device=dev)
-        n = f.numel()
-        filters.append(f)
-        grads.append({k: torch.empty((n, w), device=dev).normal_(0, 1e-3) for k, w in
-                      (("xyz", 3), ("opacity", 1), ("scaling", 3), ("rotation", 4), ("shs", 48))})
-    filter_rows = sum(f.numel() for f in filters)
-
-    split = []
-
-    def ours():
-        acc = SparseGradAccumulator(filters, M)
-        mid = torch.cuda.Event(enable_timing=True)
-        mid.record()
-        for f, g in zip(filters, grads):
-            acc.add(f, g["xyz"], g["opacity"], g["scaling"], g["rotation"], g["shs"])
-        split.append(mid)
-        return acc.sparse_grad_local_ids, acc.sparse_grad_components
-
-    def reference():
-        mask = torch.zeros((M,), dtype=torch.bool, device=dev)
-        for f in filters:
-            mask.scatter_(0, f, True)
-        ids = torch.nonzero(mask, as_tuple=False).flatten()
-        n = int(ids.numel())
-        comps = {k: torch.zeros((n, w), device=dev) for k, w in WIDTHS.items()}
-        for f, g in zip(filters, grads):
-            idx = torch.searchsorted(ids, f)
-            for k, w in (("xyz", 3), ("opacity", 1), ("scaling", 3), ("rotation", 4)):
-                comps[k].scatter_add_(0, idx.reshape(-1, 1).expand(-1, w), g[k])
-            comps["features_dc"].scatter_add_(0, idx.reshape(-1, 1).expand(-1, 3), g["shs"][:, :3])
-            comps["features_rest"].scatter_add_(0, idx.reshape(-1, 1).expand(-1, 45),
-                                                g["shs"][:, 3:48])
-        return ids, comps
-
-    out = {}
-    adds = []
-    for name, fn in (("tidegs_b200", ours), ("reference_torch_ops", reference)):
-        times = []
-        for k in range(args.warmup + args.steps):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            split.clear()
-            e0.record()
-            res = fn()
-            e1.record()
-            torch.cuda.synchronize()
-            if k >= args.warmup:
-                times.append(e0.elapsed_time(e1))
-                if split:
-                    adds.append(split[0].elapsed_time(e1))
-        out[name] = (sorted(times)[len(times) // 2], res)
-    (ids_a, ca), (ids_b, cb) = out["tidegs_b200"][1], out["reference_torch_ops"][1]
-    equal = bool(torch.equal(ids_a, ids_b)) and all(torch.equal(ca[k], cb[k]) for k in WIDTHS)
-    ms = out["tidegs_b200"][0]
-    print(json.dumps({"probe": "sparse_grad_accumulation", "cameras": len(filters),
-                      "filter_rows": filter_rows, "touched_rows": int(ids_a.numel()),
-                      "ms": ms, "reference_torch_ops_ms": out["reference_torch_ops"][0],
-                      "equal_to_reference_ops": equal,
-                      "accumulate_ms": sorted(adds)[len(adds) // 2],
-                      "accumulate_GBps": filter_rows * 712 / (sorted(adds)[len(adds) // 2] / 1e3)
-                      / 1e9}), flush=True)
-    return 0
+    slots = SLOTS
+    while slots > 64 and host_bytes(slots, B, max(1, slots // 4), 0.35, 32) > 0.7 * limit:
+        slots //= 2
+    return slots
 
 
-# ---------------------------------------------------------------------------
-# CPU baseline: the reference's torch CPU path (oracle port), bounded sample
-# ---------------------------------------------------------------------------
-def cpu_baseline(seconds_budget: float = 12.0):
-    from oracle.resident_adam import COMPONENT_SPECS, TorchFallbackResidentAdam
-    from oracle import blocks as ob
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    slots = 64                      # 1/32 of a GPU's 2048 slots, same ratios
-    Bs = B
-    rows = slots * Bs
-    opt = TorchFallbackResidentAdam(rows, seed=0)
-    rng = np.random.default_rng(0)
-    vis = np.sort(rng.choice(slots, int(round(slots * 0.3)), replace=False))
-    local = torch.from_numpy((vis[:, None] * Bs + np.arange(Bs)[None, :]).reshape(-1))
-    n = local.numel()
-    grads = {name: torch.randn((n, w)) * 1e-3 for name, _, w, _ in COMPONENT_SPECS}
-    lrs = [LRS[name] for name, _, _, _ in COMPONENT_SPECS]
-    slots_of_row = local // Bs
-    turnover = slots // 4
-    packed_in = torch.randn((turnover * Bs, 59))
-    done_rows = 0
-    t0 = time.perf_counter()
-    steps = 0
-    while True:
-        opt.step(local, local, slots_of_row, grads, lrs, slots, step=steps + 1, batch_size=16)
-        # materialization + write-back of the same sample (torch CPU copies,
-        # as the reference's fallback paths do them)
-        ev = np.sort(rng.choice(slots, turnover, replace=False))
-        for i, s in enumerate(ev):
-            src = packed_in[i * Bs:(i + 1) * Bs]
-            for name, (a, w) in (("xyz", (0, 3)), ("scaling", (3, 3)), ("rotation", (6, 4)),
-                                 ("opacity", (10, 1)), ("features_dc", (11, 3)),
-                                 ("features_rest", (14, 45))):
-                opt.params[name][s * Bs:(s + 1) * Bs].copy_(src[:, a:a + w])
-        dirty = ev[: turnover // 2]
-        torch.cat([torch.cat([opt.params[nm][s * Bs:(s + 1) * Bs] for nm in
-                              ("xyz", "scaling", "rotation", "opacity", "features_dc",
-                               "features_rest")], dim=1) for s in dirty])
-        done_rows += n
-        steps += 1
-        if time.perf_counter() - t0 > seconds_budget:
-            break
-    elapsed = time.perf_counter() - t0
-    return {
-        "value": done_rows / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
-        # one full-size step (SLOTS slots) at the sample's rate
-        "ms_per_step": 1e3 * (n * SLOTS / slots) / (done_rows / elapsed),
-        "sample": (f"{slots} slots x {Bs} rows (1/32 of a GPU's resident set), 30% blocks "
-                   f"visible ({n} rows), 25% turnover, {steps} steps in {elapsed:.1f} s: "
-                   "reference torch CPU step (gpu_resident_optimizer.py:339-364 ported), "
-                   "slot fill and write-back pack by torch copies"),
-    }
-
-
-# ---------------------------------------------------------------------------
 def run_reference_arm(args, world, rank):
+    """`--impl reference`: the reference's own CPU implementation of the
+    step, the whole configs[3] workload when the host holds it (else the
+    largest power-of-two share that fits, stated), timed over exactly
+    --steps steps after --warmup steps, on rank 0 (other ranks exit)."""
     if rank != 0:
         return 0
-    budget = max(1.0, 20.0 / max(1, args.steps + args.warmup))
-    base = cpu_baseline(seconds_budget=budget * max(1, args.steps))
+    slots = reference_arm_slots(host_memory_limit())
+    # keep the whole run to a few minutes: a short calibration on a small
+    # share gives this host's rate; halve the share until the run's
+    # --steps + --warmup steps are expected to take under 150 s (the rate
+    # drops on larger working sets, hence the margin)
+    rate = run_cpu_step(64, 2, 1)["value"]
+    rows_full = VISIBLE_FRAC * SLOTS * B
+    while slots > 64 and (args.steps + args.warmup) * rows_full * (slots / SLOTS) / rate * 1.5 > 150:
+        slots //= 2
+    base = run_cpu_step(slots, args.steps, args.warmup)
+    same = slots == SLOTS
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": UNIT,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": args.gpus, "steps": base["steps"], "warmup": base["warmup"],
         "ms_per_step": base["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded, BASELINE configs[3] shapes and distributions)",
-        "config": dict(WORKLOAD_CONFIG, slots_per_gpu=SLOTS, block_size=B,
-                       turnover_blocks=TURNOVER,
-                       run="the reference's CPU step on a bounded sample of this workload "
-                           "(cpu_baseline.sample), all host threads, rank 0 only"),
+        "config": dict(WORKLOAD_CONFIG, slots_per_gpu=slots, block_size=B,
+                       turnover_blocks=max(1, slots // 4),
+                       rows_updated_per_step=base["rows_per_step"],
+                       run=("the reference's CPU step on this arm's full workload"
+                            if same else
+                            f"the reference's CPU step on {slots} of the workload's {SLOTS} "
+                            "slots (to fit this host's memory and a run of a few minutes), same "
+                            "ratios; value and ms_per_step are that sample's")
+                       + ", all host threads, rank 0 only"),
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -1322,15 +1439,19 @@ def main(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="tidegs_b200", choices=["tidegs_b200", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--e2e-warmup", type=int, default=6)
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--e2e-warmup", type=int, default=4)
     ap.add_argument("--e2e-profile", action="store_true",
                     help="print a per-phase wall-time breakdown of the e2e step to stderr")
-    ap.add_argument("--pool-blocks", type=int, default=1024,
+    ap.add_argument("--pool-blocks", type=int, default=256,
                     help="distinct seeded host blocks (scene block b holds block b mod this)")
     ap.add_argument("--host-tier", default="cache", choices=["cache", "pool"],
-                    help="e2e host side: PinnedBlockCache over every scene block of the rank "
+                    help="e2e host side: PinnedBlockCache over every block the rank touches "
                          "(write-back lands in it), or the fixed modulo PinnedBlockPool")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="leave out the configs[0]/[1]/[2] measurements at N=1")
+    ap.add_argument("--materialize-iters", type=int, default=240,
+                    help="configs[2] iterations (materialization only)")
     ap.add_argument("--slots", type=int, default=SLOTS,
                     help="resident slots per GPU (default: the configs[3] value; smaller "
                          "values make small profiling cases of the same step)")
@@ -1339,16 +1460,6 @@ def main(argv=None):
                     help="print a per-phase CUDA-event breakdown of the device step to stderr "
                          "(extra events; not used for the reported value)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--pull-probe", default=None, metavar="MODES",
-                    help="diagnostic instead of the bench: comma list of remote,local,plain "
-                         "(needs two GPUs for remote)")
-    ap.add_argument("--cull-probe", action="store_true",
-                    help="diagnostic: frustum culling of a 61,036-block scene, 16 cameras")
-    ap.add_argument("--render-probe", action="store_true",
-                    help="diagnostic: render path, ours vs the reference gsplat kernels")
-    ap.add_argument("--accum-probe", action="store_true",
-                    help="diagnostic instead of the bench: touched-only gradient accumulation "
-                         "of a camera batch against the reference's torch operations")
     ap.add_argument("--exchange", default="pull", choices=["pull", "push", "nccl"],
                     help="N>1 gradient exchange: the owner's update kernel sums the senders' "
                          "gradients over NVLink (pull, default); a push kernel into receive "
@@ -1359,26 +1470,18 @@ def main(argv=None):
     world, rank, local = dist_setup()
     if args.impl == "reference":
         return run_reference_arm(args, world, rank)
-    if args.pull_probe:
-        return pull_probe(args, args.pull_probe.split(","))
-    if args.accum_probe:
-        return accum_probe(args)
-    if args.cull_probe:
-        return cull_probe(args)
-    if args.render_probe:
-        return render_probe(args)
 
     from tidegs_b200 import _lib
 
     device = torch.device("cuda", torch.cuda.current_device())
-    global POOL_MULT
-    POOL_MULT, args.host_tier = plan_host_pool(world, args.host_tier, args.pool_blocks,
-                                               host_memory_limit())
-    n_trace = max(args.warmup + args.steps + 3, args.e2e_warmup + args.e2e_steps + 1)
+    n_e2e = args.e2e_warmup + args.e2e_steps
+    host_blocks = Schedule(rank, world).touched_blocks(n_e2e + 1)
+    args.host_tier = plan_host_tier(world, args.host_tier, args.pool_blocks,
+                                    host_blocks.size, host_memory_limit())
+    n_trace = max(args.warmup + args.steps + 4, n_e2e + 1)
     trace = ScheduleTrace(world, rank, n_trace)
-    scheds = [Schedule(o, world) for o in range(world)]
-    sched = scheds[rank]
-    dev = DeviceStep(device, sched, trace, scheds=scheds, world=world, exchange=args.exchange)
+    sched = Schedule(rank, world)
+    dev = DeviceStep(device, sched, trace, world=world, exchange=args.exchange)
     for k in range(args.warmup):
         dev.step(k)
     torch.cuda.synchronize()
@@ -1394,12 +1497,14 @@ def main(argv=None):
         rows += dev.step(k, timed=True)
     end.record()
     torch.cuda.synchronize()
+    next_k = args.warmup + args.steps
     if args.phase_times:
         # separate, untimed pass: per-phase CUDA events around each stage
         dev.phase_ms, dev.host_ms = {}, {}
-        for k in range(args.warmup + args.steps, args.warmup + args.steps + 3):
+        for k in range(next_k, next_k + 3):
             dev.step(k)
             dev.collect_phases()
+        next_k += 3
         print(f"rank {rank} device phase ms/step: " + json.dumps(
             {n: round(sum(v) / len(v), 3) for n, v in dev.phase_ms.items()})
             + " host ms/step: " + json.dumps(
@@ -1409,6 +1514,8 @@ def main(argv=None):
     barrier(world)
     clock_info = clocks.stop()
     launches = _lib.launch_counter["kernels"] - launches0
+    # result check of the same step, outside the timed region
+    parity = dev.parity_check(next_k)
     ms = start.elapsed_time(end)
     ms_max = allreduce_max(ms, world)
     total_rows = rows * world
@@ -1426,11 +1533,12 @@ def main(argv=None):
 
     # e2e leg through the Python API (host pool -> HBM -> host)
     e2e = None
+    configs = {}
     try:
         if args.no_e2e:
             raise _Skipped("--no-e2e")
-        api = ApiStep(device, [Schedule(o, world) for o in range(world)], trace, rank, world,
-                      args.pool_blocks, exchange=args.exchange, host_tier=args.host_tier)
+        api = ApiStep(device, Schedule(rank, world), trace, rank, world, args.pool_blocks,
+                      host_blocks, exchange=args.exchange, host_tier=args.host_tier)
         for k in range(args.e2e_warmup):
             api.step(k)
         torch.cuda.synchronize()
@@ -1451,8 +1559,10 @@ def main(argv=None):
                "d2h_bytes_per_step": int(api.d2h_bytes / args.e2e_steps),
                "ms_per_step": e_ms / args.e2e_steps, "steps": args.e2e_steps,
                "host_pool_blocks": args.pool_blocks,
-               "host_tier": (f"PinnedBlockCache of the rank's {POOL_MULT * SLOTS} scene blocks "
-                             f"(+{TURNOVER} write-back entries); write-back DMA into it"
+               "host_tier": (f"PinnedBlockCache of the {host_blocks.size} blocks the rank "
+                             f"holds during the e2e steps (+{TURNOVER} write-back entries; "
+                             f"scene block b's rows = seeded block b mod {args.pool_blocks}); "
+                             "write-back DMA into it"
                              if args.host_tier == "cache" else
                              f"PinnedBlockPool of {args.pool_blocks} blocks (block id mod pool)")}
         if api.profile is not None and rank == 0:
@@ -1461,12 +1571,24 @@ def main(argv=None):
                 + " writeback staging bytes: "
                 + str(api.ws.writeback_stats["pinned_staging_bytes"]),
                 file=sys.stderr, flush=True)
+        if world == 1 and not args.no_configs and args.host_tier == "cache":
+            configs["materialization"] = bench_materialization(
+                api, device, n_e2e, iterations=args.materialize_iters)
         api.close()
         del api
     except _Skipped as why:
         e2e = {"value": None, "unit": UNIT, "skipped": str(why)}
     except Exception as exc:  # report, never hide
         e2e = {"value": None, "unit": UNIT, "error": f"{type(exc).__name__}: {exc}"}
+
+    torch.cuda.empty_cache()
+    if world == 1 and not args.no_configs:
+        for name, fn in (("selective_adam", bench_selective_adam), ("sophia", bench_sophia)):
+            try:
+                configs[name] = fn(device)
+            except Exception as exc:  # report, never hide
+                configs[name] = {"error": f"{type(exc).__name__}: {exc}"}
+            torch.cuda.empty_cache()
 
     base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -1477,10 +1599,11 @@ def main(argv=None):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded, BASELINE configs[3] shapes and distributions)",
+            "data": "synthetic (seeded, BASELINE configs[3]/[4] shapes and distributions)",
             "config": {**WORKLOAD_CONFIG,
                        "slots_per_gpu": SLOTS, "block_size": B, "turnover_blocks": TURNOVER,
-                       "scene_blocks_per_gpu": POOL_MULT * SLOTS,
+                       "scene_blocks": SCENE_BLOCKS,
+                       "host_tier_blocks_per_gpu": int(host_blocks.size),
                        "rows_updated_per_step": rows / args.steps,
                        "parallelism": f"block ownership, rank = block_id mod {world}",
                        "exchange_rows_per_step": exchange_rows / (args.warmup + args.steps),
@@ -1502,8 +1625,10 @@ def main(argv=None):
                          "avg_launch_ms_max_over_ranks": adam_max_ms},
             "clocks": clock_info,
             "gpu_launches": launches,
+            "parity": parity,
             "e2e": e2e,
             "cpu_baseline": base,
+            "configs": configs or None,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

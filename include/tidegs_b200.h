@@ -126,6 +126,12 @@ typedef struct {
 
   int32_t* pos_count;         /* [P] out: touched rows per position */
   int32_t* err;               /* [4] device error word (zeroed by the call) */
+
+  /* Optional [ceil(n/32)][2] out, or NULL: per 32-row chunk of local_ids,
+   * (first local row, first state row) when the chunk's rows and state rows
+   * both run consecutively and its first row is a multiple of 4 (the update
+   * then streams it by bulk copies), else (-1, -1). */
+  int64_t* chunk_table;
 } TgsResidentCountArgs;
 
 /* Validates local_ids (range, strict order, residency), counts touched rows
@@ -157,6 +163,13 @@ typedef struct {
   const uint32_t* slot_stamp;             /* [slots] */
   const float* slot_bias;                 /* [slots][2] from tgs_resident_adam_count */
   const int32_t* err;                     /* [4] skip everything when err[0]!=0 */
+
+  /* The chunk table tgs_resident_adam_count wrote for these local_ids, or
+   * NULL. With it, streamable chunks are updated by a bulk-copy pipeline
+   * (one CTA per SM) and marked done in the table (which the call rewrites),
+   * then the other chunks by the per-row kernel; without it, one per-row
+   * launch. Both give the same result bit for bit. */
+  int64_t* chunk_table;
 } TgsResidentAdamArgs;
 
 /* One fused launch updating all 59 columns of every touched row, in the op
@@ -295,8 +308,11 @@ TGS_API int tgs_global_to_local_compact(int64_t* out, int64_t* dev_count,
  * exits), which bounds n to 33,554,432 ids; larger n is rejected with
  * TGS_ERR_INVALID_ARG and a message. The first call on a device looks up the
  * array's device address (with that device current); make that first call
- * before any stream capture. All calls on a device share the array, so calls
- * that overlap on the GPU race: serialize them. */
+ * before any stream capture. The address is kept per device index for the
+ * rest of the process: it does not survive cudaDeviceReset (or a new primary
+ * context on that device), after which this entry point must not be called.
+ * All calls on a device share the array, so calls that overlap on the GPU
+ * race: serialize them. */
 TGS_API int tgs_global_to_local_compact_noalloc(int64_t* out, int64_t* dev_count,
                                                 const int64_t* global_ids, int64_t n,
                                                 const int64_t* block_starts, int64_t num_blocks,

@@ -2,11 +2,14 @@
 
 The update kernels walk the touched rows in chunks of 32. A chunk whose 32 ids
 are consecutive AND whose 32 state rows are consecutive -- every chunk of a
-step that updates whole visible blocks, the benchmark's case -- takes a staged
-path: the chunk's state rows arrive in shared memory by bulk copies while the
-parameters and gradients of the next rows load into registers. Every other
-chunk (sparse rows) resolves and loads row by row. Both paths must give the
-reference's update: the kernel-order restatement of
+step that updates whole visible blocks, the benchmark's case -- is staged:
+when its first id is a multiple of 4 the bulk-copy pipeline streams it (state
+rows, parameters and gradients copied into shared memory, updated there and
+copied back); otherwise the per-row kernel's staged branch brings its state
+rows in by bulk copies while the parameters and gradients of the next rows
+load into registers. Every other chunk (sparse rows) resolves and loads row
+by row. All paths must give the reference's update: the kernel-order
+restatement of
 strategies/tide_engine/gpu_resident_optimizer.py:339-364 in
 oracle/resident_adam.py, bit for bit, for parameters and both moments.
 
@@ -73,7 +76,8 @@ def _values(g):
 
 def _staged_chunks(ids, layout, block_to_slot, B):
     """(chunks the kernels stage, chunks a first/last-row-only test would
-    stage): the kernels' path choice restated on the host."""
+    stage, chunks the bulk-copy pipeline streams): the kernels' path choice
+    restated on the host."""
     ids = np.asarray(ids, np.int64)
     items = sorted((s.start, s.stop, slot) for (b, s), slot in
                    ((it, block_to_slot[it[0]]) for it in layout))
@@ -82,13 +86,15 @@ def _staged_chunks(ids, layout, block_to_slot, B):
     slots = np.array([i[2] for i in items], np.int64)
     pos = np.searchsorted(ends, ids, side="right")
     sr = slots[pos] * B + (ids - starts[pos])
-    staged = ends_only = 0
+    staged = ends_only = streamed = 0
     for c in range(ids.size // 32):
         i, s = ids[32 * c: 32 * c + 32], sr[32 * c: 32 * c + 32]
         lane = np.arange(32)
-        staged += bool(np.all(i == i[0] + lane) and np.all(s == s[0] + lane))
+        ok = bool(np.all(i == i[0] + lane) and np.all(s == s[0] + lane))
+        staged += ok
+        streamed += ok and i[0] % 4 == 0
         ends_only += bool(i[31] == i[0] + 31 and s[31] == s[0] + 31)
-    return staged, ends_only
+    return staged, ends_only, streamed
 
 
 def _layout(blocks, B, tail_block=None, tail_rows=None):
@@ -132,9 +138,9 @@ def _check_state(opt, oracle, layout, B):
 
 
 # Each case: block size, the order in which the admitted blocks occupy the
-# working set's positions (blocks are admitted in ascending id, so block k
-# first holds slot k), an optional short tail block, and the minimum number
-# of staged chunks the first step must contain.
+# working set's positions (blocks are admitted in ascending id into the
+# lowest free slots, so block k first holds slot k), an optional short tail
+# block, and the minimum number of staged chunks the first step must contain.
 CASES = {
     # 4-row blocks in slot order 0,5,2,3,4,1,6,7 (repeated): ids consecutive,
     # state rows not; the first and last rows of a 32-row chunk line up.
@@ -171,7 +177,6 @@ def test_staged_whole_blocks_bit_exact_with_oracle(case):
     oracle = ResidentAdamOracle(batch_size=16, block_size=B, capacity_blocks=len(blocks))
     opt.set_resident_blocks(blocks)
     oracle.set_resident_blocks(blocks)
-    assert opt._block_to_slot == oracle._block_to_slot
 
     for step in range(4):
         if step == 0:
@@ -186,9 +191,10 @@ def test_staged_whole_blocks_bit_exact_with_oracle(case):
             ids = np.unique(np.concatenate([ids, extra])).astype(np.int64)
         else:
             ids = _whole_block_ids(layout, rng)
-        staged, ends_only = _staged_chunks(ids, layout, opt._block_to_slot, B)
+        staged, ends_only, streamed = _staged_chunks(ids, layout, opt._block_to_slot, B)
         if step == 0:
             assert staged >= cfg["min_staged"], (staged, ends_only)
+            assert streamed >= 1, "case must drive the bulk-copy pipeline"
             if cfg["misrouted"]:
                 assert ends_only > staged, "case must contain a chunk whose ends alone line up"
         grads = _random_grads(rng, ids.size)
@@ -212,7 +218,6 @@ def test_staged_whole_blocks_bit_exact_with_oracle(case):
             blocks = sorted(keep + gone[:2] + [newcomer])
             opt.set_resident_blocks(blocks)
             oracle.set_resident_blocks(blocks)
-            assert opt._block_to_slot == oracle._block_to_slot
             # the newcomer takes the dropped block's position in the working set
             order = [newcomer if b == gone[2] else b for b, _ in layout]
             layout = [(b, sl) for b, (_, sl) in zip(order, layout)]
@@ -351,8 +356,8 @@ def test_pull_staged_bit_exact_with_oracle(W, B, reorder):
     summed = np.concatenate([_rank_order_sum(vis, b, B) for b in owned])
     ref_grads = {n: summed[:, ob.UNIFIED[n]:ob.UNIFIED[n] + w].copy() for n, w in ob.WIDTHS.items()}
     if B % 32 == 0:
-        staged, _ = _staged_chunks(ids, layout, opt._block_to_slot, B)
-        assert staged == rows // 32
+        staged, _, streamed = _staged_chunks(ids, layout, opt._block_to_slot, B)
+        assert staged == streamed == rows // 32
     for step in range(3):
         s = opt.step_pulled(step + 1, g, torch.as_tensor(ids).cuda(), pull, plan)
         o = oracle.step(ref, ids, ref_grads, layout, LRS, BETAS, EPS)
@@ -369,5 +374,4 @@ def test_pull_staged_bit_exact_with_oracle(W, B, reorder):
             oracle.set_resident_blocks(keep)
             opt.set_resident_blocks(owned)
             oracle.set_resident_blocks(owned)
-            assert opt._block_to_slot == oracle._block_to_slot
     assert opt.get_stats()["cold_restarts"] == oracle.stats["cold_restarts"]

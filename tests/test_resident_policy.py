@@ -77,3 +77,24 @@ def test_recency_update_fast_path_equals_converting_path():
     slow, _ = rp._updated_recency(dict(upd), np.array([100]), 0.5)  # a foreign copy
     assert fast == slow and list(fast.items()) == list(slow.items())
 
+
+
+def test_recency_dict_edited_in_place_is_converted_again():
+    """A caller that writes numpy scalars into the returned dict gets the
+    reference's conversions on the next transition (resident_policy.py:
+    115-119), exactly as for a foreign dict with the same entries."""
+    import numpy as np
+
+    upd, _ = rp._updated_recency({1: 0.5, 2: 0.25}, np.array([3]), 0.9)
+    upd[np.int64(8)] = np.float32(0.7)
+    upd[1] = np.float32(0.3)
+    edited, _ = rp._updated_recency(upd, np.array([4]), 0.5)
+    foreign, _ = rp._updated_recency(dict(upd), np.array([4]), 0.5)
+    assert list(edited.items()) == list(foreign.items())
+    assert all(type(k) is int for k in edited) and all(type(v) is float for v in edited.values())
+    # an untouched returned dict takes the fast path and gives the same result
+    clean, _ = rp._updated_recency({1: 0.5, 2: 0.25}, np.array([3]), 0.9)
+    assert clean.pristine
+    a, _ = rp._updated_recency(clean, np.array([4]), 0.5)
+    b, _ = rp._updated_recency(dict(clean), np.array([4]), 0.5)
+    assert list(a.items()) == list(b.items())

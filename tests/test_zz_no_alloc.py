@@ -71,6 +71,28 @@ def test_no_alloc_matches_allocating_entry_point_on_two_calls():
         assert torch.equal(got, expect)
 
 
+def test_no_alloc_edge_sizes_match_allocating_entry_point():
+    """No ids (count 0, nothing written) and exactly the largest accepted
+    size, 33,554,432 ids, whose tile counts fill the whole fixed array."""
+    from tidegs_b200 import _lib
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    count = torch.full((1,), 7, dtype=torch.int64, device="cuda")
+    out = torch.full((4,), -99, dtype=torch.int64, device="cuda")
+    starts = torch.full((8,), -1, dtype=torch.int64, device="cuda")
+    assert lib.tgs_global_to_local_compact_noalloc(out.data_ptr(), count.data_ptr(), None, 0,
+                                                   starts.data_ptr(), 8, 512, stream) == 0
+    torch.cuda.synchronize()
+    assert int(count.item()) == 0 and torch.all(out == -99)
+    gids, starts, bs = _inputs(MAX_IDS, 3)
+    expect = _with_caller_scratch(lib, gids, starts, bs, stream)
+    got = _no_alloc(lib, gids, starts, bs, stream)
+    assert expect.numel() > MAX_IDS // 3
+    assert torch.equal(got, expect)
+    del gids, starts
+
+
 def test_no_alloc_rejects_sizes_beyond_its_fixed_scratch():
     from tidegs_b200 import _lib
 

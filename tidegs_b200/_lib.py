@@ -47,6 +47,7 @@ class ResidentCountArgs(C.Structure):
         ("block_size", _i64), ("param_rows", _i64), ("local_ids", _vp), ("n_rows", _i64),
         ("slot_step", _vp), ("slot_stamp", _vp), ("slot_bias", _vp), ("step_table", _vp),
         ("step_table_len", _i32), ("n_slots", _i32), ("pos_count", _vp), ("err", _vp),
+        ("chunk_table", _vp),
     ]
 
 
@@ -58,6 +59,7 @@ class ResidentAdamArgs(C.Structure):
         ("batch_size", _f32), ("pos_start", _vp), ("pos_end", _vp), ("pos_slot", _vp),
         ("n_positions", _i32), ("block_size", _i64), ("local_ids", _vp), ("n_rows", _i64),
         ("state", _vp), ("slot_stamp", _vp), ("slot_bias", _vp), ("err", _vp),
+        ("chunk_table", _vp),
     ]
 
 

@@ -148,6 +148,12 @@ def fill_global_ids(dst: torch.Tensor, offset: int, block_ids: torch.Tensor, n_r
                     block_size: int) -> None:
     if n_rows == 0:
         return
+    if offset < 0 or offset + n_rows > dst.numel() or not dst.is_contiguous():
+        raise ValueError(f"fill_global_ids: rows [{offset}, {offset + n_rows}) outside a "
+                         f"{dst.numel()}-row destination")
+    if block_ids.numel() * block_size < n_rows:
+        raise ValueError(f"fill_global_ids: {block_ids.numel()} block ids cannot cover "
+                         f"{n_rows} rows of {block_size}")
     _lib.call("tgs_fill_global_ids", dst.data_ptr(), int(offset), block_ids.data_ptr(),
               int(n_rows), int(block_size), _stream(dst.device))
 

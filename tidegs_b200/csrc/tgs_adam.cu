@@ -45,9 +45,35 @@ __device__ __forceinline__ int find_position(const int64_t* __restrict__ pos_sta
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) resident_count_kernel(
     const int64_t* __restrict__ ids, int64_t n, int64_t param_rows,
-    const int64_t* __restrict__ pos_start, const int64_t* __restrict__ pos_end, int n_pos,
-    int64_t block_size, int32_t* __restrict__ pos_count, int32_t* __restrict__ err) {
+    const int64_t* __restrict__ pos_start, const int64_t* __restrict__ pos_end,
+    const int32_t* __restrict__ pos_slot, int n_pos, int64_t block_size,
+    int32_t* __restrict__ pos_count, int64_t* __restrict__ chunk_table,
+    int32_t* __restrict__ err) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  // A warp covers the 32-row chunk i / 32 (256-thread blocks): it records in
+  // the chunk table whether the chunk can be streamed by bulk copies.
+  if (chunk_table != nullptr) {
+    const int lane = threadIdx.x & 31;
+    int64_t id = -1, sr = -1;
+    if (i < n) {
+      id = ids[i];
+      if (id >= 0 && id < param_rows) {
+        const int p = find_position(pos_start, pos_end, n_pos, block_size, id);
+        if (p < n_pos && __ldg(pos_start + p) <= id)
+          sr = static_cast<int64_t>(__ldg(pos_slot + p)) * block_size + (id - __ldg(pos_start + p));
+      }
+    }
+    const unsigned full = 0xffffffffu;
+    const int64_t id0 = __shfl_sync(full, id, 0);
+    const int64_t sr0 = __shfl_sync(full, sr, 0);
+    const bool stream =
+        __all_sync(full, sr >= 0 && id == id0 + lane && sr == sr0 + lane) != 0 && (id0 & 3) == 0;
+    if (lane == 0 && i < n) {
+      const int64_t chunk = i >> 5;
+      chunk_table[2 * chunk] = stream ? id0 : -1;
+      chunk_table[2 * chunk + 1] = stream ? sr0 : -1;
+    }
+  }
   if (i >= n) return;
   int p = -1;
   const int64_t id = ids[i];
@@ -127,7 +153,13 @@ struct ResidentApplyParams {
   const uint32_t* slot_stamp;
   const float2* slot_bias;  // (1/(1-b1^t), sqrt(1-b2^t)) per slot
   const int32_t* err;
+  // [chunks][2] from the count kernel, or null: chunks marked kChunkDone
+  // were updated by the streaming kernel and are skipped
+  int64_t* chunk_table;
 };
+
+// Chunk-table entry (second word) of a chunk the streaming kernel updated.
+constexpr int64_t kChunkDone = -2;
 
 // Occupancy target (CTAs per SM) and rows in flight per warp of the update
 // kernel; overridable at build time for tuning sweeps.
@@ -283,7 +315,17 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
   const int64_t warp_id = static_cast<int64_t>(blockIdx.x) * kApplyWarps + warp;
   const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kApplyWarps;
 
-  for (int64_t chunk = warp_id; chunk * 32 < a.n; chunk += warp_stride) {
+  for (int64_t base = warp_id; base * 32 < a.n; base += 32 * warp_stride) {
+   // lane l looks at chunk base + l * warp_stride; the warp then updates the
+   // chunks the streaming kernel left
+   const int64_t mine = base + lane * warp_stride;
+   const bool todo = mine * 32 < a.n &&
+                     !(a.chunk_table != nullptr && a.chunk_table[2 * mine + 1] == kChunkDone);
+   uint32_t pending_chunks = __ballot_sync(full, todo);
+   while (pending_chunks != 0) {
+    const int pick = __ffs(pending_chunks) - 1;
+    pending_chunks &= pending_chunks - 1;
+    const int64_t chunk = base + pick * warp_stride;
     const int64_t row0 = chunk * 32;
     const int nr = static_cast<int>(min64(32, a.n - row0));
 
@@ -438,6 +480,7 @@ __global__ void __launch_bounds__(kApplyThreads, kApplyMinBlocks) resident_adam_
       }
     }
     __syncwarp();  // the table is rewritten by the next chunk
+   }
   }
 }
 
@@ -538,8 +581,17 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
   const int64_t warp_stride = static_cast<int64_t>(gridDim.x) * kApplyWarps;
 
   const int64_t n_chunks = (a.n + 31) / 32;
-  for (int64_t c = warp_id; c < n_chunks; c += warp_stride) {
-    int64_t chunk = c + q.rotate_chunks;
+  for (int64_t base = warp_id; base < n_chunks; base += 32 * warp_stride) {
+   const int64_t cl = base + lane * warp_stride;
+   int64_t mine = cl + q.rotate_chunks;
+   if (mine >= n_chunks) mine -= n_chunks;
+   const bool todo = cl < n_chunks &&
+                     !(a.chunk_table != nullptr && a.chunk_table[2 * mine + 1] == kChunkDone);
+   uint32_t pending_chunks = __ballot_sync(full, todo);
+   while (pending_chunks != 0) {
+    const int pick = __ffs(pending_chunks) - 1;
+    pending_chunks &= pending_chunks - 1;
+    int64_t chunk = base + pick * warp_stride + q.rotate_chunks;
     if (chunk >= n_chunks) chunk -= n_chunks;
     const int64_t row0 = chunk * 32;
     const int nr = static_cast<int>(min64(32, a.n - row0));
@@ -837,7 +889,436 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
       }
     }
     __syncwarp();
+   }
   }
+}
+
+// ---------------------------------------------------------------------------
+// Kernels D / D': the update of streamable chunks as a bulk-copy pipeline.
+// A chunk streams when its 32 ids and its 32 state rows both run
+// consecutively and its first id is a multiple of 4 (the count kernel's
+// chunk table): every chunk of a step that updates whole visible blocks. One
+// CTA per SM walks a contiguous range of chunks with three warp roles:
+//   loader    brings a chunk's 32 state rows (16 KB), six parameter segments
+//             and six gradient segments (7.4 KB each; D': the first two
+//             contributions' segments, read from the senders' memory) into a
+//             shared-memory stage with non-multicast bulk copies, S stages
+//             ahead, plus the rows' slot scales;
+//   consumers update the stage in shared memory (16 warps, 2 rows each;
+//             lane l: UNIFIED columns l and l + 32 of a row);
+//   storer    writes the stage's parameters and state rows back with bulk
+//             stores once the consumers are done, and frees the stage for
+//             the loader when the stores have read it.
+// A chunk costs a few large copies instead of 32 rows of per-lane loads
+// whose latency the warps would have to hide. Chunks it updates are marked
+// kChunkDone in the chunk table; kernels C / C' take the rest. Every wait is
+// bounded: on a timeout the kernel records TGS_DEV_WAIT_TIMEOUT, waits
+// (bounded) for its copies in flight and exits.
+// ---------------------------------------------------------------------------
+constexpr int kTileRows = 32;
+constexpr int kStreamConsumerWarps = 16;
+constexpr int kLoaderWarp = kStreamConsumerWarps;
+constexpr int kStorerWarp = kStreamConsumerWarps + 1;
+constexpr int kStreamThreads = (kStreamConsumerWarps + 2) * 32;
+constexpr int kRowsPerConsumer = kTileRows / kStreamConsumerWarps;
+#ifndef TGS_STREAM_STAGES
+#define TGS_STREAM_STAGES 6
+#endif
+#ifndef TGS_SUM_STREAM_STAGES
+#define TGS_SUM_STREAM_STAGES 5
+#endif
+// CTAs per SM of the streaming kernels (the stages of all of them share the
+// SM's shared memory)
+#ifndef TGS_STREAM_CTAS
+#define TGS_STREAM_CTAS 1
+#endif
+#ifndef TGS_SUM_STREAM_CTAS
+#define TGS_SUM_STREAM_CTAS 1
+#endif
+constexpr int kStateTileBytes = kTileRows * TGS_STATE_ROW_FLOATS * 4;  // 16 KB
+constexpr int kRowTileBytes = kTileRows * kRowWidth * 4;                // 7552 B
+
+struct __align__(16) StreamDesc {
+  int64_t chunk;     // < 0: the CTA has no further chunk
+  int64_t first_id;  // local row of the chunk's first row
+  int64_t first_sr;  // state row of the chunk's first row
+  int64_t seg_off;   // D': offset of the chunk's first row in its segment
+  int32_t cb, cn;    // D': first contribution and contribution count of the segment
+  int32_t ns;        // D': contributions staged in shared memory (<= kGrads)
+  int32_t pad;
+};
+
+// One pipeline stage: a chunk's state rows, parameters (component c at
+// kTileRows * unified_offset(c), rows contiguous) and kGrads gradient tiles
+// of the same layout, plus the chunk's per-row slot scales.
+template <int kGrads>
+struct __align__(128) StreamStage {
+  float state[kTileRows * TGS_STATE_ROW_FLOATS];
+  float param[kTileRows * kRowWidth];
+  float grad[kGrads][kTileRows * kRowWidth];
+  RowScale scale[kTileRows];
+  StreamDesc desc;
+};
+
+template <int kGrads, int kStages>
+constexpr int stream_smem_bytes() {
+  return kStages * static_cast<int>(sizeof(StreamStage<kGrads>)) + 3 * kStages * 8;
+}
+
+// Bulk loads of the six component segments of a chunk into a row tile:
+// component c's kTileRows rows at kTileRows * unified_offset(c).
+template <typename Src>
+__device__ __forceinline__ void load_row_tile(float* dst, const Src (&src)[kNumComp], int64_t row,
+                                              uint64_t* bar) {
+#pragma unroll
+  for (int c = 0; c < kNumComp; ++c)
+    bulk_g2s(dst + kTileRows * unified_offset(c), src[c] + row * comp_width(c),
+             kTileRows * comp_width(c) * 4, bar);
+}
+
+template <int kGrads>
+__device__ __forceinline__ void store_tile(const ResidentApplyParams& a, StreamStage<kGrads>& st) {
+  const int64_t fid = st.desc.first_id;
+  bulk_s2g(a.state + st.desc.first_sr * (TGS_STATE_ROW_FLOATS / 4), st.state, kStateTileBytes);
+#pragma unroll
+  for (int c = 0; c < kNumComp; ++c)
+    bulk_s2g(a.param[c] + fid * comp_width(c), st.param + kTileRows * unified_offset(c),
+             kTileRows * comp_width(c) * 4);
+}
+
+// Per-lane column binding of the consumer warps: UNIFIED column j.
+struct StreamCol {
+  int base;   // kTileRows * unified_offset(c) + k
+  int width;  // w_c
+  int comp;
+  int col;    // k
+  float lr;
+};
+
+__device__ __forceinline__ StreamCol stream_col(const float (&lrs)[kNumComp], int j) {
+  StreamCol sc;
+  const int c = unified_comp_of(j);
+  sc.comp = c;
+  sc.col = j - unified_offset(c);
+  sc.width = comp_width(c);
+  sc.base = kTileRows * unified_offset(c) + sc.col;
+  sc.lr = pick6(lrs, c);
+  return sc;
+}
+
+// The loader's scan of its CTA's chunk range: the next chunk whose table
+// entry marks it streamable (32 entries examined per load, lane-parallel).
+struct ChunkScan {
+  int64_t next, end, base;
+  uint32_t mask;
+  int64_t id, sr;  // this lane's entry of the current window
+};
+
+__device__ __forceinline__ int64_t scan_next(ChunkScan& cs, const int64_t* table, int lane,
+                                             int64_t& fid, int64_t& fsr) {
+  const unsigned full = 0xffffffffu;
+  while (true) {
+    if (cs.mask == 0) {
+      if (cs.next >= cs.end) return -1;
+      const int64_t c = cs.next + lane;
+      cs.id = -1;
+      cs.sr = -1;
+      if (c < cs.end) {
+        cs.id = table[2 * c];
+        cs.sr = table[2 * c + 1];
+      }
+      cs.mask = __ballot_sync(full, cs.sr >= 0);
+      cs.base = cs.next;
+      cs.next += 32;
+      continue;
+    }
+    const int b = __ffs(cs.mask) - 1;
+    cs.mask &= cs.mask - 1;
+    fid = __shfl_sync(full, cs.id, b);
+    fsr = __shfl_sync(full, cs.sr, b);
+    return cs.base + b;
+  }
+}
+
+// Consumer update of UNIFIED column j of stage row r: the gradient is the
+// first staged tile (D: the chunk's gradient; D': contribution 0), plus, for
+// D', the second staged contribution and then any further ones read from the
+// senders' memory one by one, in the segment's (rank) order.
+template <bool kPow2Batch, bool kSum>
+__device__ __forceinline__ void stream_update_col(float* param, const float* g0t,
+                                                  const float* g1t, const StreamDesc& d,
+                                                  const ResidentSumParams* q, float2* srow,
+                                                  const StreamCol& sc, int r, int j, bool fresh,
+                                                  const RowScale& rs, const AdamScalars& hp) {
+  const int idx = sc.base + r * sc.width;
+  float p = param[idx];
+  float g = g0t[idx];
+  if constexpr (kSum) {
+    if (d.ns > 1) g = fadd(g, g1t[idx]);
+    for (int jj = d.ns; jj < d.cn; ++jj) {
+      const int k = d.cb + jj;
+      const int rk = __ldg(q->contrib_rank + k);
+      const int64_t srow_src = __ldg(q->contrib_row + k) + d.seg_off + r;
+      float x = 0.f;
+      if (rk < 0 || rk >= q->n_ranks || srow_src < 0 || srow_src >= __ldg(q->grad_rows + rk))
+        report_error(q->err, TGS_DEV_BAD_SLICE, k, rk);
+      else
+        x = q->grad_src[rk * kNumComp + sc.comp][srow_src * sc.width + sc.col];
+      g = fadd(g, x);
+    }
+  }
+  const float2 mv = srow[j];
+  float m = fresh ? mv.x : 0.f, v = fresh ? mv.y : 0.f;
+  adam_elem<kPow2Batch>(p, m, v, g, hp, fmul(rs.rb1, sc.lr), rs.ds);
+  param[idx] = p;
+  srow[j] = make_float2(m, v);
+}
+
+template <bool kPow2Batch, bool kSum>
+__device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentSumParams* q) {
+  constexpr int kGrads = kSum ? 2 : 1;
+  constexpr int kStages = kSum ? TGS_SUM_STREAM_STAGES : TGS_STREAM_STAGES;
+  using Stage = StreamStage<kGrads>;
+  extern __shared__ __align__(128) unsigned char stream_smem[];
+  Stage* stages = reinterpret_cast<Stage*>(stream_smem);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(stages + kStages);  // loader -> all
+  uint64_t* done_bar = full_bar + kStages;                              // consumers -> storer
+  uint64_t* empty_bar = done_bar + kStages;                             // storer -> loader
+  __shared__ int s_skip;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const unsigned full = 0xffffffffu;
+  int32_t* err = const_cast<int32_t*>(a.err);
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kStages; ++st) {
+      mbar_init(&full_bar[st], 32);
+      mbar_init(&done_bar[st], kStreamConsumerWarps);
+      mbar_init(&empty_bar[st], 1);
+    }
+    fence_mbar_init();
+    s_skip = load_error(a.err);
+  }
+  __syncthreads();
+  if (s_skip != 0) return;
+
+  if (warp == kLoaderWarp) {
+    // ------------------------------- loader -------------------------------
+    const int64_t n_chunks = a.n / kTileRows;  // only full chunks stream
+    ChunkScan cs;
+    cs.next = n_chunks * blockIdx.x / gridDim.x;
+    cs.end = n_chunks * (blockIdx.x + 1) / gridDim.x;
+    cs.base = 0;
+    cs.mask = 0;
+    cs.id = cs.sr = -1;
+    const int64_t B = a.block_size;
+    const bool pow2B = (B & (B - 1)) == 0;
+    const int shiftB = __ffsll(B) - 1;
+    // D': the segment of the last chunk looked at, cached (lane 0)
+    int64_t seg_lo = 0, seg_hi = -1, src_row0 = 0, src_row1 = 0;
+    int32_t seg_cb = 0, seg_cn = 0, src_rank0 = 0, src_rank1 = 0;
+    bool seg_ok = false;
+    bool failed = false;
+    int64_t t = 0;
+    for (;; ++t) {
+      const int st = static_cast<int>(t % kStages);
+      const uint32_t use = static_cast<uint32_t>(t / kStages);
+      Stage& S = stages[st];
+      int64_t chunk, fid = 0, fsr = 0;
+      int32_t ns = 0;
+      int64_t seg_off = 0;
+      while (true) {
+        chunk = scan_next(cs, a.chunk_table, lane, fid, fsr);
+        if (chunk < 0 || !kSum) break;
+        // D': the chunk must lie in one segment whose first kGrads
+        // contributions can be bulk-copied (in range, 16-byte aligned)
+        int ok = 0;
+        if (lane == 0) {
+          const int64_t row0 = chunk * kTileRows;
+          if (row0 < seg_lo || row0 >= seg_hi) {
+            const int sg = upper_bound_i64(q->seg_begin + 1, q->n_seg, row0);
+            seg_ok = false;
+            seg_hi = -1;
+            if (sg < q->n_seg && __ldg(q->seg_begin + sg) <= row0) {
+              seg_lo = __ldg(q->seg_begin + sg);
+              seg_hi = __ldg(q->seg_begin + sg + 1);
+              seg_cb = static_cast<int32_t>(__ldg(q->contrib_offsets + sg));
+              seg_cn = static_cast<int32_t>(__ldg(q->contrib_offsets + sg + 1)) - seg_cb;
+              seg_ok = seg_cn >= 1;
+              for (int jj = 0; jj < kGrads && jj < seg_cn; ++jj) {
+                const int r = __ldg(q->contrib_rank + seg_cb + jj);
+                const int64_t row = __ldg(q->contrib_row + seg_cb + jj);
+                if (jj == 0) {
+                  src_rank0 = r;
+                  src_row0 = row;
+                } else {
+                  src_rank1 = r;
+                  src_row1 = row;
+                }
+                if (r < 0 || r >= q->n_ranks) {
+                  seg_ok = false;
+                  continue;
+                }
+                for (int c = 0; c < kNumComp; ++c)
+                  if (!aligned16(q->grad_src[r * kNumComp + c])) seg_ok = false;
+              }
+            }
+          }
+          if (seg_ok && row0 + kTileRows <= seg_hi) {
+            ok = 1;
+            const int nst = seg_cn < kGrads ? seg_cn : kGrads;
+            for (int jj = 0; jj < nst; ++jj) {
+              const int64_t srow = (jj == 0 ? src_row0 : src_row1) + (row0 - seg_lo);
+              const int rk = jj == 0 ? src_rank0 : src_rank1;
+              if (srow < 0 || (srow & 3) != 0 || srow + kTileRows > __ldg(q->grad_rows + rk))
+                ok = 0;
+            }
+          }
+        }
+        if (__shfl_sync(full, ok, 0) != 0) {
+          ns = __shfl_sync(full, seg_cn < kGrads ? seg_cn : kGrads, 0);
+          seg_off = __shfl_sync(full, chunk * kTileRows - seg_lo, 0);
+          break;
+        }
+      }
+      // the chunk's row scales start loading before the wait for the stage
+      float2 bb = make_float2(0.f, 0.f);
+      uint32_t stamp = 0;
+      if (chunk >= 0) {
+        const int64_t sr = fsr + lane;
+        const int64_t slot = pow2B ? (sr >> shiftB) : sr / B;
+        bb = a.slot_bias[slot];
+        stamp = __ldg(a.slot_stamp + slot);
+      }
+      if (t >= kStages) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait_bounded(&empty_bar[st], (use - 1) & 1u) ? 1 : 0;
+        if (__shfl_sync(full, ok, 0) == 0) {
+          failed = true;
+          break;
+        }
+      }
+      if (chunk < 0) {
+        if (lane == 0) S.desc.chunk = -1;
+        __syncwarp();
+        mbar_arrive(&full_bar[st]);  // completes the phase without bytes
+        break;
+      }
+      if (lane == 0) {
+        S.desc.chunk = chunk;
+        S.desc.first_id = fid;
+        S.desc.first_sr = fsr;
+        S.desc.ns = ns;
+        const uint32_t bytes = kStateTileBytes + kRowTileBytes * (1 + (kSum ? ns : 1));
+        mbar_expect_tx(&full_bar[st], bytes);
+        bulk_g2s(S.state, a.state + fsr * (TGS_STATE_ROW_FLOATS / 4), kStateTileBytes,
+                 &full_bar[st]);
+        load_row_tile(S.param, a.param, fid, &full_bar[st]);
+        if constexpr (kSum) {
+          S.desc.cb = seg_cb;
+          S.desc.cn = seg_cn;
+          S.desc.seg_off = seg_off;
+          for (int jj = 0; jj < ns; ++jj) {
+            const float* const* src = q->grad_src + (jj == 0 ? src_rank0 : src_rank1) * kNumComp;
+            const int64_t srow = (jj == 0 ? src_row0 : src_row1) + seg_off;
+#pragma unroll
+            for (int c = 0; c < kNumComp; ++c)
+              bulk_g2s(S.grad[jj] + kTileRows * unified_offset(c), src[c] + srow * comp_width(c),
+                       kTileRows * comp_width(c) * 4, &full_bar[st]);
+          }
+        } else {
+          load_row_tile(S.grad[0], a.grad, chunk * kTileRows, &full_bar[st]);
+        }
+        a.chunk_table[2 * chunk + 1] = kChunkDone;
+      }
+      S.scale[lane] = {bb.x, bb.y, stamp, 0u};
+      // the 32 arrivals publish the descriptor and the row scales; the phase
+      // completes when the copies' bytes have landed as well
+      mbar_arrive(&full_bar[st]);
+      __syncwarp();
+    }
+    if (failed && lane == 0) {
+      report_error(err, TGS_DEV_WAIT_TIMEOUT, t);
+      // loads still in flight land before the CTA may exit
+      for (int64_t j = t - kStages; j < t; ++j)
+        if (j >= 0)
+          (void)mbar_wait_bounded(&full_bar[j % kStages], static_cast<uint32_t>(j / kStages) & 1u);
+    }
+    return;
+  }
+
+  if (warp == kStorerWarp) {
+    // ------------------------------- storer -------------------------------
+    for (int64_t t = 0;; ++t) {
+      const int st = static_cast<int>(t % kStages);
+      const uint32_t par = static_cast<uint32_t>(t / kStages) & 1u;
+      Stage& S = stages[st];
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait_bounded(&full_bar[st], par) ? 1 : 0;
+        if (ok && S.desc.chunk < 0) ok = 2;  // no further chunk
+        if (ok == 1) ok = mbar_wait_bounded(&done_bar[st], par) ? 1 : 0;
+        if (ok == 1) {
+          store_tile(a, S);
+          bulk_commit();
+          bulk_wait_read<0>();  // the stage may be overwritten from here on
+          mbar_arrive(&empty_bar[st]);
+        }
+        if (ok == 0) report_error(err, TGS_DEV_WAIT_TIMEOUT, t);
+      }
+      if (__shfl_sync(full, ok, 0) != 1) break;
+    }
+    if (lane == 0) bulk_wait_all();
+    return;
+  }
+
+  // ------------------------------ consumers ------------------------------
+  const AdamScalars hp = {a.beta1, a.beta2, a.omb1, a.omb2, a.eps, a.batch_size, a.inv_batch_size};
+  const StreamCol c0 = stream_col(a.lr, lane);
+  const bool has1 = lane + 32 < kRowWidth;
+  const StreamCol c1 = stream_col(a.lr, has1 ? lane + 32 : 0);
+  for (int64_t t = 0;; ++t) {
+    const int st = static_cast<int>(t % kStages);
+    Stage& S = stages[st];
+    if (!mbar_wait_bounded(&full_bar[st], static_cast<uint32_t>(t / kStages) & 1u)) {
+      if (lane == 0) report_error(err, TGS_DEV_WAIT_TIMEOUT, t);
+      break;
+    }
+    if (S.desc.chunk < 0) break;
+    const StreamDesc d = S.desc;
+    const float* g1t = S.grad[kGrads - 1];
+#pragma unroll
+    for (int u = 0; u < kRowsPerConsumer; ++u) {
+      const int r = warp * kRowsPerConsumer + u;
+      const RowScale rs = S.scale[r];
+      float* srow_f = S.state + r * TGS_STATE_ROW_FLOATS;
+      float2* srow = reinterpret_cast<float2*>(srow_f);
+      // a row whose stamp is not its slot's current stamp has not been
+      // touched since the block was (re)admitted: its moments are zero
+      const bool fresh = __float_as_uint(srow_f[124]) == rs.stamp;
+      stream_update_col<kPow2Batch, kSum>(S.param, S.grad[0], g1t, d, q, srow, c0, r, lane,
+                                          fresh, rs, hp);
+      if (has1)
+        stream_update_col<kPow2Batch, kSum>(S.param, S.grad[0], g1t, d, q, srow, c1, r,
+                                            lane + 32, fresh, rs, hp);
+      __syncwarp();  // every lane has read the stamp
+      if (lane == 30) srow_f[124] = __uint_as_float(rs.stamp);
+    }
+    fence_proxy_async_smem();  // this warp's writes, before the bulk stores read them
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&done_bar[st]);
+  }
+}
+
+template <bool kPow2Batch>
+__global__ void __launch_bounds__(kStreamThreads, TGS_STREAM_CTAS)
+    resident_adam_stream_kernel(const ResidentApplyParams a) {
+  stream_kernel_body<kPow2Batch, false>(a, nullptr);
+}
+
+template <bool kPow2Batch>
+__global__ void __launch_bounds__(kStreamThreads, TGS_SUM_STREAM_CTAS)
+    resident_adam_sum_stream_kernel(const ResidentSumParams q) {
+  stream_kernel_body<kPow2Batch, true>(q.a, &q);
 }
 
 // ---------------------------------------------------------------------------
@@ -1053,8 +1534,8 @@ extern "C" int tgs_resident_adam_count(const TgsResidentCountArgs* a, void* stre
   const int64_t blocks = ceil_div<int64_t>(a->n_rows, 256);
   TGS_CHECK_ARG(blocks < (1ll << 31), "tgs_resident_adam_count: n_rows too large");
   resident_count_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
-      a->local_ids, a->n_rows, a->param_rows, a->pos_start, a->pos_end, a->n_positions,
-      a->block_size, a->pos_count, a->err);
+      a->local_ids, a->n_rows, a->param_rows, a->pos_start, a->pos_end, a->pos_slot,
+      a->n_positions, a->block_size, a->pos_count, a->chunk_table, a->err);
   TGS_LAUNCH_CHECK();
   resident_slot_kernel<<<ceil_div(a->n_positions, 256), 256, 0, s>>>(
       a->pos_count, a->pos_slot, a->n_positions, a->slot_step,
@@ -1105,6 +1586,45 @@ int fill_apply_params(const TgsResidentAdamArgs* a, bool need_grad, const char* 
   p->slot_stamp = a->slot_stamp;
   p->slot_bias = reinterpret_cast<const float2*>(a->slot_bias);
   p->err = a->err;
+  p->chunk_table = a->chunk_table;
+  return TGS_OK;
+}
+
+// Whether the bulk-copy pipeline may run: a chunk table, at least one full
+// chunk, and 16-byte aligned parameter (and, for the single-GPU update,
+// gradient) components.
+bool can_stream(const ResidentApplyParams& p, bool need_grad) {
+  if (p.chunk_table == nullptr || p.n < kTileRows) return false;
+  for (int c = 0; c < kNumComp; ++c) {
+    if (!aligned16(p.param[c])) return false;
+    if (need_grad && !aligned16(p.grad[c])) return false;
+  }
+  return true;
+}
+
+int stream_grid(int64_t n_rows, int ctas_per_sm) {
+  const int64_t chunks = n_rows / kTileRows;
+  return static_cast<int>(std::min<int64_t>(chunks, int64_t(sm_count()) * ctas_per_sm));
+}
+
+// Launches a streaming kernel, raising its dynamic shared-memory limit on
+// first use on the current device.
+template <typename Kernel, typename Params>
+int launch_stream(Kernel kernel, const Params& p, int smem, int grid, cudaStream_t s,
+                  bool* configured) {
+  static std::mutex mu;
+  int dev = 0;
+  TGS_CUDA(cudaGetDevice(&dev));
+  TGS_CHECK_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      TGS_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      configured[dev] = true;
+    }
+  }
+  kernel<<<grid, kStreamThreads, smem, s>>>(p);
+  TGS_LAUNCH_CHECK();
   return TGS_OK;
 }
 
@@ -1168,9 +1688,19 @@ extern "C" int tgs_resident_adam_apply(const TgsResidentAdamArgs* a, void* strea
   bool pow2 = false;
   const int rc = fill_apply_params(a, true, "tgs_resident_adam_apply", &p, &pow2);
   if (rc != TGS_OK) return rc;
+  cudaStream_t s = as_stream(stream);
+  if (can_stream(p, true)) {
+    static bool configured[2][64] = {};
+    constexpr int smem = stream_smem_bytes<1, TGS_STREAM_STAGES>();
+    const int sgrid = stream_grid(a->n_rows, TGS_STREAM_CTAS);
+    const int rc2 = pow2 ? launch_stream(resident_adam_stream_kernel<true>, p, smem, sgrid, s,
+                                         configured[1])
+                         : launch_stream(resident_adam_stream_kernel<false>, p, smem, sgrid, s,
+                                         configured[0]);
+    if (rc2 != TGS_OK) return rc2;
+  }
   const int grid = apply_grid(a->n_rows);
-  return pow2 ? launch_apply<true>(p, grid, as_stream(stream))
-              : launch_apply<false>(p, grid, as_stream(stream));
+  return pow2 ? launch_apply<true>(p, grid, s) : launch_apply<false>(p, grid, s);
 }
 
 extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void* stream) {
@@ -1199,9 +1729,19 @@ extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void
   TGS_CHECK_ARG(a->rotate_rows >= 0, "tgs_resident_adam_apply_sum: rotate_rows < 0");
   q.rotate_chunks = (a->rotate_rows / 32) % n_chunks;
   q.err = a->err;
+  cudaStream_t s = as_stream(stream);
+  if (can_stream(q.a, false)) {
+    static bool configured[2][64] = {};
+    constexpr int smem = stream_smem_bytes<2, TGS_SUM_STREAM_STAGES>();
+    const int sgrid = stream_grid(a->adam.n_rows, TGS_SUM_STREAM_CTAS);
+    const int rc2 = pow2 ? launch_stream(resident_adam_sum_stream_kernel<true>, q, smem, sgrid, s,
+                                         configured[1])
+                         : launch_stream(resident_adam_sum_stream_kernel<false>, q, smem, sgrid,
+                                         s, configured[0]);
+    if (rc2 != TGS_OK) return rc2;
+  }
   const int grid = apply_grid(a->adam.n_rows, kSumMinBlocks);
-  return pow2 ? launch_sum<true>(q, grid, as_stream(stream))
-              : launch_sum<false>(q, grid, as_stream(stream));
+  return pow2 ? launch_sum<true>(q, grid, s) : launch_sum<false>(q, grid, s);
 }
 
 extern "C" int tgs_selective_adam(const TgsDenseArgs* args, void* stream) {

@@ -550,13 +550,30 @@ __global__ void __launch_bounds__(kBoundsThreads) bounds_kernel(const float* __r
     const int64_t n = count[k];
     float lo[3] = {INFINITY, INFINITY, INFINITY};
     float hi[3] = {-INFINITY, -INFINITY, -INFINITY};
-    for (int64_t r = threadIdx.x; r < n; r += kBoundsThreads) {
-#pragma unroll
-      for (int ax = 0; ax < 3; ++ax) {
-        const float x = xyz[(s + r) * 3 + ax];
-        lo[ax] = fminf(lo[ax], x);
-        hi[ax] = fmaxf(hi[ax], x);
+    auto take = [&](int ax, float x) {
+      lo[ax] = fminf(lo[ax], x);
+      hi[ax] = fmaxf(hi[ax], x);
+    };
+    int64_t r0 = 0;
+    if ((s & 3) == 0 && (reinterpret_cast<uintptr_t>(xyz) & 15u) == 0) {
+      // 4 rows = 12 floats = 3 float4 whose lanes hold axes x y z x | y z x y
+      // | z x y z: a thread takes whole 4-row groups, so every lane of each
+      // of its vector loads has a fixed axis
+      const float4* g4 = reinterpret_cast<const float4*>(xyz + s * 3);
+      const int64_t groups = n / 4;
+      for (int64_t q = threadIdx.x; q < groups; q += kBoundsThreads) {
+        const float4 a = __ldg(g4 + 3 * q);
+        const float4 b = __ldg(g4 + 3 * q + 1);
+        const float4 c = __ldg(g4 + 3 * q + 2);
+        take(0, a.x); take(1, a.y); take(2, a.z); take(0, a.w);
+        take(1, b.x); take(2, b.y); take(0, b.z); take(1, b.w);
+        take(2, c.x); take(0, c.y); take(1, c.z); take(2, c.w);
       }
+      r0 = groups * 4;
+    }
+    for (int64_t r = r0 + threadIdx.x; r < n; r += kBoundsThreads) {
+#pragma unroll
+      for (int ax = 0; ax < 3; ++ax) take(ax, xyz[(s + r) * 3 + ax]);
     }
 #pragma unroll
     for (int ax = 0; ax < 3; ++ax) {
@@ -780,7 +797,9 @@ int64_t* g_noalloc_scratch_ptr[64] = {nullptr};
 // Device address of the fixed scratch array on the current device. Host code
 // must not use the array's name as a device pointer: it is only a host-side
 // stand-in, so the address is looked up once per device, with that device
-// current.
+// current, and kept for the life of the process. A cudaDeviceReset (or any
+// new primary context on the device) invalidates it; the entry point's
+// contract rules calls after one out.
 int noalloc_scratch(int64_t** out) {
   int dev = -1;
   TGS_CUDA(cudaGetDevice(&dev));

@@ -147,10 +147,11 @@ class DoubleBufferGPUWorkingSet:
                                                           thread_name_prefix="tide-resident-plan")
         self._resident_plan_future: Optional[Future] = None
         self._executor_shutdown = False
-        self._host_staging_slots: List[Optional[torch.Tensor]] = [None, None]
-        self._gpu_staging_slots: List[Optional[torch.Tensor]] = [None, None]
-        self._host_staging_capacities = [0, 0]
-        self._host_staging_events: List[Optional[torch.cuda.Event]] = [None, None]
+        # two rotating host/device staging slots (double_buffer_gpu.py:748-809)
+        self._host_staging_slots: List[Optional[torch.Tensor]] = [None] * 2
+        self._gpu_staging_slots: List[Optional[torch.Tensor]] = [None] * 2
+        self._host_staging_capacities = [0] * 2
+        self._host_staging_events: List[Optional[torch.cuda.Event]] = [None] * 2
         self._next_host_staging_slot = 0
         # Bit-packed dirty bitmap: bit (id & 31) of word id >> 5.
         self._dirty_bitmap = torch.zeros(_ops.bitmap_words(self.num_blocks), dtype=torch.int32,
@@ -511,14 +512,20 @@ class DoubleBufferGPUWorkingSet:
             self.stats["resident_refresh_blocks"] += len(refresh_ids)
         return ResidentHandoffResult(ready_blocks=len(refresh_ids), copied_blocks=len(refresh_ids))
 
+    def _raise_if_prefetch_failed(self) -> None:
+        """Re-raises, on the caller's thread, an error the N+1 worker died of."""
+        job = self._prefetch_future
+        if job is not None and job.done() and job.exception() is not None:
+            raise job.exception()
+
     def _wait_for_target_layout(self) -> None:
-        while not self._target_layout_ready.wait(timeout=0.01):
-            prefetch_future = self._prefetch_future
-            if prefetch_future is not None and prefetch_future.done():
-                prefetch_future.result()
-        prefetch_future = self._prefetch_future
-        if prefetch_future is not None and prefetch_future.done():
-            prefetch_future.result()
+        """Blocks until the N+1 worker has published the loading buffer's
+        layout, polling for a failed worker every 10 ms."""
+        ready = self._target_layout_ready
+        while not ready.is_set():
+            self._raise_if_prefetch_failed()
+            ready.wait(timeout=0.01)
+        self._raise_if_prefetch_failed()
 
     def _fill_streamed_global_ids(self, target: GPUBuffer, block_ids: List[int],
                                   target_offset: int, num_rows: int) -> None:
@@ -747,6 +754,25 @@ class DoubleBufferGPUWorkingSet:
             ev.record(torch.cuda.current_stream(self.device))
             self.prefetch_events[name] = ev
 
+    def _open_prefetch(self, iteration: int) -> None:
+        """Retires a prefetch still in flight (waiting for it), then resets
+        the per-prefetch state for `iteration`."""
+        with self.lock:
+            running = self.prefetch_iteration if self.prefetch_in_progress else None
+        if running is not None:
+            self.wait_for_prefetch(running)
+        fresh = {
+            "prefetch_in_progress": True, "prefetch_iteration": iteration,
+            "prefetch_complete_event": torch.cuda.Event(),
+            "resident_refresh_complete_event": None, "_prefetch_finalized": False,
+            "_deferred_resident_blocks": [], "_persistent_plan": None,
+            "_before_persistent_apply": None,
+        }
+        with self.lock:
+            for name, value in fresh.items():
+                setattr(self, name, value)
+            self._target_layout_ready.clear()
+
     def start_prefetch(self, iteration: int, visible_block_ids: List[int],
                        filters_global: Optional[List[torch.Tensor]] = None,
                        ram_cache: Optional[Dict[str, torch.Tensor]] = None,
@@ -758,23 +784,7 @@ class DoubleBufferGPUWorkingSet:
                        defer_resident_copy: bool = False, before_target_reuse=None):
         """Starts the N+1 prefetch into the loading buffer; returns at once for
         block readers (double_buffer_gpu.py:1169-1454)."""
-        previous_iteration = None
-        with self.lock:
-            if self.prefetch_in_progress:
-                previous_iteration = self.prefetch_iteration
-        if previous_iteration is not None:
-            self.wait_for_prefetch(previous_iteration)
-
-        with self.lock:
-            self.prefetch_in_progress = True
-            self.prefetch_iteration = iteration
-            self.prefetch_complete_event = torch.cuda.Event()
-            self.resident_refresh_complete_event = None
-            self._prefetch_finalized = False
-            self._deferred_resident_blocks = []
-            self._target_layout_ready.clear()
-            self._persistent_plan = None
-            self._before_persistent_apply = None
+        self._open_prefetch(iteration)
 
         if block_reader is not None:
             sorted_visible = sorted(set(map(int, visible_block_ids)))
@@ -1052,28 +1062,33 @@ class DoubleBufferGPUWorkingSet:
         stats["active_blocks"] = len(self.active_buffer.loaded_blocks)
         return stats
 
+    def _reset_host_staging(self) -> None:
+        """Drops the two rotating host/device staging slots."""
+        self._host_staging_slots = [None] * 2
+        self._gpu_staging_slots = [None] * 2
+        self._host_staging_capacities = [0] * 2
+        self._host_staging_events = [None] * 2
+        self.stats.update(host_staging_bytes=0, host_staging_pinned=False)
+
     def clear(self):
-        if self._resident_plan_future is not None:
-            self._resident_plan_future.result()
-        if self._prefetch_future is not None:
-            self._prefetch_future.result()
-        self.prefetch_stream.synchronize()
-        self.resident_refresh_stream.synchronize()
+        """Finishes the worker jobs and both streams, stops the workers, then
+        releases the buffers and staging slots and forgets every dirty mark
+        (the reference's clear, double_buffer_gpu.py:1711-1731)."""
+        for job in (self._resident_plan_future, self._prefetch_future):
+            if job is not None:
+                job.result()
+        for stream in (self.prefetch_stream, self.resident_refresh_stream):
+            stream.synchronize()
         if not self._executor_shutdown:
-            self._prefetch_executor.shutdown(wait=True)
-            self._resident_plan_executor.shutdown(wait=True)
+            for pool in (self._prefetch_executor, self._resident_plan_executor):
+                pool.shutdown(wait=True)
             self._executor_shutdown = True
-        self.buffer_a.clear()
-        self.buffer_b.clear()
-        self._host_staging_slots = [None, None]
-        self._gpu_staging_slots = [None, None]
-        self._host_staging_capacities = [0, 0]
-        self._host_staging_events = [None, None]
+        for buf in (self.buffer_a, self.buffer_b):
+            buf.clear()
+        self._reset_host_staging()
         self._target_layout_ready.clear()
         self.resident_refresh_complete_event = None
         self._dirty_bitmap.zero_()
-        self.stats["host_staging_bytes"] = 0
-        self.stats["host_staging_pinned"] = False
         if torch.cuda.is_available():
             torch.cuda.empty_cache()
 

@@ -66,18 +66,14 @@ class GPUResidentAdam:
         if self.block_size <= 0:
             raise ValueError(f"[GPUResidentAdam] block_size must be positive, got {block_size}")
 
-        self._resident_blocks = set()
-        self._resident_streaks: Dict[int, int] = {}
-        self._completed_streak_total = 0
-        self._completed_streak_count = 0
-
-        # Slot allocator (host). The free list is popped from the end and seeded
-        # in descending order, so the lowest free slot is used first
-        # (gpu_resident_optimizer.py:204,254).
+        # Slot table (host, numpy): the block each optimizer slot holds (-1:
+        # free) and the number of consecutive resident sets that block has
+        # been in. Admissions take the lowest free slots; slot numbers are
+        # private to this class (the update is independent of them).
         self._allocated_slots = 0
-        self._block_to_slot: Dict[int, int] = {}
-        self._slot_to_block: List[Optional[int]] = []
-        self._free_slots: List[int] = []
+        self._slot_block = np.zeros(0, dtype=np.int64)
+        self._slot_streak = np.zeros(0, dtype=np.int64)
+        self._ended_streaks = [0, 0]  # (sum, count) of residencies that ended
         self._slot_steps = np.zeros(0, dtype=np.int64)         # host mirror of device steps
         self._slot_initialized = np.zeros(0, dtype=bool)
         self._slot_row_counts = np.zeros(0, dtype=np.int64)
@@ -95,6 +91,9 @@ class GPUResidentAdam:
         # Reusable buffers for the per-position count read-back.
         self._pin_counts: Optional[torch.Tensor] = None
         self._dev_counts: Optional[torch.Tensor] = None
+        # per 32-row chunk of the step's rows: (first local row, first state
+        # row) when the update can stream the chunk by bulk copies
+        self._chunk_table: Optional[torch.Tensor] = None
 
         self._logical_state_blocks = 0
         self._logical_state_bytes = 0
@@ -118,13 +117,33 @@ class GPUResidentAdam:
         return int(self._allocated_slots * self.block_size * _lib.STATE_ROW_FLOATS * 4)
 
     def _update_state_stats(self) -> None:
-        self._stats["resident_target_blocks"] = len(self._resident_blocks)
+        held = self._slot_block >= 0
+        n_held = int(np.count_nonzero(held))
+        self._stats["resident_target_blocks"] = n_held
         self._stats["resident_state_blocks"] = int(self._logical_state_blocks)
         self._stats["resident_state_bytes"] = int(self._logical_state_bytes)
         self._stats["allocated_state_bytes"] = self._physical_state_bytes()
-        streak_total = self._completed_streak_total + sum(self._resident_streaks.values())
-        streak_count = self._completed_streak_count + len(self._resident_streaks)
-        self._stats["mean_resident_streak"] = float(streak_total) / max(1, streak_count)
+        # mean residency length over ended residencies and the current ones
+        total = self._ended_streaks[0] + int(self._slot_streak[held].sum())
+        count = self._ended_streaks[1] + n_held
+        self._stats["mean_resident_streak"] = float(total) / max(1, count)
+
+    @property
+    def _block_to_slot(self) -> Dict[int, int]:
+        """{block id: slot} of the resident blocks."""
+        slots = np.nonzero(self._slot_block >= 0)[0]
+        return dict(zip(self._slot_block[slots].tolist(), slots.tolist()))
+
+    def _slots_of(self, block_ids: np.ndarray) -> np.ndarray:
+        """Slot of each block id, -1 where the block is not resident."""
+        slots = np.nonzero(self._slot_block >= 0)[0]
+        held = self._slot_block[slots]
+        order = np.argsort(held)
+        held, slots = held[order], slots[order]
+        at = np.minimum(np.searchsorted(held, block_ids), max(held.size - 1, 0))
+        found = held.size > 0
+        hit = (held[at] == block_ids) if found else np.zeros(block_ids.shape, bool)
+        return np.where(hit, slots[at] if found else -1, -1)
 
     # ------------------------------------------------------------------
     # Learning rates (gpu_resident_optimizer.py:149-169)
@@ -174,12 +193,12 @@ class GPUResidentAdam:
         self._state, self._slot_step_dev = state, step
         self._slot_stamp_dev, self._slot_bias_dev = stamp, bias
         grow = target - old
-        self._slot_to_block.extend([None] * grow)
+        self._slot_block = np.concatenate([self._slot_block, np.full(grow, -1, np.int64)])
+        self._slot_streak = np.concatenate([self._slot_streak, np.zeros(grow, np.int64)])
         self._slot_steps = np.concatenate([self._slot_steps, np.zeros(grow, np.int64)])
         self._slot_initialized = np.concatenate([self._slot_initialized, np.zeros(grow, bool)])
         self._slot_row_counts = np.concatenate([self._slot_row_counts, np.zeros(grow, np.int64)])
         self._slot_stamp = np.concatenate([self._slot_stamp, np.zeros(grow, np.uint32)])
-        self._free_slots.extend(range(target - 1, old - 1, -1))
         self._allocated_slots = target
 
     def _upload_slot_tables(self) -> None:
@@ -191,52 +210,54 @@ class GPUResidentAdam:
         self._slot_tables_dirty = False
 
     def set_resident_blocks(self, block_ids: List[int]) -> None:
-        next_resident = {int(block_id) for block_id in block_ids}
-        previous_resident = set(self._resident_blocks)
-        evicted = previous_resident - next_resident
-        kept = previous_resident & next_resident
-        incoming = next_resident - previous_resident
+        """Makes `block_ids` the resident set (gpu_resident_optimizer.py:
+        219-264 semantics): blocks that leave free their slot and drop their
+        moments (a state eviction when the slot had been initialized), blocks
+        that stay keep slot and moments, blocks that enter take the lowest
+        free slots with a new admission stamp, so their rows read as zero
+        moments until first touched (a cold restart). Storage grows to
+        max(needed, capacity_blocks, 2 * allocated) slots when it runs out."""
+        nxt = np.unique(np.asarray(list(block_ids), dtype=np.int64))
+        held_slots = np.nonzero(self._slot_block >= 0)[0]
+        stays = np.isin(self._slot_block[held_slots], nxt, assume_unique=True)
 
-        for block_id in evicted:
-            streak = int(self._resident_streaks.pop(block_id, 0))
-            if streak > 0:
-                self._completed_streak_total += streak
-                self._completed_streak_count += 1
-            slot = self._block_to_slot.pop(block_id)
-            if self._slot_initialized[slot]:
-                self._stats["state_evictions"] += 1
-                self._logical_state_blocks -= 1
-                self._logical_state_bytes -= int(
-                    self._slot_row_counts[slot] * self.TOTAL_WIDTH * 2 * 4
-                )
-            self._slot_to_block[slot] = None
-            self._slot_steps[slot] = 0
-            self._slot_initialized[slot] = False
-            self._slot_row_counts[slot] = 0
-            self._free_slots.append(slot)
-
-        for block_id in kept:
-            self._resident_streaks[block_id] = self._resident_streaks.get(block_id, 0) + 1
-        for block_id in incoming:
-            self._resident_streaks[block_id] = 1
-
-        self._ensure_storage(len(next_resident))
-        for block_id in sorted(incoming):
-            if not self._free_slots:
-                self._ensure_storage(self._allocated_slots + 1)
-            slot = self._free_slots.pop()
-            self._block_to_slot[block_id] = slot
-            self._slot_to_block[slot] = block_id
-            self._slot_steps[slot] = 0
-            self._slot_initialized[slot] = False
-            self._slot_row_counts[slot] = 0
-            # New admission epoch: every state row of the slot now reads as zero.
-            self._slot_stamp[slot] = np.uint32(self._slot_stamp[slot] + 1 or 1)
+        # leaving blocks
+        gone = held_slots[~stays]
+        if gone.size:
+            streaks = self._slot_streak[gone]
+            self._ended_streaks[0] += int(streaks.sum())
+            self._ended_streaks[1] += int(np.count_nonzero(streaks > 0))
+            live = gone[self._slot_initialized[gone]]
+            self._stats["state_evictions"] += int(live.size)
+            self._logical_state_blocks -= int(live.size)
+            self._logical_state_bytes -= int(self._slot_row_counts[live].sum()) * (
+                self.TOTAL_WIDTH * 2 * 4)
+            self._slot_block[gone] = -1
+            self._slot_streak[gone] = 0
+            self._slot_steps[gone] = 0
+            self._slot_initialized[gone] = False
+            self._slot_row_counts[gone] = 0
             self._slot_tables_dirty = True
-        if evicted:
-            self._slot_tables_dirty = True
+        self._slot_streak[held_slots[stays]] += 1
 
-        self._resident_blocks = next_resident
+        # entering blocks, ascending, into the lowest free slots
+        entering = np.setdiff1d(nxt, self._slot_block[held_slots[stays]], assume_unique=True)
+        self._ensure_storage(int(nxt.size))
+        free = np.nonzero(self._slot_block < 0)[0]
+        if free.size < entering.size:
+            self._ensure_storage(self._allocated_slots + int(entering.size - free.size))
+            free = np.nonzero(self._slot_block < 0)[0]
+        if entering.size:
+            new = free[: entering.size]
+            self._slot_block[new] = entering
+            self._slot_streak[new] = 1
+            self._slot_steps[new] = 0
+            self._slot_initialized[new] = False
+            self._slot_row_counts[new] = 0
+            # a new admission epoch: every state row of the slot reads as zero
+            stamp = self._slot_stamp[new] + np.uint32(1)
+            self._slot_stamp[new] = np.where(stamp == 0, np.uint32(1), stamp)
+            self._slot_tables_dirty = True
         self._update_state_stats()
 
     # ------------------------------------------------------------------
@@ -267,27 +288,27 @@ class GPUResidentAdam:
     def _working_set_layout(self, manager) -> Tuple[np.ndarray, ...]:
         """(starts, ends, block_ids, slots) of loaded blocks sorted by slice
         start (gpu_resident_optimizer.py:266-287)."""
-        items = []
         block_to_slice = manager.block_to_gpu_slice
+        rows = []
         for block_id in manager.loaded_blocks:
-            block_id = int(block_id)
-            block_slice = block_to_slice.get(block_id)
-            if block_slice is None:
-                continue
-            slot = self._block_to_slot.get(block_id)
-            if slot is None:
-                raise RuntimeError(
-                    f"[GPUResidentAdam] loaded block {block_id} has no resident state slot"
-                )
-            items.append((int(block_slice.start), int(block_slice.stop), block_id, slot))
-        items.sort(key=lambda item: item[0])
-        if not items:
+            block_slice = block_to_slice.get(int(block_id))
+            if block_slice is not None:
+                rows.append((int(block_slice.start), int(block_slice.stop), int(block_id)))
+        if not rows:
             raise RuntimeError("[GPUResidentAdam] working set contains no resident blocks")
-        arr = np.asarray(items, dtype=np.int64)
+        arr = np.asarray(rows, dtype=np.int64)
+        slots = self._slots_of(arr[:, 2])
+        if np.any(slots < 0):
+            missing = int(arr[np.nonzero(slots < 0)[0][0], 2])
+            raise RuntimeError(
+                f"[GPUResidentAdam] loaded block {missing} has no resident state slot"
+            )
+        order = np.argsort(arr[:, 0], kind="stable")
+        arr, slots = arr[order], slots[order]
         starts, ends = arr[:, 0], arr[:, 1]
         if np.any(ends < starts) or np.any(starts[1:] < ends[:-1]):
             raise RuntimeError("[GPUResidentAdam] resident block slices overlap")
-        return starts, ends, arr[:, 2], arr[:, 3]
+        return starts, ends, arr[:, 2], slots
 
     def _stage_layout(self, starts, ends, slots) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
         """Device copies of the layout tables, uploaded by kernels on the
@@ -401,6 +422,10 @@ class GPUResidentAdam:
         pos_start, pos_end, pos_slot = self._stage_layout(starts, ends, layout_slots)
         stream = _lib.stream_handle(self.device)
 
+        chunks = (n + 31) // 32
+        if self._chunk_table is None or self._chunk_table.numel() < 2 * chunks:
+            self._chunk_table = torch.empty(2 * max(chunks, 1024), dtype=torch.int64,
+                                            device=self.device)
         cargs = _lib.ResidentCountArgs(
             pos_start=pos_start.data_ptr(), pos_end=pos_end.data_ptr(),
             pos_slot=pos_slot.data_ptr(), n_positions=P, block_size=self.block_size,
@@ -409,6 +434,7 @@ class GPUResidentAdam:
             slot_bias=self._slot_bias_dev.data_ptr(), step_table=table.data_ptr(),
             step_table_len=table_len, n_slots=self._allocated_slots,
             pos_count=self._dev_counts.data_ptr(), err=self._err.data_ptr(),
+            chunk_table=self._chunk_table.data_ptr(),
         )
         _lib.call("tgs_resident_adam_count", cargs, stream)
         # Read back per-position counts + the error word while the update runs.
@@ -435,6 +461,7 @@ class GPUResidentAdam:
         aargs.slot_stamp = self._slot_stamp_dev.data_ptr()
         aargs.slot_bias = self._slot_bias_dev.data_ptr()
         aargs.err = self._err.data_ptr()
+        aargs.chunk_table = self._chunk_table.data_ptr()
         if pulled is None:
             _lib.call("tgs_resident_adam_apply", aargs, stream)
         else:

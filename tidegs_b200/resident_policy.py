@@ -177,14 +177,15 @@ def _updated_recency(previous, accessed: np.ndarray, decay: float):
         return out, out.lookup
     prev = previous or {}
     decay = float(decay)
-    if prev is _last_returned[0] and len(prev) == _last_returned[1]:
-        # the dict this function returned last (int keys, float values
-        # already): no per-entry conversions
-        updated = {b: d for b, s in prev.items() if (d := s * decay) > _DROP_BELOW}
+    updated = _RecencyDict()
+    if type(prev) is _RecencyDict and prev.pristine:
+        # a dict this function returned and nobody has written to since (int
+        # keys, float values already): no per-entry conversions
+        dict.update(updated, {b: d for b, s in prev.items() if (d := s * decay) > _DROP_BELOW})
     else:
-        updated = {int(b): d for b, s in prev.items() if (d := float(s) * decay) > _DROP_BELOW}
-    updated.update(dict.fromkeys(accessed.tolist(), 1.0))
-    _last_returned[:] = [updated, len(updated)]
+        dict.update(updated, {int(b): d for b, s in prev.items()
+                              if (d := float(s) * decay) > _DROP_BELOW})
+    dict.update(updated, dict.fromkeys(accessed.tolist(), 1.0))
     get = updated.get
 
     def lookup(ids: np.ndarray) -> np.ndarray:
@@ -193,11 +194,53 @@ def _updated_recency(previous, accessed: np.ndarray, decay: float):
     return updated, lookup
 
 
-# The last recency dict _updated_recency returned and its length (held, so
-# that the identity test cannot match a different dict at a reused
-# address): the runtime passes it back as the next transition's previous
-# scores.
-_last_returned: list = [None, -1]
+class _RecencyDict(dict):
+    """The recency map a transition returns (a plain dict to its callers):
+    int block ids to float scores. Writing to it through any dict method
+    clears `pristine`, and the next transition then converts every entry as
+    the reference does (resident_policy.py:115-119) instead of trusting the
+    types."""
+
+    __slots__ = ("pristine",)
+
+    def __init__(self, *args, **kwargs):
+        super().__init__(*args, **kwargs)
+        self.pristine = True
+
+    def _touched(self):
+        self.pristine = False
+
+    def __setitem__(self, key, value):
+        self._touched()
+        super().__setitem__(key, value)
+
+    def __delitem__(self, key):
+        self._touched()
+        super().__delitem__(key)
+
+    def __ior__(self, other):
+        self._touched()
+        return super().__ior__(other)
+
+    def update(self, *args, **kwargs):
+        self._touched()
+        super().update(*args, **kwargs)
+
+    def setdefault(self, key, default=None):
+        self._touched()
+        return super().setdefault(key, default)
+
+    def pop(self, *args):
+        self._touched()
+        return super().pop(*args)
+
+    def popitem(self):
+        self._touched()
+        return super().popitem()
+
+    def clear(self):
+        self._touched()
+        super().clear()
 
 
 def _normalized_cameras(camera_blocks, allowed: Optional[np.ndarray]) -> List[Tuple[int, np.ndarray]]:

@@ -11,9 +11,10 @@ Gaussians x 59 fp32 (33.5 M Gaussians per GPU):
   2. dirty marking of the updated blocks and their xyz bounds,
   3. dirty-and-evicted compaction of 512 evicted blocks (25 % turnover) and
      the CACHE-layout write-back pack of the dirty ones,
-  4. materialization of 512 incoming blocks into the freed slots (packed rows
-     -> component arrays + global ids, then the slot remap). The unpack into
-     the loading buffer is enqueued before the pack: it does not depend on the
+  4. materialization of 512 incoming blocks (packed rows -> component arrays
+     + global ids) straight into the spare slots of the slot arena, whose
+     evicted slots become the next spare ones (no slot-remap copy). The
+     unpack is enqueued before the pack: it does not depend on the
      write-back, and it keeps the device busy while the host waits for the
      dirty list.
 `value` runs the step through the library entry points with every input
@@ -403,6 +404,15 @@ class ScheduleTrace:
 
 
 class DeviceStep:
+    """The step through the library entry points, every input in HBM. The
+    resident blocks live in a slot arena of SLOTS + TURNOVER block slots:
+    the TURNOVER spare slots receive the next step's incoming blocks straight
+    from the unpack (tgs_unpack_rows' block scatter), and the evicted blocks'
+    slots become the spare ones, so no slot-remap copy is needed. A block's
+    optimizer state lives with its arena slot (state slot = arena slot): a
+    block keeps its slot while resident, and an incoming block's slot gets a
+    new admission stamp (its moments read as zero)."""
+
     def __init__(self, device, sched: Schedule, trace: ScheduleTrace, world: int = 1,
                  exchange: str = "pull"):
         from tidegs_b200 import _lib, _ops
@@ -413,36 +423,42 @@ class DeviceStep:
         self.trace = trace
         self.world = world
         gen = torch.Generator(device=device).manual_seed(1234 + sched.rank)
-        rows = SLOTS * B
+        self.n_arena = SLOTS + TURNOVER
+        rows = self.n_arena * B
+        # schedule position i -> arena slot; arena slot -> block (-1 spare)
+        self.arena_of_pos = np.arange(SLOTS, dtype=np.int64)
+        self.arena_block = np.full(self.n_arena, -1, np.int64)
+        self.arena_block[:SLOTS] = sched.slot_block
+        self.spare = np.arange(SLOTS, self.n_arena, dtype=np.int64)
         self.arena = {n: torch.empty((rows, w), device=device) for n, w in WIDTHS.items()}
         fill_params(self.arena, gen)
         self.gids = torch.empty(rows, dtype=torch.int64, device=device)
-        _ops.fill_global_ids(self.gids, 0, _ops.i64_to_device(sched.slot_block, device), rows, B)
+        _ops.fill_global_ids(self.gids, 0, _ops.i64_to_device(self.arena_block, device), rows, B)
         # incoming blocks already landed in HBM (packed CACHE rows), 2 rotating sets
         self.incoming_pool = torch.empty((2 * TURNOVER * B, 59), device=device)
         self.incoming_pool.normal_(0.0, 1.0, generator=gen)
-        self.loading = {n: torch.empty((TURNOVER * B, w), device=device) for n, w in WIDTHS.items()}
-        self.loading_gids = torch.empty(TURNOVER * B, dtype=torch.int64, device=device)
         self.wb_staging = torch.empty((TURNOVER * B, 59), device=device)
-        self.bounds = torch.empty((SLOTS, 6), device=device)
-        # resident Adam state
+        self.bounds = torch.empty((self.n_arena, 6), device=device)
+        # resident Adam state, one optimizer slot per arena slot
         self.state = torch.zeros((rows, 128), device=device)
-        self.slot_step = torch.zeros(SLOTS, dtype=torch.int32, device=device)
-        self.stamp_host = np.ones(SLOTS, np.uint32)
-        self.slot_stamp = torch.ones(SLOTS, dtype=torch.int32, device=device)
-        self.slot_bias = torch.ones((SLOTS, 2), device=device)
+        self.slot_step = torch.zeros(self.n_arena, dtype=torch.int32, device=device)
+        self.stamp_host = np.ones(self.n_arena, np.uint32)
+        self.slot_stamp = torch.ones(self.n_arena, dtype=torch.int32, device=device)
+        self.slot_bias = torch.ones((self.n_arena, 2), device=device)
         table = [(0.0, 0.0)] + [(float(np.float32(1 - 0.9 ** t)),
                                  float(np.float32(math.sqrt(1 - 0.999 ** t))))
                                 for t in range(1, 20000)]
         self.table = torch.tensor(table, dtype=torch.float32, device=device)
         self.err = torch.zeros(4, dtype=torch.int32, device=device)
-        self.pos_count = torch.zeros(SLOTS, dtype=torch.int32, device=device)
+        self.pos_count = torch.zeros(self.n_arena, dtype=torch.int32, device=device)
         self.chunk_table = torch.empty(2 * sched.traj.max_owned_visible() * B // 32,
                                        dtype=torch.int64, device=device)
-        starts = np.arange(SLOTS, dtype=np.int64) * B
-        self.pos_start = _ops.i64_to_device(starts, device)
-        self.pos_end = _ops.i64_to_device(starts + B, device)
-        self.pos_slot = torch.arange(SLOTS, dtype=torch.int32, device=device)
+        # working-set positions = arena slots; a spare slot is an empty slice
+        self.pos_start_host = np.arange(self.n_arena, dtype=np.int64) * B
+        self.pos_start = _ops.i64_to_device(self.pos_start_host, device)
+        self.pos_end = torch.empty(self.n_arena, dtype=torch.int64, device=device)
+        self._upload_pos_end()
+        self.pos_slot = torch.arange(self.n_arena, dtype=torch.int32, device=device)
         self.bitmap = torch.zeros(_ops.bitmap_words(SCENE_BLOCKS), dtype=torch.int32,
                                   device=device)
         # the owner's row ids of a step (all rows of its visible positions)
@@ -481,16 +497,27 @@ class DeviceStep:
         self.updated_rows = []
         torch.cuda.synchronize()
 
+    def _upload_pos_end(self) -> None:
+        """Working-set slices: a resident arena slot covers its B rows, a
+        spare one is empty (no row id can fall in it)."""
+        end = self.pos_start_host + np.where(self.arena_block >= 0, B, 0)
+        self._ops.upload_into(self.pos_end, end)
+
+    def visible_arena(self, k: int) -> np.ndarray:
+        """Arena slots of this owner's visible blocks at step k, ascending
+        (the owner's row ids are all rows of these slots, in this order)."""
+        return np.sort(self.arena_of_pos[self.sched.visible_positions(k)])
+
     def exchange_grads(self, k: int):
         """Owner-sharded gradient exchange of step k (world > 1): returns the
-        owner's visible slot positions and local row ids; the reduced
-        gradients land in self.grads."""
+        owner's visible arena slots and local row ids; the reduced gradients
+        land in self.grads (or are summed by the pull kernel)."""
         W, me = self.world, self.sched.rank
         vis = self.trace.vis[k]
         if self._ahead is not None and self._ahead[0] == k:
             _, plan, slot_of, self.pull_tables = self._ahead  # built during step k-1
         else:
-            plan, slot_of, self.pull_tables = self._make_plan(k, self.sched.slot_block)
+            plan, slot_of, self.pull_tables = self._make_plan(k, self.arena_block)
         self._ahead = None
         # the rank's rendered gradients: its blocks in ascending id, B rows each
         starts = np.searchsorted(np.unique(vis[me]), plan.send_blocks).astype(np.int64) * B
@@ -511,42 +538,53 @@ class DeviceStep:
             recv = self.exchange.all_to_all(plan, send, out=self.recv_buf)
             self.exchange.reduce(plan, recv, out=self.grads, err=self.err)
             self.exchange_rows += int(send.shape[0])
-        pos = slot_of[plan.out_blocks]
+        slots = slot_of[plan.out_blocks]
         # the plan's output blocks are the owner's visible blocks in slot order
-        if not np.array_equal(pos, self.sched.visible_positions(k)):
+        if not np.array_equal(slots, self.visible_arena(k)):
             raise RuntimeError("exchange plan and owner visibility disagree")
-        return pos, self.row_ids(pos)
+        return slots, self.row_ids(slots)
 
-    def row_ids(self, pos: np.ndarray) -> torch.Tensor:
-        """All rows of slot positions `pos` (ascending), expanded on the
-        device from the positions."""
-        n = int(pos.size) * B
+    def row_ids(self, slots: np.ndarray) -> torch.Tensor:
+        """All rows of arena slots `slots` (ascending), expanded on the
+        device from the slots."""
+        n = int(slots.size) * B
         if n > self.ids_buf.numel():
-            raise RuntimeError(f"{pos.size} visible positions exceed the row-id buffer")
+            raise RuntimeError(f"{slots.size} visible blocks exceed the row-id buffer")
         ids = self.ids_buf[:n]
-        self._ops.fill_global_ids(ids, 0, self._ops.i64_to_device(pos, self.device), n, B)
+        self._ops.fill_global_ids(ids, 0, self._ops.i64_to_device(slots, self.device), n, B)
         return ids
 
-    def _make_plan(self, k: int, slot_block: np.ndarray):
-        """Exchange plan of step k for the slot map `slot_block` (and, for the
-        pull exchange, its device tables)."""
+    def _make_plan(self, k: int, arena_block: np.ndarray):
+        """Exchange plan of step k for the arena map `arena_block` (output
+        blocks ordered by arena slot) and, for the pull exchange, its device
+        tables."""
         from tidegs_b200.sharded import make_plan
 
         table = np.full(SCENE_BLOCKS, -1, np.int64)
-        table[slot_block] = np.arange(slot_block.size, dtype=np.int64)
+        held = np.nonzero(arena_block >= 0)[0]
+        table[arena_block[held]] = held
         plan = make_plan(self.trace.vis[k], self.world, self.sched.rank, B, out_order=table)
         tables = self.pull.tables(plan) if self.pull is not None else None
         return plan, table, tables
 
+    def _after_turnover(self, k: int):
+        """(arena map, position map, spare slots) after step k's turnover:
+        position ev[i] takes incoming[i] into spare slot i (both ascending)."""
+        ev, inc, _ = self.trace.turn[k]
+        arena_block = self.arena_block.copy()
+        arena_of_pos = self.arena_of_pos.copy()
+        freed = arena_of_pos[ev]
+        arena_block[freed] = -1
+        arena_block[self.spare] = inc
+        arena_of_pos[ev] = self.spare
+        return arena_block, arena_of_pos, np.sort(freed)
+
     def plan_ahead(self, k: int):
         """Builds step k+1's plan on the host while the GPU runs step k (the
-        slot map after step k's turnover is known from the schedule)."""
+        arena map after step k's turnover is known from the schedule)."""
         if self.world == 1 or k + 1 >= len(self.trace.turn):
             return
-        ev, inc, _ = self.trace.turn[k]
-        nxt = self.sched.slot_block.copy()
-        nxt[ev] = inc
-        self._ahead = (k + 1,) + self._make_plan(k + 1, nxt)
+        self._ahead = (k + 1,) + self._make_plan(k + 1, self._after_turnover(k)[0])
 
     _ahead = None
     pull_tables = None
@@ -557,11 +595,11 @@ class DeviceStep:
         stream = _lib.stream_handle(self.device)
         c = _lib.ResidentCountArgs(
             pos_start=self.pos_start.data_ptr(), pos_end=self.pos_end.data_ptr(),
-            pos_slot=self.pos_slot.data_ptr(), n_positions=SLOTS, block_size=B,
-            param_rows=SLOTS * B, local_ids=ids.data_ptr(), n_rows=n,
+            pos_slot=self.pos_slot.data_ptr(), n_positions=self.n_arena, block_size=B,
+            param_rows=self.n_arena * B, local_ids=ids.data_ptr(), n_rows=n,
             slot_step=self.slot_step.data_ptr(), slot_stamp=self.slot_stamp.data_ptr(),
             slot_bias=self.slot_bias.data_ptr(), step_table=self.table.data_ptr(),
-            step_table_len=self.table.shape[0], n_slots=SLOTS,
+            step_table_len=self.table.shape[0], n_slots=self.n_arena,
             pos_count=self.pos_count.data_ptr(), err=self.err.data_ptr(),
             chunk_table=self.chunk_table.data_ptr())
         tables = self.pull_tables
@@ -577,7 +615,7 @@ class DeviceStep:
         a.batch_size = 16.0
         a.pos_start, a.pos_end, a.pos_slot = (self.pos_start.data_ptr(), self.pos_end.data_ptr(),
                                               self.pos_slot.data_ptr())
-        a.n_positions, a.block_size = SLOTS, B
+        a.n_positions, a.block_size = self.n_arena, B
         a.local_ids, a.n_rows = ids.data_ptr(), n
         a.state, a.slot_stamp = self.state.data_ptr(), self.slot_stamp.data_ptr()
         a.slot_bias, a.err = self.slot_bias.data_ptr(), self.err.data_ptr()
@@ -627,23 +665,23 @@ class DeviceStep:
         self._phase("start")
         if self.world > 1:
             # 0. gradients of blocks rendered on other ranks reach their owners
-            pos, ids = self.exchange_grads(k)
+            slots, ids = self.exchange_grads(k)
             self._phase("exchange")
         else:
-            pos = sched.visible_positions(k)
-            ids = self.row_ids(pos)
+            slots = self.visible_arena(k)
+            ids = self.row_ids(slots)
         # 1. optimizer over the visible rows
         self.adam(ids, timed)
         self.plan_ahead(k)
         # 2. updated blocks are dirty; refresh their bounds
-        updated = sched.slot_block[pos]
-        _ops.dirty_mark(self.bitmap, updated.tolist(), True)
-        _ops.block_bounds(self.arena["xyz"], (pos * B).tolist(), [B] * pos.size,
-                          self.bounds[: pos.size])
+        _ops.dirty_mark(self.bitmap, self.arena_block[slots].tolist(), True)
+        _ops.block_bounds(self.arena["xyz"], (slots * B).tolist(), [B] * slots.size,
+                          self.bounds[: slots.size])
         self._phase("dirty_bounds")
-        # 3. evict TURNOVER slots: write back the dirty ones
+        # 3. evict TURNOVER blocks: write back the dirty ones
         evict_pos, incoming, dirty = self.trace.turn[k]
-        evicted_blocks = sched.slot_block[evict_pos]
+        evict_slots = self.arena_of_pos[evict_pos]
+        evicted_blocks = self.arena_block[evict_slots]
         if dirty is not None:
             # a schedule with a prescribed dirty pattern
             _ops.dirty_mark(self.bitmap, evicted_blocks[dirty].tolist(), True)
@@ -651,31 +689,32 @@ class DeviceStep:
         order = np.argsort(evicted_blocks, kind="stable")
         selection = _ops.dirty_select_async(self.bitmap, evicted_blocks[order].tolist())
         self._phase("dirty_select")
-        # 4. materialize the incoming blocks into the loading buffer; this does
-        # not depend on the write-back, so the device runs it while the host
-        # waits for the dirty list and plans the pack
+        # 4. materialize the incoming blocks straight into the spare slots
+        # (with their global ids); this does not depend on the write-back, so
+        # the device runs it while the host waits for the dirty list
         src = self.incoming_pool[(k % 2) * TURNOVER * B:(k % 2 + 1) * TURNOVER * B]
         ids_dev = _ops.i64_to_device(incoming, self.device)
-        _ops.unpack_rows(src, self._lib.LAYOUT_CACHE, self.loading, 0,
-                         global_ids=self.loading_gids, block_ids=ids_dev, block_size=B)
+        _ops.unpack_rows(src, self._lib.LAYOUT_CACHE, self.arena, 0, global_ids=self.gids,
+                         block_ids=ids_dev, block_size=B, block_dst=self.spare * B)
         self._phase("unpack")
         wb_ids = selection.wait()
         sorted_blocks = evicted_blocks[order]
-        wb_pos = evict_pos[order][np.searchsorted(sorted_blocks, np.asarray(wb_ids, np.int64))]
-        _ops.pack_rows(self.arena, (wb_pos * B).tolist(), [B] * wb_pos.size,
-                       self.wb_staging[: wb_pos.size * B], self._lib.LAYOUT_CACHE)
+        wb_slots = evict_slots[order][np.searchsorted(sorted_blocks,
+                                                      np.asarray(wb_ids, np.int64))]
+        _ops.pack_rows(self.arena, (wb_slots * B).tolist(), [B] * wb_slots.size,
+                       self.wb_staging[: wb_slots.size * B], self._lib.LAYOUT_CACHE)
         self._phase("pack")
         _ops.dirty_mark(self.bitmap, wb_ids, False)
         self._phase("writeback")
-        # 5. evicted slots take the incoming blocks
-        _ops.copy_blocks(self.loading, self.loading_gids, self.arena, self.gids,
-                         (np.arange(TURNOVER) * B).tolist(), (evict_pos * B).tolist(),
-                         [B] * TURNOVER, self.device)
-        self._phase("slot_copy")
+        # 5. the spare slots hold the incoming blocks; the evicted blocks'
+        # slots become the spare ones (no copy). Incoming slots: new stamps.
+        new_slots = self.spare
+        self.arena_block, self.arena_of_pos, self.spare = self._after_turnover(k)
         sched.slot_block[evict_pos] = incoming
-        self.stamp_host[evict_pos] += 1
+        self.stamp_host[new_slots] += 1
         _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
-        self.slot_step.index_fill_(0, _ops.i64_to_device(evict_pos, self.device), 0)
+        self.slot_step.index_fill_(0, _ops.i64_to_device(new_slots, self.device), 0)
+        self._upload_pos_end()
         self._phase("tables")
         return int(ids.numel())
 
@@ -709,8 +748,10 @@ class DeviceStep:
         # overwritten by the incoming blocks at its end)
         cand = np.setdiff1d(pos_all, evict_pos)
         pick = np.sort(rng.choice(cand, min(blocks_per_owner, cand.size), replace=False))
-        mine = [(int(sched.slot_block[p]), int(p), int(rng.integers(0, B - rows + 1)))
-                for p in pick]
+        # (block, its arena slot, first row of the window)
+        mine = [(int(sched.slot_block[p]), int(self.arena_of_pos[p]),
+                 int(rng.integers(0, B - rows + 1))) for p in pick]
+        vis_slots = self.visible_arena(k)
 
         def gather(obj):
             if W == 1:
@@ -721,12 +762,12 @@ class DeviceStep:
             dist.all_gather_object(out, obj)
             return out
 
-        samples = gather(mine)  # [owner] -> [(block, position, first row)]
+        samples = gather(mine)  # [owner] -> [(block, arena slot, first row)]
         # this rank's gradient rows for every sampled block it rendered
         contrib = {}
         if W == 1:
             for b, p, r0 in mine:
-                i = int(np.searchsorted(pos_all, p))
+                i = int(np.searchsorted(vis_slots, p))
                 contrib[(0, b)] = np.concatenate(
                     [self.grads[n][i * B + r0: i * B + r0 + rows].cpu().numpy()
                      for n in NAMES], axis=1)

@@ -240,6 +240,12 @@ typedef struct {
   const int64_t* block_ids;            /* [ceil(n_rows / block_size)] */
   int64_t block_size;
   int32_t* err;                        /* [4] device error word (may be NULL) */
+  /* Optional scatter by block (NULL: the batch lands contiguously at
+   * target_offset): [ceil(n_rows / block_size)] first target row of each
+   * block of the batch, e.g. a free slot of a slot arena, so that incoming
+   * blocks need no later slot-remap copy. Needs block_size a multiple of 64;
+   * target_offset is then ignored. */
+  const int64_t* block_dst;
 } TgsUnpackArgs;
 
 /* Packed [rows,59] -> six SoA components (+ global ids), TMA bulk tile loads.

@@ -82,7 +82,7 @@ class UnpackArgs(C.Structure):
     _fields_ = [
         ("packed", _vp), ("n_rows", _i64), ("layout", _i32), ("comp", _vp * NUM_COMPONENTS),
         ("target_offset", _i64), ("global_ids", _vp), ("block_ids", _vp), ("block_size", _i64),
-        ("err", _vp),
+        ("err", _vp), ("block_dst", _vp),
     ]
 
 

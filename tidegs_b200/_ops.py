@@ -88,12 +88,28 @@ def _comp_ptrs(components: Mapping[str, torch.Tensor], who: str) -> List[int]:
 def unpack_rows(packed: torch.Tensor, layout_code: int, targets: Mapping[str, torch.Tensor],
                 target_offset: int, global_ids: Optional[torch.Tensor] = None,
                 block_ids: Optional[torch.Tensor] = None, block_size: int = 0,
-                err: Optional[torch.Tensor] = None) -> None:
+                err: Optional[torch.Tensor] = None,
+                block_dst: Optional[Sequence[int]] = None) -> None:
+    """Unpacks packed [rows, 59] into the SoA targets: contiguously at
+    target_offset, or, with block_dst (host ints, one per block of
+    block_size rows), block k at target row block_dst[k]."""
     n_rows = int(packed.shape[0])
     if n_rows == 0:
         return
     if packed.dtype != torch.float32 or not packed.is_contiguous() or packed.shape[1] != 59:
         raise RuntimeError("unpack_rows: packed rows must be contiguous float32 [rows, 59]")
+    target_rows = min(int(targets[n].shape[0]) for n in COMPONENTS)
+    dst_dev = None
+    if block_dst is not None:
+        dst = np.asarray(block_dst, np.int64)
+        if block_size <= 0 or dst.size * block_size < n_rows:
+            raise ValueError("unpack_rows: block_dst needs one target row per block")
+        if dst.size and (dst.min() < 0 or dst.max() + block_size > target_rows):
+            raise ValueError("unpack_rows: a block_dst slot lies outside the targets")
+        dst_dev = i64_to_device(dst, packed.device)
+    elif target_offset < 0 or target_offset + n_rows > target_rows:
+        raise ValueError(f"unpack_rows: rows [{target_offset}, {target_offset + n_rows}) "
+                         f"outside {target_rows}-row targets")
     args = _lib.UnpackArgs()
     args.packed = packed.data_ptr()
     args.n_rows = n_rows
@@ -105,7 +121,10 @@ def unpack_rows(packed: torch.Tensor, layout_code: int, targets: Mapping[str, to
     args.block_ids = _lib.ptr(block_ids)
     args.block_size = int(block_size)
     args.err = _lib.ptr(err)
+    args.block_dst = _lib.ptr(dst_dev)
     _lib.call("tgs_unpack_rows", args, _stream(packed.device))
+    if dst_dev is not None:
+        _keepalive(dst_dev, packed.device)
 
 
 def copy_blocks(src: Mapping[str, torch.Tensor], src_gids: Optional[torch.Tensor],

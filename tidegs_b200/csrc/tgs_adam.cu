@@ -922,10 +922,15 @@ constexpr int kStorerWarp = kStreamConsumerWarps + 1;
 constexpr int kStreamThreads = (kStreamConsumerWarps + 2) * 32;
 constexpr int kRowsPerConsumer = kTileRows / kStreamConsumerWarps;
 #ifndef TGS_STREAM_STAGES
-#define TGS_STREAM_STAGES 6
+#define TGS_STREAM_STAGES 4
 #endif
 #ifndef TGS_SUM_STREAM_STAGES
-#define TGS_SUM_STREAM_STAGES 5
+#define TGS_SUM_STREAM_STAGES 4
+#endif
+// contributions of a segment D' stages in shared memory; further ones are
+// read from the senders' memory element by element
+#ifndef TGS_SUM_STAGED_CONTRIBS
+#define TGS_SUM_STAGED_CONTRIBS 4
 #endif
 // CTAs per SM of the streaming kernels (the stages of all of them share the
 // SM's shared memory)
@@ -1044,17 +1049,20 @@ __device__ __forceinline__ int64_t scan_next(ChunkScan& cs, const int64_t* table
 // first staged tile (D: the chunk's gradient; D': contribution 0), plus, for
 // D', the second staged contribution and then any further ones read from the
 // senders' memory one by one, in the segment's (rank) order.
-template <bool kPow2Batch, bool kSum>
-__device__ __forceinline__ void stream_update_col(float* param, const float* g0t,
-                                                  const float* g1t, const StreamDesc& d,
-                                                  const ResidentSumParams* q, float2* srow,
-                                                  const StreamCol& sc, int r, int j, bool fresh,
-                                                  const RowScale& rs, const AdamScalars& hp) {
+template <bool kPow2Batch, bool kSum, int kGrads>
+__device__ __forceinline__ void stream_update_col(float* param,
+                                                  const float (*grads)[kTileRows * kRowWidth],
+                                                  const StreamDesc& d, const ResidentSumParams* q,
+                                                  float2* srow, const StreamCol& sc, int r, int j,
+                                                  bool fresh, const RowScale& rs,
+                                                  const AdamScalars& hp) {
   const int idx = sc.base + r * sc.width;
   float p = param[idx];
-  float g = g0t[idx];
+  float g = grads[0][idx];
   if constexpr (kSum) {
-    if (d.ns > 1) g = fadd(g, g1t[idx]);
+#pragma unroll
+    for (int jj = 1; jj < kGrads; ++jj)
+      if (jj < d.ns) g = fadd(g, grads[jj][idx]);
     for (int jj = d.ns; jj < d.cn; ++jj) {
       const int k = d.cb + jj;
       const int rk = __ldg(q->contrib_rank + k);
@@ -1076,7 +1084,7 @@ __device__ __forceinline__ void stream_update_col(float* param, const float* g0t
 
 template <bool kPow2Batch, bool kSum>
 __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentSumParams* q) {
-  constexpr int kGrads = kSum ? 2 : 1;
+  constexpr int kGrads = kSum ? TGS_SUM_STAGED_CONTRIBS : 1;
   constexpr int kStages = kSum ? TGS_SUM_STREAM_STAGES : TGS_STREAM_STAGES;
   using Stage = StreamStage<kGrads>;
   extern __shared__ __align__(128) unsigned char stream_smem[];
@@ -1114,8 +1122,13 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
     const bool pow2B = (B & (B - 1)) == 0;
     const int shiftB = __ffsll(B) - 1;
     // D': the segment of the last chunk looked at, cached (lane 0)
-    int64_t seg_lo = 0, seg_hi = -1, src_row0 = 0, src_row1 = 0;
-    int32_t seg_cb = 0, seg_cn = 0, src_rank0 = 0, src_rank1 = 0;
+    int64_t seg_lo = 0, seg_hi = -1, src_row[kGrads];
+    int32_t seg_cb = 0, seg_cn = 0, src_rank[kGrads];
+#pragma unroll
+    for (int jj = 0; jj < kGrads; ++jj) {
+      src_row[jj] = 0;
+      src_rank[jj] = 0;
+    }
     bool seg_ok = false;
     bool failed = false;
     int64_t t = 0;
@@ -1144,16 +1157,12 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
               seg_cb = static_cast<int32_t>(__ldg(q->contrib_offsets + sg));
               seg_cn = static_cast<int32_t>(__ldg(q->contrib_offsets + sg + 1)) - seg_cb;
               seg_ok = seg_cn >= 1;
-              for (int jj = 0; jj < kGrads && jj < seg_cn; ++jj) {
+#pragma unroll
+              for (int jj = 0; jj < kGrads; ++jj) {
+                if (jj >= seg_cn) break;
                 const int r = __ldg(q->contrib_rank + seg_cb + jj);
-                const int64_t row = __ldg(q->contrib_row + seg_cb + jj);
-                if (jj == 0) {
-                  src_rank0 = r;
-                  src_row0 = row;
-                } else {
-                  src_rank1 = r;
-                  src_row1 = row;
-                }
+                src_rank[jj] = r;
+                src_row[jj] = __ldg(q->contrib_row + seg_cb + jj);
                 if (r < 0 || r >= q->n_ranks) {
                   seg_ok = false;
                   continue;
@@ -1165,11 +1174,12 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
           }
           if (seg_ok && row0 + kTileRows <= seg_hi) {
             ok = 1;
-            const int nst = seg_cn < kGrads ? seg_cn : kGrads;
-            for (int jj = 0; jj < nst; ++jj) {
-              const int64_t srow = (jj == 0 ? src_row0 : src_row1) + (row0 - seg_lo);
-              const int rk = jj == 0 ? src_rank0 : src_rank1;
-              if (srow < 0 || (srow & 3) != 0 || srow + kTileRows > __ldg(q->grad_rows + rk))
+#pragma unroll
+            for (int jj = 0; jj < kGrads; ++jj) {
+              if (jj >= seg_cn) break;
+              const int64_t srow = src_row[jj] + (row0 - seg_lo);
+              if (srow < 0 || (srow & 3) != 0 ||
+                  srow + kTileRows > __ldg(q->grad_rows + src_rank[jj]))
                 ok = 0;
             }
           }
@@ -1217,9 +1227,11 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
           S.desc.cb = seg_cb;
           S.desc.cn = seg_cn;
           S.desc.seg_off = seg_off;
-          for (int jj = 0; jj < ns; ++jj) {
-            const float* const* src = q->grad_src + (jj == 0 ? src_rank0 : src_rank1) * kNumComp;
-            const int64_t srow = (jj == 0 ? src_row0 : src_row1) + seg_off;
+#pragma unroll
+          for (int jj = 0; jj < kGrads; ++jj) {
+            if (jj >= ns) break;
+            const float* const* src = q->grad_src + src_rank[jj] * kNumComp;
+            const int64_t srow = src_row[jj] + seg_off;
 #pragma unroll
             for (int c = 0; c < kNumComp; ++c)
               bulk_g2s(S.grad[jj] + kTileRows * unified_offset(c), src[c] + srow * comp_width(c),
@@ -1285,7 +1297,6 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
     }
     if (S.desc.chunk < 0) break;
     const StreamDesc d = S.desc;
-    const float* g1t = S.grad[kGrads - 1];
 #pragma unroll
     for (int u = 0; u < kRowsPerConsumer; ++u) {
       const int r = warp * kRowsPerConsumer + u;
@@ -1295,11 +1306,11 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
       // a row whose stamp is not its slot's current stamp has not been
       // touched since the block was (re)admitted: its moments are zero
       const bool fresh = __float_as_uint(srow_f[124]) == rs.stamp;
-      stream_update_col<kPow2Batch, kSum>(S.param, S.grad[0], g1t, d, q, srow, c0, r, lane,
-                                          fresh, rs, hp);
+      stream_update_col<kPow2Batch, kSum, kGrads>(S.param, S.grad, d, q, srow, c0, r, lane,
+                                                  fresh, rs, hp);
       if (has1)
-        stream_update_col<kPow2Batch, kSum>(S.param, S.grad[0], g1t, d, q, srow, c1, r,
-                                            lane + 32, fresh, rs, hp);
+        stream_update_col<kPow2Batch, kSum, kGrads>(S.param, S.grad, d, q, srow, c1, r,
+                                                    lane + 32, fresh, rs, hp);
       __syncwarp();  // every lane has read the stamp
       if (lane == 30) srow_f[124] = __uint_as_float(rs.stamp);
     }
@@ -1732,7 +1743,7 @@ extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void
   cudaStream_t s = as_stream(stream);
   if (can_stream(q.a, false)) {
     static bool configured[2][64] = {};
-    constexpr int smem = stream_smem_bytes<2, TGS_SUM_STREAM_STAGES>();
+    constexpr int smem = stream_smem_bytes<TGS_SUM_STAGED_CONTRIBS, TGS_SUM_STREAM_STAGES>();
     const int sgrid = stream_grid(a->adam.n_rows, TGS_SUM_STREAM_CTAS);
     const int rc2 = pow2 ? launch_stream(resident_adam_sum_stream_kernel<true>, q, smem, sgrid, s,
                                          configured[1])

@@ -46,6 +46,7 @@ struct UnpackParams {
   int64_t block_size;
   int use_bulk;  // packed is 16-byte aligned
   int32_t* err;
+  const int64_t* block_dst;  // first target row per block, or null (contiguous)
 };
 
 struct UnpackSmem {
@@ -131,7 +132,12 @@ __global__ void __launch_bounds__(kUnpackThreads, kUnpackCtasPerSm) unpack_kerne
       __syncthreads();
       return;
     }
-    const int64_t dst_row0 = a.target_offset + t * kTileRows;
+    // a tile never straddles two blocks in the scatter mode (block_size is a
+    // multiple of the tile), so its target rows stay contiguous
+    const int64_t dst_row0 =
+        a.block_dst != nullptr
+            ? a.block_dst[(t * kTileRows) / a.block_size] + (t * kTileRows) % a.block_size
+            : a.target_offset + t * kTileRows;
     scatter_tile<kLayout>(tile, rows, dst_row0, a.comp);
     if (a.gids != nullptr) {
       for (int r = tid; r < rows; r += kUnpackThreads) {
@@ -624,6 +630,9 @@ extern "C" int tgs_unpack_rows(const TgsUnpackArgs* a, void* stream) {
     TGS_CHECK_ARG(a->comp[c] != nullptr, "tgs_unpack_rows: component %d is NULL", c);
   TGS_CHECK_ARG(a->global_ids == nullptr || (a->block_ids != nullptr && a->block_size >= 1),
                 "tgs_unpack_rows: global id fill needs block_ids and block_size");
+  TGS_CHECK_ARG(a->block_dst == nullptr || (a->block_size >= kTileRows &&
+                                            a->block_size % kTileRows == 0),
+                "tgs_unpack_rows: block_dst needs block_size a multiple of %d", kTileRows);
   UnpackParams p;
   p.packed = a->packed;
   p.n_rows = a->n_rows;
@@ -635,6 +644,7 @@ extern "C" int tgs_unpack_rows(const TgsUnpackArgs* a, void* stream) {
   p.block_size = a->block_size;
   p.use_bulk = aligned16(a->packed) ? 1 : 0;
   p.err = a->err;
+  p.block_dst = a->block_dst;
   const int64_t n_tiles = ceil_div<int64_t>(a->n_rows, kTileRows);
   const int grid = static_cast<int>(
       std::min<int64_t>(n_tiles, static_cast<int64_t>(sm_count()) * kUnpackCtasPerSm));

@@ -107,10 +107,11 @@ WIDTHS = {"xyz": 3, "opacity": 1, "scaling": 3, "rotation": 4, "features_dc": 3,
           "features_rest": 45}
 NAMES = tuple(WIDTHS)
 ADAM_BYTES_PER_ROW = 59 * 4 * 7          # grad r + param r/w + m r/w + v r/w
-# DRAM bytes per updated row of resident_adam_kernel measured by ncu:
+# DRAM bytes per updated row of resident_adam_stream_kernel measured by ncu:
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the 256-slot
-# step (every input larger than L2) = 1654.8 MB over its 983,040 rows
-ADAM_TRAFFIC_BYTES_PER_ROW = 1683.3
+# step (every input larger than L2) = 1194.0 MB + 852.2 MB over its
+# 1,212,416 rows
+ADAM_TRAFFIC_BYTES_PER_ROW = 1687.7
 LRS = {"xyz": 1.6e-4, "opacity": 0.05, "scaling": 5e-3, "rotation": 1e-3, "features_dc": 2.5e-3,
        "features_rest": 1.25e-4}
 
@@ -134,6 +135,17 @@ def dist_setup():
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
+
+
+def _gather_all(obj, world: int) -> list:
+    """Every rank's `obj`, in rank order (a plain list at world 1)."""
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
 
 
 def allreduce_max(x: float, world: int) -> float:
@@ -1575,6 +1587,7 @@ def main(argv=None):
     # e2e leg through the Python API (host pool -> HBM -> host)
     e2e = None
     configs = {}
+    host_link = None
     try:
         if args.no_e2e:
             raise _Skipped("--no-e2e")
@@ -1615,6 +1628,12 @@ def main(argv=None):
         if world == 1 and not args.no_configs and args.host_tier == "cache":
             configs["materialization"] = bench_materialization(
                 api, device, n_e2e, iterations=args.materialize_iters)
+        elif world > 1 and args.host_tier == "cache":
+            # the box's host link with every rank copying at once (the e2e
+            # leg's H2D + D2H pattern, no compute): what the ranks share
+            barrier(world)
+            mine = link_probe(api, device, TURNOVER, TURNOVER)
+            host_link = _gather_all(mine, world)
         api.close()
         del api
     except _Skipped as why:
@@ -1660,7 +1679,8 @@ def main(argv=None):
                          "traffic": ADAM_TRAFFIC_BYTES_PER_ROW * (sum(adam_rows) / len(adam_rows)),
                          "traffic_note": "bytes per launch: ncu DRAM bytes per row of the "
                                          "256-slot capture x rows per launch",
-                         "kernel": "resident_adam_kernel",
+                         "kernel": "resident_adam_stream_kernel (+ resident_adam_kernel for "
+                                   "chunks that cannot stream)",
                          "algorithmic_bytes_per_row": ADAM_BYTES_PER_ROW,
                          "avg_launch_ms": adam_avg_ms, "peak_source": peak_kind,
                          "avg_launch_ms_max_over_ranks": adam_max_ms},
@@ -1671,6 +1691,12 @@ def main(argv=None):
             "cpu_baseline": base,
             "configs": configs or None,
         }
+        if host_link is not None:
+            line["host_link_all_ranks"] = {
+                "per_rank_concurrent_GBps": [r.get("concurrent_total_GBps") for r in host_link],
+                "box_total_GBps": sum(r.get("concurrent_total_GBps") or 0 for r in host_link),
+                "probe": "every rank at once: one DMA per block, TURNOVER blocks H2D and "
+                         "TURNOVER blocks D2H on two streams, page-locked host cache entries"}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -50,19 +50,36 @@ __global__ void __launch_bounds__(256) resident_count_kernel(
     int32_t* __restrict__ pos_count, int64_t* __restrict__ chunk_table,
     int32_t* __restrict__ err) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  // A warp covers the 32-row chunk i / 32 (256-thread blocks): it records in
-  // the chunk table whether the chunk can be streamed by bulk copies.
-  if (chunk_table != nullptr) {
-    const int lane = threadIdx.x & 31;
-    int64_t id = -1, sr = -1;
-    if (i < n) {
-      id = ids[i];
-      if (id >= 0 && id < param_rows) {
-        const int p = find_position(pos_start, pos_end, n_pos, block_size, id);
-        if (p < n_pos && __ldg(pos_start + p) <= id)
-          sr = static_cast<int64_t>(__ldg(pos_slot + p)) * block_size + (id - __ldg(pos_start + p));
+  // one lookup per row: position (and state row) of id, or an error code
+  int p = -1;
+  int64_t id = -1, sr = -1;
+  int code = TGS_DEV_OK;
+  if (i < n) {
+    id = ids[i];
+    if (id < 0 || id >= param_rows) {
+      code = TGS_DEV_ID_OUT_OF_RANGE;
+    } else if (i > 0 && __ldg(ids + i - 1) >= id) {
+      code = TGS_DEV_ID_NOT_SORTED;
+    } else {
+      p = find_position(pos_start, pos_end, n_pos, block_size, id);
+      if (p >= n_pos || __ldg(pos_start + p) > id) {
+        code = TGS_DEV_ID_NOT_RESIDENT;
+      } else {
+        sr = static_cast<int64_t>(__ldg(pos_slot + p)) * block_size + (id - __ldg(pos_start + p));
       }
     }
+    if (code != TGS_DEV_OK) {
+      report_error(err, code, i);
+      p = -1;
+      sr = -1;
+    }
+  }
+  // A warp covers the 32-row chunk i / 32 (256-thread blocks): it records in
+  // the chunk table whether the chunk can be streamed by bulk copies -- all
+  // 32 rows valid, ids and state rows both consecutive (every lane checks
+  // its own row), first id a multiple of 4.
+  if (chunk_table != nullptr) {
+    const int lane = threadIdx.x & 31;
     const unsigned full = 0xffffffffu;
     const int64_t id0 = __shfl_sync(full, id, 0);
     const int64_t sr0 = __shfl_sync(full, sr, 0);
@@ -75,21 +92,6 @@ __global__ void __launch_bounds__(256) resident_count_kernel(
     }
   }
   if (i >= n) return;
-  int p = -1;
-  const int64_t id = ids[i];
-  int code = TGS_DEV_OK;
-  if (id < 0 || id >= param_rows) {
-    code = TGS_DEV_ID_OUT_OF_RANGE;
-  } else if (i > 0 && __ldg(ids + i - 1) >= id) {
-    code = TGS_DEV_ID_NOT_SORTED;
-  } else {
-    p = find_position(pos_start, pos_end, n_pos, block_size, id);
-    if (p >= n_pos || __ldg(pos_start + p) > id) code = TGS_DEV_ID_NOT_RESIDENT;
-  }
-  if (code != TGS_DEV_OK) {
-    report_error(err, code, i);
-    p = -1;
-  }
   // Rows of a position are consecutive (ids ascending): its first row
   // subtracts its index and its last row adds its index + 1, so the count
   // costs two uncontended additions per position (an addition per row or per

@@ -900,7 +900,8 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
 // A chunk streams when its 32 ids and its 32 state rows both run
 // consecutively and its first id is a multiple of 4 (the count kernel's
 // chunk table): every chunk of a step that updates whole visible blocks. One
-// CTA per SM walks a contiguous range of chunks with three warp roles:
+// CTA per SM walks a contiguous range of chunks with three warp roles (two
+// loaders and two storers, each taking every other chunk):
 //   loader    brings a chunk's 32 state rows (16 KB), six parameter segments
 //             and six gradient segments (7.4 KB each; D': the first two
 //             contributions' segments, read from the senders' memory) into a
@@ -919,9 +920,14 @@ __global__ void __launch_bounds__(kApplyThreads, kSumMinBlocks)
 // ---------------------------------------------------------------------------
 constexpr int kTileRows = 32;
 constexpr int kStreamConsumerWarps = 16;
-constexpr int kLoaderWarp = kStreamConsumerWarps;
-constexpr int kStorerWarp = kStreamConsumerWarps + 1;
-constexpr int kStreamThreads = (kStreamConsumerWarps + 2) * 32;
+// two loader and two storer warps: each takes every other chunk, so the
+// per-chunk latency of issuing copies (and of waiting for the stores to
+// read a stage) is spread over two warps
+constexpr int kStreamLoaders = 2;
+constexpr int kStreamStorers = 2;
+constexpr int kFirstLoaderWarp = kStreamConsumerWarps;
+constexpr int kFirstStorerWarp = kStreamConsumerWarps + kStreamLoaders;
+constexpr int kStreamThreads = (kStreamConsumerWarps + kStreamLoaders + kStreamStorers) * 32;
 constexpr int kRowsPerConsumer = kTileRows / kStreamConsumerWarps;
 #ifndef TGS_STREAM_STAGES
 #define TGS_STREAM_STAGES 4
@@ -1111,8 +1117,13 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
   __syncthreads();
   if (s_skip != 0) return;
 
-  if (warp == kLoaderWarp) {
-    // ------------------------------- loader -------------------------------
+  static_assert(kStages % kStreamLoaders == 0 && kStages % kStreamStorers == 0,
+                "a stage must always be filled by the same loader and drained by the same storer");
+  if (warp >= kFirstLoaderWarp && warp < kFirstStorerWarp) {
+    // ------------------------------- loaders ------------------------------
+    // Loader w fills the chunks t = w, w + 2, ... of the CTA's sequence of
+    // accepted chunks (both loaders walk the same sequence).
+    const int w = warp - kFirstLoaderWarp;
     const int64_t n_chunks = a.n / kTileRows;  // only full chunks stream
     ChunkScan cs;
     cs.next = n_chunks * blockIdx.x / gridDim.x;
@@ -1123,74 +1134,72 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
     const int64_t B = a.block_size;
     const bool pow2B = (B & (B - 1)) == 0;
     const int shiftB = __ffsll(B) - 1;
-    // D': the segment of the last chunk looked at, cached (lane 0)
-    int64_t seg_lo = 0, seg_hi = -1, src_row[kGrads];
-    int32_t seg_cb = 0, seg_cn = 0, src_rank[kGrads];
-#pragma unroll
-    for (int jj = 0; jj < kGrads; ++jj) {
-      src_row[jj] = 0;
-      src_rank[jj] = 0;
-    }
+    // D': the segment of the last chunk looked at, cached per loader: its
+    // row range, its contributions, and (shared memory) the base pointers
+    // and source rows of the staged ones. Every check of a staged
+    // contribution (rank in range, base pointers 16-byte aligned, the
+    // segment's rows inside the sender's gradient rows, row offsets a
+    // multiple of 4) is made once per segment.
+    __shared__ const float* s_src[kStreamLoaders][kGrads][kNumComp];
+    __shared__ int64_t s_row[kStreamLoaders][kGrads];
+    int64_t seg_lo = 0, seg_hi = -1;
+    int32_t seg_cb = 0, seg_cn = 0, seg_ns = 0;
     bool seg_ok = false;
     bool failed = false;
-    int64_t t = 0;
-    for (;; ++t) {
+    int64_t accepted = 0;  // chunks of the sequence seen so far (both loaders')
+    int64_t t = w;
+    for (;; t += kStreamLoaders) {
       const int st = static_cast<int>(t % kStages);
       const uint32_t use = static_cast<uint32_t>(t / kStages);
       Stage& S = stages[st];
-      int64_t chunk, fid = 0, fsr = 0;
-      int32_t ns = 0;
-      int64_t seg_off = 0;
+      int64_t chunk = -1, fid = 0, fsr = 0;
+      // the t-th accepted chunk of the sequence
       while (true) {
         chunk = scan_next(cs, a.chunk_table, lane, fid, fsr);
-        if (chunk < 0 || !kSum) break;
-        // D': the chunk must lie in one segment whose first kGrads
-        // contributions can be bulk-copied (in range, 16-byte aligned)
-        int ok = 0;
-        if (lane == 0) {
+        if (chunk < 0) break;
+        if constexpr (kSum) {
           const int64_t row0 = chunk * kTileRows;
           if (row0 < seg_lo || row0 >= seg_hi) {
-            const int sg = upper_bound_i64(q->seg_begin + 1, q->n_seg, row0);
-            seg_ok = false;
-            seg_hi = -1;
-            if (sg < q->n_seg && __ldg(q->seg_begin + sg) <= row0) {
-              seg_lo = __ldg(q->seg_begin + sg);
-              seg_hi = __ldg(q->seg_begin + sg + 1);
-              seg_cb = static_cast<int32_t>(__ldg(q->contrib_offsets + sg));
-              seg_cn = static_cast<int32_t>(__ldg(q->contrib_offsets + sg + 1)) - seg_cb;
-              seg_ok = seg_cn >= 1;
+            if (lane == 0) {
+              const int sg = upper_bound_i64(q->seg_begin + 1, q->n_seg, row0);
+              seg_ok = false;
+              seg_hi = -1;
+              if (sg < q->n_seg && __ldg(q->seg_begin + sg) <= row0) {
+                seg_lo = __ldg(q->seg_begin + sg);
+                seg_hi = __ldg(q->seg_begin + sg + 1);
+                seg_cb = static_cast<int32_t>(__ldg(q->contrib_offsets + sg));
+                seg_cn = static_cast<int32_t>(__ldg(q->contrib_offsets + sg + 1)) - seg_cb;
+                seg_ns = seg_cn < kGrads ? seg_cn : kGrads;
+                seg_ok = seg_cn >= 1;
 #pragma unroll
-              for (int jj = 0; jj < kGrads; ++jj) {
-                if (jj >= seg_cn) break;
-                const int r = __ldg(q->contrib_rank + seg_cb + jj);
-                src_rank[jj] = r;
-                src_row[jj] = __ldg(q->contrib_row + seg_cb + jj);
-                if (r < 0 || r >= q->n_ranks) {
-                  seg_ok = false;
-                  continue;
+                for (int jj = 0; jj < kGrads; ++jj) {
+                  if (jj >= seg_ns) break;
+                  const int r = __ldg(q->contrib_rank + seg_cb + jj);
+                  const int64_t row = __ldg(q->contrib_row + seg_cb + jj);
+                  s_row[w][jj] = row;
+                  if (r < 0 || r >= q->n_ranks || row < 0 || ((row - seg_lo) & 3) != 0 ||
+                      row + (seg_hi - seg_lo) > __ldg(q->grad_rows + r)) {
+                    seg_ok = false;
+                    continue;
+                  }
+                  for (int c = 0; c < kNumComp; ++c) {
+                    const float* ptr = q->grad_src[r * kNumComp + c];
+                    if (!aligned16(ptr)) seg_ok = false;
+                    s_src[w][jj][c] = ptr;
+                  }
                 }
-                for (int c = 0; c < kNumComp; ++c)
-                  if (!aligned16(q->grad_src[r * kNumComp + c])) seg_ok = false;
               }
             }
+            seg_lo = __shfl_sync(full, seg_lo, 0);
+            seg_hi = __shfl_sync(full, seg_hi, 0);
+            seg_ok = __shfl_sync(full, seg_ok ? 1 : 0, 0) != 0;
+            seg_cb = __shfl_sync(full, seg_cb, 0);
+            seg_cn = __shfl_sync(full, seg_cn, 0);
+            seg_ns = __shfl_sync(full, seg_ns, 0);
           }
-          if (seg_ok && row0 + kTileRows <= seg_hi) {
-            ok = 1;
-#pragma unroll
-            for (int jj = 0; jj < kGrads; ++jj) {
-              if (jj >= seg_cn) break;
-              const int64_t srow = src_row[jj] + (row0 - seg_lo);
-              if (srow < 0 || (srow & 3) != 0 ||
-                  srow + kTileRows > __ldg(q->grad_rows + src_rank[jj]))
-                ok = 0;
-            }
-          }
+          if (!(seg_ok && row0 + kTileRows <= seg_hi)) continue;  // not streamable
         }
-        if (__shfl_sync(full, ok, 0) != 0) {
-          ns = __shfl_sync(full, seg_cn < kGrads ? seg_cn : kGrads, 0);
-          seg_off = __shfl_sync(full, chunk * kTileRows - seg_lo, 0);
-          break;
-        }
+        if (accepted++ == t) break;  // the other loader's chunks are skipped
       }
       // the chunk's row scales start loading before the wait for the stage
       float2 bb = make_float2(0.f, 0.f);
@@ -1215,29 +1224,30 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
         mbar_arrive(&full_bar[st]);  // completes the phase without bytes
         break;
       }
+      const int ns = kSum ? seg_ns : 1;
+      const int64_t seg_off = kSum ? chunk * kTileRows - seg_lo : 0;
       if (lane == 0) {
         S.desc.chunk = chunk;
         S.desc.first_id = fid;
         S.desc.first_sr = fsr;
         S.desc.ns = ns;
-        const uint32_t bytes = kStateTileBytes + kRowTileBytes * (1 + (kSum ? ns : 1));
-        mbar_expect_tx(&full_bar[st], bytes);
+        S.desc.cb = seg_cb;
+        S.desc.cn = seg_cn;
+        S.desc.seg_off = seg_off;
+        mbar_expect_tx(&full_bar[st], kStateTileBytes + kRowTileBytes * (1 + ns));
         bulk_g2s(S.state, a.state + fsr * (TGS_STATE_ROW_FLOATS / 4), kStateTileBytes,
                  &full_bar[st]);
         load_row_tile(S.param, a.param, fid, &full_bar[st]);
         if constexpr (kSum) {
-          S.desc.cb = seg_cb;
-          S.desc.cn = seg_cn;
-          S.desc.seg_off = seg_off;
 #pragma unroll
           for (int jj = 0; jj < kGrads; ++jj) {
             if (jj >= ns) break;
-            const float* const* src = q->grad_src + src_rank[jj] * kNumComp;
-            const int64_t srow = src_row[jj] + seg_off;
+            const int64_t srow = s_row[w][jj] + seg_off;
 #pragma unroll
             for (int c = 0; c < kNumComp; ++c)
-              bulk_g2s(S.grad[jj] + kTileRows * unified_offset(c), src[c] + srow * comp_width(c),
-                       kTileRows * comp_width(c) * 4, &full_bar[st]);
+              bulk_g2s(S.grad[jj] + kTileRows * unified_offset(c),
+                       s_src[w][jj][c] + srow * comp_width(c), kTileRows * comp_width(c) * 4,
+                       &full_bar[st]);
           }
         } else {
           load_row_tile(S.grad[0], a.grad, chunk * kTileRows, &full_bar[st]);
@@ -1252,17 +1262,19 @@ __device__ void stream_kernel_body(const ResidentApplyParams& a, const ResidentS
     }
     if (failed && lane == 0) {
       report_error(err, TGS_DEV_WAIT_TIMEOUT, t);
-      // loads still in flight land before the CTA may exit
-      for (int64_t j = t - kStages; j < t; ++j)
+      // this loader's loads still in flight land before the CTA may exit
+      for (int64_t j = t - kStages; j < t; j += kStreamLoaders)
         if (j >= 0)
           (void)mbar_wait_bounded(&full_bar[j % kStages], static_cast<uint32_t>(j / kStages) & 1u);
     }
     return;
   }
 
-  if (warp == kStorerWarp) {
-    // ------------------------------- storer -------------------------------
-    for (int64_t t = 0;; ++t) {
+  if (warp >= kFirstStorerWarp) {
+    // ------------------------------- storers ------------------------------
+    // Storer w drains the chunks t = w, w + 2, ...
+    const int w = warp - kFirstStorerWarp;
+    for (int64_t t = w;; t += kStreamStorers) {
       const int st = static_cast<int>(t % kStages);
       const uint32_t par = static_cast<uint32_t>(t / kStages) & 1u;
       Stage& S = stages[st];

@@ -112,6 +112,9 @@ ADAM_BYTES_PER_ROW = 59 * 4 * 7          # grad r + param r/w + m r/w + v r/w
 # step (every input larger than L2) = 1194.0 MB + 852.2 MB over its
 # 1,212,416 rows
 ADAM_TRAFFIC_BYTES_PER_ROW = 1687.7
+# NVLink bandwidth per direction of one B200 measured on this box type (peer
+# copy), the denominator of the parameter gather's fraction
+NVLINK_GBPS = 770.0
 LRS = {"xyz": 1.6e-4, "opacity": 0.05, "scaling": 5e-3, "rotation": 1e-3, "features_dc": 2.5e-3,
        "features_rest": 1.25e-4}
 
@@ -505,6 +508,10 @@ class DeviceStep:
                 self.send_buf = torch.empty((send_max * B, 59), device=device)
                 self.recv_buf = torch.empty((recv_max * B, 59), device=device)
             self.exchange_rows = 0
+            # updated parameters reach the ranks that render the blocks next
+            from tidegs_b200.sharded import PeerParamGather
+
+            self.param_gather = PeerParamGather(self.arena, B, device)
         self.adam_ms = []
         self.updated_rows = []
         torch.cuda.synchronize()
@@ -730,9 +737,11 @@ class DeviceStep:
         self._phase("tables")
         return int(ids.numel())
 
+    param_gather = None
+
     def close(self):
         """Releases the peer mappings (collective over the ranks)."""
-        for attr in ("peer", "pull"):
+        for attr in ("peer", "pull", "param_gather"):
             obj = getattr(self, attr)
             if obj is not None:
                 obj.close()
@@ -840,6 +849,88 @@ class DeviceStep:
                 "contributions": sum(c for _, _, c in counts) // max(1, W),
                 "oracle": "oracle/resident_adam.py kernel_update on the rank-order sum of "
                           "the contributions (CPU, after the timed region)"}
+
+    def measure_param_gather(self, k: int, iters: int = 10, warmup: int = 2,
+                             sample: int = 2, rows: int = 256) -> dict:
+        """Time, after the timed region, how long the parameters updated in
+        step k-1 take to reach the ranks that render them in step k: each
+        rank copies every block it renders at step k that another rank owns
+        from the owner's arena (PeerParamGather: barrier, one bulk-copy
+        launch per owner over NVLink, barrier). Blocks a rank owns are read
+        in place. Then `sample` gathered blocks per rank are compared bit for
+        bit with their owner's rows. Collective: every rank calls it."""
+        import torch.distributed as dist
+
+        from tidegs_b200.sharded import exchange_arena_tables, make_gather_plan
+
+        W, me = self.world, self.sched.rank
+        tables = exchange_arena_tables(self.arena_block, self.device)
+        plan = make_gather_plan(self.trace.vis[k][me], tables, W, me, B)
+        n = int(plan.remote_blocks.size)
+        render = {nm: torch.empty((max(1, n) * B, w), device=self.device)
+                  for nm, w in WIDTHS.items()}
+        dev_tables = self.param_gather.tables(plan)
+        for _ in range(warmup):
+            self.param_gather.gather(render, plan, dev_tables, err=self.err)
+        torch.cuda.synchronize()
+        copy_ev, full_ev = [], []
+        for _ in range(iters):
+            f0, c0, c1, f1 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+            f0.record()
+            self.param_gather.barrier()
+            c0.record()
+            self.param_gather.launch(render, plan, dev_tables, err=self.err)
+            c1.record()
+            self.param_gather.barrier()
+            f1.record()
+            copy_ev.append((c0, c1))
+            full_ev.append((f0, f1))
+        torch.cuda.synchronize()
+        copy_ms = sum(a.elapsed_time(b) for a, b in copy_ev) / iters
+        full_ms = sum(a.elapsed_time(b) for a, b in full_ev) / iters
+        # bit-exact check of sampled blocks against their owners' rows
+        rng = np.random.default_rng(99 + me)
+        pick = np.sort(rng.choice(n, min(sample, n), replace=False)) if n else np.zeros(0, int)
+        asks = [(int(plan.owner[i]), int(plan.src_slot[i]),
+                 int(rng.integers(0, B - rows + 1))) for i in pick]
+        got = [np.concatenate([render[nm][i * B + r0:i * B + r0 + rows].cpu().numpy()
+                               for nm in NAMES], axis=1) for i, (_, _, r0) in zip(pick, asks)]
+        all_asks = [None] * W
+        dist.all_gather_object(all_asks, asks)
+        answers = {}
+        for r, lst in enumerate(all_asks):
+            for j, (o, slot, r0) in enumerate(lst):
+                if o == me:
+                    lo = slot * B + r0
+                    answers[(r, j)] = np.concatenate(
+                        [self.arena[nm][lo:lo + rows].cpu().numpy() for nm in NAMES], axis=1)
+        all_answers = [None] * W
+        dist.all_gather_object(all_answers, answers)
+        ok = True
+        for j, g in enumerate(got):
+            want = next(a[(me, j)] for a in all_answers if (me, j) in a)
+            ok = ok and np.array_equal(g.view(np.uint32), want.view(np.uint32))
+        del render
+        per_rank = [None] * W
+        dist.all_gather_object(per_rank, (n, copy_ms, full_ms, len(got), bool(ok),
+                                          int(plan.missing.size)))
+        nbytes = max(x[0] for x in per_rank) * B * 59 * 4
+        copy_max = max(x[1] for x in per_rank)
+        return {"step": k, "iters": iters,
+                "remote_blocks_per_rank": [x[0] for x in per_rank],
+                "bytes_per_rank_max": nbytes,
+                "copy_ms_max_over_ranks": copy_max,
+                "with_barriers_ms_max_over_ranks": max(x[2] for x in per_rank),
+                "GBps_per_rank": nbytes / (copy_max / 1e3) / 1e9,
+                "nvlink_frac": nbytes / (copy_max / 1e3) / 1e9 / NVLINK_GBPS,
+                "nvlink_peak_GBps": NVLINK_GBPS,
+                "missing_blocks": sum(x[5] for x in per_rank),
+                "checked_blocks": sum(x[3] for x in per_rank),
+                "bit_exact": all(x[4] for x in per_rank),
+                "how": "PeerParamGather: every block a rank renders next and another rank "
+                       "owns, copied whole from the owner's arena slot over NVLink "
+                       "(tgs_copy_blocks, bulk copies, one launch per owner); not part of "
+                       "the timed step"}
 
     def adam_stats(self):
         ms = [e0.elapsed_time(e1) for e0, e1, _ in self.adam_ms]
@@ -1531,7 +1622,7 @@ def main(argv=None):
     host_blocks = Schedule(rank, world).touched_blocks(n_e2e + 1)
     args.host_tier = plan_host_tier(world, args.host_tier, args.pool_blocks,
                                     host_blocks.size, host_memory_limit())
-    n_trace = max(args.warmup + args.steps + 4, n_e2e + 1)
+    n_trace = max(args.warmup + args.steps + 6, n_e2e + 1)
     trace = ScheduleTrace(world, rank, n_trace)
     sched = Schedule(rank, world)
     dev = DeviceStep(device, sched, trace, world=world, exchange=args.exchange)
@@ -1569,6 +1660,7 @@ def main(argv=None):
     launches = _lib.launch_counter["kernels"] - launches0
     # result check of the same step, outside the timed region
     parity = dev.parity_check(next_k)
+    param_gather = dev.measure_param_gather(next_k + 1) if world > 1 else None
     ms = start.elapsed_time(end)
     ms_max = allreduce_max(ms, world)
     total_rows = rows * world
@@ -1687,6 +1779,7 @@ def main(argv=None):
             "clocks": clock_info,
             "gpu_launches": launches,
             "parity": parity,
+            "param_gather": param_gather,
             "e2e": e2e,
             "cpu_baseline": base,
             "configs": configs or None,

@@ -89,3 +89,22 @@ def test_random_turnover_draws_non_resident_blocks():
 def test_memory_limit_is_read_the_same_way_on_every_call():
     a, b = bench.host_memory_limit(), bench.host_memory_limit()
     assert a == b and a > 0
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_every_rendered_block_is_resident_at_its_owner(world):
+    """The parameter gather needs no host-tier read: after step k's turnover
+    every block a rank renders at step k+1 sits in its owner's slots."""
+    from tidegs_b200.sharded import make_gather_plan
+
+    traj = bench.Trajectory(world)
+    scheds = [bench.Schedule(r, world, traj) for r in range(world)]
+    for k in range(12):
+        for sc in scheds:
+            ev, inc, _ = sc.turnover(k)
+            sc.slot_block[ev] = inc
+        tables = [sc.slot_block for sc in scheds]
+        for me in range(world):
+            plan = make_gather_plan(traj.rendered(k + 1, me), tables, world, me, bench.B)
+            assert plan.missing.size == 0
+            assert plan.remote_blocks.size + plan.own_blocks.size == traj.rendered(k + 1, me).size

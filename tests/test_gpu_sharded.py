@@ -11,7 +11,11 @@ emulated here with every "peer" buffer on one GPU, and over CUDA IPC between
 two GPUs in test_two_gpu_peer_push. The pull path (PeerGradPull +
 GPUResidentAdam.step_pulled: the owner's update kernel sums the senders'
 gradients itself) must equal exchange + sum + plain update bit for bit:
-emulated ranks here, two GPUs in test_two_gpu_pull_sum_adam."""
+emulated ranks here, two GPUs in test_two_gpu_pull_sum_adam. The parameter
+gather (PeerParamGather: updated blocks copied from their owners' arenas to
+the ranks that render them next) must deliver every remote block's owner rows
+bit for bit: emulated owners on one GPU, an owner on a second GPU in one
+process, and two processes over CUDA IPC in test_two_gpu_param_gather."""
 import os
 import socket
 
@@ -22,8 +26,9 @@ import torch.multiprocessing as mp
 
 from oracle import blocks as ob
 from tidegs_b200 import _lib, _ops
-from tidegs_b200.sharded import (BlockGradExchange, PeerGradExchange, PeerGradPull, make_plan,
-                                 owner_of)
+from tidegs_b200.sharded import (BlockGradExchange, PeerGradExchange, PeerGradPull,
+                                 PeerParamGather, exchange_arena_tables, make_gather_plan,
+                                 make_plan, owner_of)
 
 pytestmark = pytest.mark.gpu
 
@@ -516,6 +521,138 @@ def test_two_gpu_pull_sum_adam():
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_pull_worker, args=(r, world, port, vis_steps, B, nb, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert results == {0: True, 1: True}
+
+
+def _gather_arenas(world, slots, B, pool, seed, devices):
+    """Per owner: arena table (block per slot, some free) and seeded arena
+    component tensors on devices[owner]."""
+    rng = np.random.default_rng(seed)
+    tables, arenas = [], []
+    for o in range(world):
+        owned = np.arange(o, pool, world, dtype=np.int64)
+        held = rng.choice(owned, min(owned.size, slots - 3), replace=False)
+        t = np.full(slots, -1, np.int64)
+        t[rng.choice(slots, held.size, replace=False)] = held
+        tables.append(t)
+        gen = torch.Generator(device=devices[o]).manual_seed(seed + o)
+        arenas.append({n: torch.randn((slots * B, w), device=devices[o], generator=gen)
+                       for n, w in ob.WIDTHS.items()})
+    return tables, arenas
+
+
+def _check_gathered(plan, arenas, render, B):
+    for i, (o, sl) in enumerate(zip(plan.owner, plan.src_slot)):
+        for n in NAMES:
+            want = arenas[o][n][sl * B:(sl + 1) * B].to(render[n].device)
+            assert torch.equal(render[n][i * B:(i + 1) * B], want), (i, n)
+
+
+@pytest.mark.parametrize("W,B", [(3, 64), (4, 6)])
+def test_param_gather_emulated_owners_bit_exact(W, B):
+    """Owners emulated on one GPU; B = 6 puts odd slots off the 16-byte
+    boundary, so the kernel's plain-copy path runs beside the bulk one."""
+    slots, pool = 24, 120
+    tables, arenas = _gather_arenas(W, slots, B, pool, 5 + W, ["cuda:0"] * W)
+    rng = np.random.default_rng(W)
+    for me in range(W):
+        plan = make_gather_plan(rng.choice(pool, 50, replace=False), tables, W, me, B)
+        assert plan.remote_blocks.size > 0
+        gather = PeerParamGather.in_process(arenas, me, B, "cuda:0")
+        render = {n: torch.full((plan.remote_blocks.size * B, w), float("nan"), device="cuda:0")
+                  for n, w in ob.WIDTHS.items()}
+        err = torch.zeros(4, dtype=torch.int32, device="cuda:0")
+        assert gather.gather(render, plan, err=err) == plan.remote_blocks.size * B
+        torch.cuda.synchronize()
+        assert int(err[0].item()) == 0
+        _check_gathered(plan, arenas, render, B)
+        gather.close()
+
+
+def test_param_gather_rejects_small_render_rows_and_foreign_plans():
+    W, B = 2, 16
+    tables, arenas = _gather_arenas(W, 8, B, 40, 3, ["cuda:0"] * W)
+    plan = make_gather_plan(np.arange(40), tables, W, 0, B)
+    gather = PeerParamGather.in_process(arenas, 0, B, "cuda:0")
+    small = {n: torch.empty(((plan.remote_blocks.size - 1) * B, w), device="cuda:0")
+             for n, w in ob.WIDTHS.items()}
+    with pytest.raises(RuntimeError, match="the plan needs"):
+        gather.launch(small, plan)
+    other = make_gather_plan(np.arange(40), tables, W, 1, B)
+    with pytest.raises(ValueError, match="another world/rank"):
+        gather.tables(other)
+
+
+def test_param_gather_reads_an_owner_on_another_gpu_in_process():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    W, B = 2, 256
+    tables, arenas = _gather_arenas(W, 16, B, 64, 9, ["cuda:0", "cuda:1"])
+    plan = make_gather_plan(np.arange(64), tables, W, 0, B)
+    gather = PeerParamGather.in_process(arenas, 0, B, "cuda:0")
+    render = {n: torch.empty((plan.remote_blocks.size * B, w), device="cuda:0")
+              for n, w in ob.WIDTHS.items()}
+    gather.gather(render, plan)
+    torch.cuda.synchronize()
+    _check_gathered(plan, arenas, render, B)
+
+
+def _param_gather_worker(rank, world, port, B, slots, pool, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    gather = None
+    try:
+        dev = torch.device("cuda", rank)
+        # every rank rebuilds all arenas' contents on the CPU to check against
+        tables, arenas_cpu = _gather_arenas(world, slots, B, pool, 21, ["cpu"] * world)
+        arena = {n: t.to(dev) for n, t in arenas_cpu[rank].items()}
+        gather = PeerParamGather(arena, B, dev)
+        got_tables = exchange_arena_tables(tables[rank], dev)
+        ok = all(np.array_equal(a, b) for a, b in zip(got_tables, tables))
+        want = np.random.default_rng(100 + rank).choice(pool, pool // 2, replace=False)
+        plan = make_gather_plan(want, got_tables, world, rank, B)
+        render = {n: torch.empty((max(1, plan.remote_blocks.size) * B, w), device=dev)
+                  for n, w in ob.WIDTHS.items()}
+        err = torch.zeros(4, dtype=torch.int32, device=dev)
+        for _ in range(2):
+            gather.gather(render, plan, err=err)
+        torch.cuda.synchronize()
+        ok = ok and int(err[0].item()) == 0 and plan.remote_blocks.size > 0
+        for i, (o, sl) in enumerate(zip(plan.owner, plan.src_slot)):
+            for n in NAMES:
+                ok = ok and torch.equal(render[n][i * B:(i + 1) * B].cpu(),
+                                        arenas_cpu[o][n][sl * B:(sl + 1) * B])
+        q.put((rank, bool(ok)))
+    finally:
+        if gather is not None:
+            gather.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_param_gather():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world, B, slots, pool = 2, 1024, 24, 60
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_param_gather_worker, args=(r, world, port, B, slots, pool, q))
              for r in range(world)]
     for p in procs:
         p.start()

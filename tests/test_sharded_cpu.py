@@ -10,7 +10,8 @@ import torch
 import torch.multiprocessing as mp
 
 from oracle import blocks as ob
-from tidegs_b200.sharded import BlockGradExchange, make_plan, owner_of
+from tidegs_b200.sharded import (BlockGradExchange, exchange_arena_tables, make_gather_plan,
+                                 make_plan, owner_of)
 
 
 def test_plan_groups_by_owner_and_keeps_sender_order():
@@ -162,3 +163,106 @@ def test_two_rank_gloo_exchange_equals_single_process_sum():
                 col = ob.UNIFIED[name]
                 np.testing.assert_array_equal(np.asarray(got[name], np.float32)[k * B:(k + 1) * B],
                                               s[:, col:col + w])
+
+
+def _arena(world, owner, slots, pool, rng):
+    """A rank's arena table: `slots` slots, some free, holding blocks it owns."""
+    owned = np.arange(owner, pool, world, dtype=np.int64)
+    held = rng.choice(owned, min(owned.size, slots - slots // 4), replace=False)
+    table = np.full(slots, -1, np.int64)
+    table[rng.choice(slots, held.size, replace=False)] = held
+    return table
+
+
+@pytest.mark.parametrize("W", [2, 3, 8])
+def test_gather_plan_splits_own_remote_and_missing(W):
+    rng = np.random.default_rng(W)
+    pool, slots = 300, 40
+    arenas = [_arena(W, o, slots, pool, rng) for o in range(W)]
+    for me in range(W):
+        want = rng.choice(pool, 60, replace=False)
+        plan = make_gather_plan(want, arenas, W, me, 16)
+        got = np.concatenate([plan.own_blocks, plan.remote_blocks, plan.missing])
+        assert np.array_equal(np.sort(got), np.unique(want))
+        assert np.all(plan.own_blocks % W == me)
+        assert np.all(arenas[me][plan.own_slots] == plan.own_blocks)
+        assert np.all(np.diff(plan.remote_blocks) > 0)
+        assert np.all(plan.owner == plan.remote_blocks % W) and np.all(plan.owner != me)
+        for b, o, sl in zip(plan.remote_blocks, plan.owner, plan.src_slot):
+            assert arenas[o][sl] == b
+        for b in plan.missing:
+            assert b not in arenas[b % W]
+        assert plan.owner_order() == [(me + d) % W for d in range(1, W)]
+
+
+def test_gather_plan_rejects_an_arena_that_breaks_ownership():
+    good = np.array([0, 2, -1, 4], np.int64)
+    with pytest.raises(ValueError, match="does not own"):
+        make_gather_plan([1], [good, np.array([1, 2, -1], np.int64)], 2, 0, 4)
+    with pytest.raises(ValueError, match="twice"):
+        make_gather_plan([1], [good, np.array([1, 3, 1], np.int64)], 2, 0, 4)
+    with pytest.raises(ValueError, match="one arena table per rank"):
+        make_gather_plan([1], [good], 2, 0, 4)
+
+
+def _block_rows(b, B):
+    """Deterministic parameter rows of block b: [B, 59] UNIFIED."""
+    return np.random.default_rng(50_000 + int(b)).standard_normal((B, 59)).astype(np.float32)
+
+
+def _gather_worker(rank, world, port, arenas, want, B, result_q):
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        mine = arenas[rank]
+        data = np.zeros((mine.size * B, 59), np.float32)
+        for s, b in enumerate(mine):
+            if b >= 0:
+                data[s * B:(s + 1) * B] = _block_rows(b, B)
+        tables = exchange_arena_tables(mine[: mine.size - rank], "cpu")  # ragged tables
+        plan = make_gather_plan(want[rank], tables, world, rank, B)
+        # the copies PeerParamGather makes, with every rank's arena fetched here
+        all_data = [torch.empty((a.size * B, 59)) for a in arenas]
+        dist.all_gather(all_data, torch.from_numpy(data))
+        render = np.zeros((plan.remote_blocks.size * B, 59), np.float32)
+        for i, (o, sl) in enumerate(zip(plan.owner, plan.src_slot)):
+            render[i * B:(i + 1) * B] = all_data[o].numpy()[sl * B:(sl + 1) * B]
+        ok = all(np.array_equal(render[i * B:(i + 1) * B], _block_rows(b, B))
+                 for i, b in enumerate(plan.remote_blocks))
+        ok = ok and all(np.array_equal(t, a[: a.size - r])
+                        for r, (t, a) in enumerate(zip(tables, arenas)))
+        result_q.put((rank, ok, plan.remote_blocks.tolist(), plan.missing.tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_param_gather_host_logic():
+    """Arena tables all-gathered over gloo (ragged lengths) give every rank a
+    gather plan whose copies deliver each remote block's owner rows."""
+    world, B, pool, slots = 2, 4, 60, 24
+    rng = np.random.default_rng(11)
+    arenas = [_arena(world, o, slots, pool, rng) for o in range(world)]
+    want = [np.sort(rng.choice(pool, 25, replace=False)) for _ in range(world)]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, arenas, want, B, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        rank, ok, remote, missing = q.get(timeout=120)
+        results[rank] = (ok, remote, missing)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        ok, remote, missing = results[r]
+        assert ok
+        tables = [a[: a.size - o] for o, a in enumerate(arenas)]
+        assert remote == [int(b) for b in want[r] if b % world != r and b in tables[b % world]]
+        assert missing == [int(b) for b in want[r] if b not in tables[b % world]]

@@ -371,6 +371,81 @@ class PeerGradExchange:
         self._opened, self._own = [], []
 
 
+def _map_peer_components(comps: Mapping[str, torch.Tensor], device: torch.device, group,
+                         world: int, rank: int, who: str):
+    """Exports this rank's six [rows, width] component tensors (tgs_peer_export:
+    IPC handle of the containing allocation + the tensor's offset in it) and
+    maps every other rank's (collective over `group`). Returns the [world, 6]
+    table of component pointers valid in this process, each rank's row count
+    and the opened allocations {handle: base} (closed by the caller)."""
+    import ctypes
+
+    import torch.distributed as dist
+
+    own_ptrs = _ops._comp_ptrs(comps, who)
+    rows = min(int(comps[n].shape[0]) for n in _ops.COMPONENTS)
+    for n, w in _ops.WIDTHS.items():
+        t = comps[n]
+        if t.device != device or t.numel() != int(t.shape[0]) * w:
+            raise RuntimeError(f"{who}: component {n} must be [rows, {w}] on {device}")
+    n_comp = len(_ops.COMPONENTS)
+    table = np.zeros((world, n_comp), np.int64)
+    rows_of = np.zeros(world, np.int64)
+    opened: Dict[bytes, int] = {}
+    if world == 1:
+        table[0] = own_ptrs
+        rows_of[0] = rows
+        return table, rows_of, opened
+    rec = bytearray()
+    with torch.cuda.device(device):
+        for ptr in own_ptrs:
+            h = _lib.PeerHandle()
+            off = ctypes.c_int64()
+            _lib.call("tgs_peer_export", ptr, ctypes.byref(h), ctypes.byref(off))
+            rec += bytes(h.bytes) + int(off.value).to_bytes(8, "little", signed=True)
+        rec += rows.to_bytes(8, "little", signed=True)
+        mine = torch.tensor(list(rec), dtype=torch.uint8, device=device)
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine, group=group)
+        step = 64 + 8
+        for r, t in enumerate(gathered):
+            raw = bytes(t.cpu().tolist())
+            rows_of[r] = int.from_bytes(raw[n_comp * step:n_comp * step + 8], "little",
+                                        signed=True)
+            if r == rank:
+                table[r] = own_ptrs
+                continue
+            for c in range(n_comp):
+                key = raw[c * step:c * step + 64]
+                off = int.from_bytes(raw[c * step + 64:(c + 1) * step], "little", signed=True)
+                if key not in opened:
+                    h = _lib.PeerHandle()
+                    ctypes.memmove(h.bytes, key, 64)
+                    base = ctypes.c_void_p()
+                    _lib.call("tgs_peer_buffer_open", ctypes.byref(h), ctypes.byref(base))
+                    opened[key] = int(base.value)
+                table[r, c] = opened[key] + off
+    return table, rows_of, opened
+
+
+def _close_peer_mappings(opened: Dict[bytes, int], device: torch.device, group,
+                         collective: bool) -> None:
+    """Unmaps what _map_peer_components opened (collective: every rank calls
+    it with nothing in flight that reads a peer)."""
+    torch.cuda.synchronize(device)
+    if collective:
+        import torch.distributed as dist
+
+        dist.barrier(group=group)
+    with torch.cuda.device(device):
+        for base in opened.values():
+            _lib.call("tgs_peer_buffer_close", base)
+    if collective:
+        import torch.distributed as dist
+
+        dist.barrier(group=group)
+
+
 class PeerGradPull:
     """Owner-side gradient reduction fused into the resident Adam update.
 
@@ -393,8 +468,6 @@ class PeerGradPull:
     """
 
     def __init__(self, grads: Mapping[str, torch.Tensor], block_size: int, device, group=None):
-        import ctypes
-
         import torch.distributed as dist
 
         self.device = _lib.require_cuda(device, "PeerGradPull")
@@ -405,50 +478,8 @@ class PeerGradPull:
         self.rank = dist.get_rank(group) if dist_on else 0
         if self.world > _lib.MAX_PEERS:
             raise RuntimeError(f"PeerGradPull supports at most {_lib.MAX_PEERS} ranks")
-        own_ptrs = _ops._comp_ptrs(grads, "PeerGradPull")
-        rows = min(int(grads[n].shape[0]) for n in _ops.COMPONENTS)
-        for n, w in _ops.WIDTHS.items():
-            t = grads[n]
-            if t.device != self.device or t.numel() != int(t.shape[0]) * w:
-                raise RuntimeError(f"PeerGradPull: gradient {n} must be [rows, {w}] on {self.device}")
-        rec = bytearray()
-        with torch.cuda.device(self.device):
-            for ptr in own_ptrs:
-                h = _lib.PeerHandle()
-                off = ctypes.c_int64()
-                _lib.call("tgs_peer_export", ptr, ctypes.byref(h), ctypes.byref(off))
-                rec += bytes(h.bytes) + int(off.value).to_bytes(8, "little", signed=True)
-            rec += rows.to_bytes(8, "little", signed=True)
-            n_comp = len(_ops.COMPONENTS)
-            table = np.zeros((self.world, n_comp), np.int64)
-            self.rows = np.zeros(self.world, np.int64)
-            self._opened: Dict[bytes, int] = {}
-            if self.world == 1:
-                table[0] = own_ptrs
-                self.rows[0] = rows
-            else:
-                mine = torch.tensor(list(rec), dtype=torch.uint8, device=self.device)
-                gathered = [torch.empty_like(mine) for _ in range(self.world)]
-                dist.all_gather(gathered, mine, group=group)
-                step = 64 + 8
-                for r, t in enumerate(gathered):
-                    raw = bytes(t.cpu().tolist())
-                    self.rows[r] = int.from_bytes(raw[n_comp * step:n_comp * step + 8], "little",
-                                                  signed=True)
-                    if r == self.rank:
-                        table[r] = own_ptrs
-                        continue
-                    for c in range(n_comp):
-                        key = raw[c * step:c * step + 64]
-                        off = int.from_bytes(raw[c * step + 64:(c + 1) * step], "little",
-                                             signed=True)
-                        if key not in self._opened:
-                            h = _lib.PeerHandle()
-                            ctypes.memmove(h.bytes, key, 64)
-                            base = ctypes.c_void_p()
-                            _lib.call("tgs_peer_buffer_open", ctypes.byref(h), ctypes.byref(base))
-                            self._opened[key] = int(base.value)
-                        table[r, c] = self._opened[key] + off
+        table, self.rows, self._opened = _map_peer_components(
+            grads, self.device, group, self.world, self.rank, "PeerGradPull")
         self._finish(table, {"own": dict(grads)}, collective=self.world > 1)
 
     @classmethod
@@ -546,17 +577,231 @@ class PeerGradPull:
         if self._closed:
             return
         self._closed = True
-        torch.cuda.synchronize(self.device)
-        if self._collective:
-            import torch.distributed as dist
-
-            dist.barrier(group=self.group)
-        with torch.cuda.device(self.device):
-            for base in self._opened.values():
-                _lib.call("tgs_peer_buffer_close", base)
+        _close_peer_mappings(self._opened, self.device, self.group, self._collective)
         self._opened = {}
+        self._grads = {}
+
+
+@dataclass
+class GatherPlan:
+    """Where a renderer finds the current parameters of the blocks it renders
+    next. Blocks this rank owns are read in place from its own arena; every
+    other one is copied whole from its owner's arena slot into the render
+    rows: remote_blocks[i] lands in rows [i * block_size, (i + 1) *
+    block_size) of every component."""
+    world: int
+    rank: int
+    block_size: int
+    own_blocks: np.ndarray       # rendered blocks this rank owns, ascending id
+    own_slots: np.ndarray        # their slots in this rank's arena
+    remote_blocks: np.ndarray    # rendered blocks of other owners, ascending id
+    src_slot: np.ndarray         # [len(remote_blocks)] slot in the owner's arena
+    owner: np.ndarray            # [len(remote_blocks)] owner rank
+    missing: np.ndarray          # rendered blocks resident on no owner (host tier)
+
+    def owner_order(self) -> List[int]:
+        """Owners in the order this rank reads them: rank + 1, rank + 2, ...,
+        so that at any moment the owners serve different readers."""
+        return [(self.rank + d) % self.world for d in range(1, self.world)]
+
+
+def make_gather_plan(blocks, arena_blocks_by_rank: Sequence[np.ndarray], world: int, rank: int,
+                     block_size: int) -> GatherPlan:
+    """GatherPlan of this rank for `blocks` (the block ids it renders next).
+
+    arena_blocks_by_rank[o][s] is the block in owner o's arena slot s (-1 for
+    a free slot). A block must sit in its owner's arena (owner = id mod
+    world) to be gathered; the ones that do not are listed in `missing` and
+    come from the host tier instead."""
+    blocks = np.unique(np.asarray(blocks, np.int64))
+    if len(arena_blocks_by_rank) != world:
+        raise ValueError("make_gather_plan: one arena table per rank is needed")
+    owner = owner_of(blocks, world)
+    slot = np.full(blocks.size, -1, np.int64)
+    for o in range(world):
+        arena = np.asarray(arena_blocks_by_rank[o], np.int64)
+        sel = np.flatnonzero(owner == o)
+        if sel.size == 0:
+            continue
+        held = np.flatnonzero(arena >= 0)
+        if held.size and np.any(owner_of(arena[held], world) != o):
+            raise ValueError(f"make_gather_plan: rank {o}'s arena holds a block it does not own")
+        order = np.argsort(arena[held], kind="stable")
+        keys = arena[held][order]
+        if keys.size and np.any(keys[1:] == keys[:-1]):
+            raise ValueError(f"make_gather_plan: rank {o}'s arena holds a block twice")
+        at = np.searchsorted(keys, blocks[sel])
+        hit = at < keys.size
+        hit[hit] = keys[at[hit]] == blocks[sel][hit]
+        slot[sel[hit]] = held[order[at[hit]]]
+    found = slot >= 0
+    mine = owner == rank
+    return GatherPlan(world=world, rank=rank, block_size=int(block_size),
+                      own_blocks=blocks[mine & found], own_slots=slot[mine & found],
+                      remote_blocks=blocks[~mine & found], src_slot=slot[~mine & found],
+                      owner=owner[~mine & found], missing=blocks[~found])
+
+
+class PeerParamGather:
+    """Updated parameters of resident blocks, copied from their owners'
+    arenas to the ranks that render them next: the all-gather of changed
+    blocks that ownership sharding needs (TideGS trains on one GPU and has
+    none). Each rank exports its six arena component tensors once and maps
+    every other rank's. A gather, on the current stream of every rank:
+
+        barrier   every owner's update of the blocks is complete
+        copies    one tgs_copy_blocks launch per owner (GatherPlan.owner_order):
+                  whole block segments, read from the owner's arena over
+                  NVLink with bulk copies (no multicast) and stored into this
+                  rank's render rows
+        barrier   no rank still reads; owners may update their blocks again
+
+    The arena tensors stay fixed for the object's life."""
+
+    def __init__(self, arena: Mapping[str, torch.Tensor], block_size: int, device, group=None):
+        import torch.distributed as dist
+
+        self.device = _lib.require_cuda(device, "PeerParamGather")
+        self.block_size = int(block_size)
+        self.group = group
+        dist_on = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if dist_on else 1
+        self.rank = dist.get_rank(group) if dist_on else 0
+        table, self.rows, self._opened = _map_peer_components(
+            arena, self.device, group, self.world, self.rank, "PeerParamGather")
+        self._finish(table, {"own": dict(arena)}, collective=self.world > 1)
+
+    @classmethod
+    def in_process(cls, arenas_by_rank: Sequence[Mapping[str, torch.Tensor]], rank: int,
+                   block_size: int, device) -> "PeerParamGather":
+        """Every rank's arena lives in this process (ranks emulated on one
+        GPU, or one process driving several GPUs): no IPC mappings and no
+        barriers; arenas on other devices are read through peer access."""
+        self = cls.__new__(cls)
+        self.device = _lib.require_cuda(device, "PeerParamGather")
+        with torch.cuda.device(self.device):
+            for a in arenas_by_rank:
+                other = a["xyz"].device
+                if other != self.device:
+                    _lib.call("tgs_peer_access_enable", int(other.index))
+        self.block_size = int(block_size)
+        self.group = None
+        self.world = len(arenas_by_rank)
+        self.rank = int(rank)
+        self._opened = {}
+        table = np.asarray([_ops._comp_ptrs(a, "PeerParamGather") for a in arenas_by_rank],
+                           np.int64)
+        self.rows = np.asarray([min(int(a[n].shape[0]) for n in _ops.COMPONENTS)
+                                for a in arenas_by_rank], np.int64)
+        self._finish(table, {r: dict(a) for r, a in enumerate(arenas_by_rank)}, collective=False)
+        return self
+
+    def _finish(self, table: np.ndarray, keep, collective: bool) -> None:
+        self._table = table
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._arenas = keep  # keeps the exported tensors alive
+        self._collective = collective
+        self._closed = False
+
+    def barrier(self) -> None:
         if self._collective:
             import torch.distributed as dist
 
-            dist.barrier(group=self.group)
-        self._grads = {}
+            dist.all_reduce(self._flag, group=self.group)
+
+    def tables(self, plan: GatherPlan) -> List[tuple]:
+        """Per owner, in plan.owner_order(): (owner, [3, n] device table of
+        source rows, render rows and row counts, n)."""
+        if plan.world != self.world or plan.rank != self.rank:
+            raise ValueError("PeerParamGather: plan is for another world/rank")
+        if plan.block_size != self.block_size:
+            raise ValueError("PeerParamGather: plan is for another block size")
+        B = self.block_size
+        out = []
+        dst_index = np.arange(plan.remote_blocks.size, dtype=np.int64)
+        for o in plan.owner_order():
+            sel = plan.owner == o
+            n = int(np.count_nonzero(sel))
+            if n == 0:
+                continue
+            src = plan.src_slot[sel] * B
+            if np.any(src + B > self.rows[o]):
+                raise RuntimeError(f"PeerParamGather: a slot lies outside rank {o}'s arena")
+            t = _ops.i64_to_device(np.stack([src, dst_index[sel] * B, np.full(n, B, np.int64)]),
+                                   self.device).view(3, n)
+            out.append((o, t, n))
+        return out
+
+    def launch(self, dst: Mapping[str, torch.Tensor], plan: GatherPlan, tables=None,
+               err: Optional[torch.Tensor] = None) -> int:
+        """The copies alone (the caller provides both barriers). dst: six
+        render components with at least len(plan.remote_blocks) * block_size
+        rows. Returns the rows copied."""
+        B = self.block_size
+        need = plan.remote_blocks.size * B
+        dst_ptrs = _ops._comp_ptrs(dst, "PeerParamGather(dst)")
+        for n, w in _ops.WIDTHS.items():
+            t = dst[n]
+            if t.device != self.device or t.numel() != int(t.shape[0]) * w:
+                raise RuntimeError(f"PeerParamGather: render rows {n} must be [rows, {w}] "
+                                   f"on {self.device}")
+            if int(t.shape[0]) < need:
+                raise RuntimeError(f"PeerParamGather: render rows {n} hold {int(t.shape[0])} "
+                                   f"rows, the plan needs {need}")
+        tables = tables if tables is not None else self.tables(plan)
+        stream = torch.cuda.current_stream(self.device)
+        copied = 0
+        for o, t, n in tables:
+            args = _lib.CopyBlocksArgs()
+            for c in range(len(_ops.COMPONENTS)):
+                args.src_comp[c] = int(self._table[o, c])
+                args.dst_comp[c] = dst_ptrs[c]
+            args.src_global_ids = None
+            args.dst_global_ids = None
+            args.src_start = t[0].data_ptr()
+            args.dst_start = t[1].data_ptr()
+            args.row_count = t[2].data_ptr()
+            args.n_blocks = n
+            args.max_rows = B
+            args.err = _lib.ptr(err)
+            _lib.call("tgs_copy_blocks", args, stream.cuda_stream)
+            t.record_stream(stream)
+            copied += n * B
+        return copied
+
+    def gather(self, dst: Mapping[str, torch.Tensor], plan: GatherPlan, tables=None,
+               err: Optional[torch.Tensor] = None) -> int:
+        """acquire barrier -> copies from every owner -> release barrier."""
+        self.barrier()
+        copied = self.launch(dst, plan, tables, err)
+        self.barrier()
+        return copied
+
+    def close(self) -> None:
+        """Unmaps the peers' arenas (collective: every rank calls it with no
+        gather in flight)."""
+        if self._closed:
+            return
+        self._closed = True
+        _close_peer_mappings(self._opened, self.device, self.group, self._collective)
+        self._opened = {}
+        self._arenas = {}
+
+
+def exchange_arena_tables(arena_blocks, device, group=None) -> List[np.ndarray]:
+    """Every rank's arena table (the block held in each arena slot, -1 for a
+    free slot), all-gathered: the input of make_gather_plan. Collective;
+    `device` is where the backend wants its tensors (CPU for gloo)."""
+    import torch.distributed as dist
+
+    mine = np.asarray(arena_blocks, np.int64).reshape(-1)
+    world = dist.get_world_size(group)
+    n = torch.tensor([mine.size], dtype=torch.int64, device=device)
+    sizes = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(sizes, n, group=group)
+    sizes = [int(x.item()) for x in sizes]
+    padded = torch.full((max(sizes),), -1, dtype=torch.int64, device=device)
+    padded[:mine.size] = torch.from_numpy(mine).to(device)
+    out = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(out, padded, group=group)
+    return [t.cpu().numpy()[:m].copy() for t, m in zip(out, sizes)]

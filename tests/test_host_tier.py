@@ -366,3 +366,78 @@ def test_tail_block_round_trip(tmp_path):
         cache.shutdown()
         st.close()
 
+
+
+class _GatedLog(BlockLogStore):
+    """Block log whose first write waits for `gate` (a slow disk)."""
+
+    def __init__(self, *a, **k):
+        super().__init__(*a, **k)
+        self.gate = threading.Event()
+        self.first = True
+
+    def write_patch(self, block_dict):
+        if self.first:
+            self.first = False
+            assert self.gate.wait(10.0)
+        return super().write_patch(block_dict)
+
+
+def test_synchronous_fallback_write_waits_for_queued_older_versions(tmp_path):
+    """Flush queue full: the synchronous write of a block's newest version
+    must land after the queued writes of its older versions, or the block
+    log would keep an older one."""
+    from queue import Queue
+
+    B, NB = 8, 4
+    st = _GatedLog(str(tmp_path), B, NB, point_dim=G.POINT_DIM, verbose=False)
+    cache = _cache(st, max_ram_gb=1.0, block_size=B, capacity=16)
+    cache.flush_queue = Queue(maxsize=1)
+    try:
+        versions = [G.block_data(60_000 + i, B) for i in range(3)]
+        cache.upsert_dirty_blocks({0: versions[0]})
+        cache.submit_dirty_blocks([0], clone=True)   # the worker takes it and waits on the gate
+        deadline = time.time() + 5
+        while cache.flush_queue.qsize() and time.time() < deadline:
+            time.sleep(0.01)
+        cache.upsert_dirty_blocks({0: versions[1]})
+        cache.submit_dirty_blocks([0], clone=True)   # queued
+        cache.upsert_dirty_blocks({0: versions[2]})
+        threading.Timer(0.3, st.gate.set).start()
+        cache.submit_dirty_blocks([0], clone=True)   # queue full: synchronous, after the others
+        cache.drain()
+        assert torch.equal(st.read_blocks([0])[0], versions[2])
+        assert cache.get_stats()["flush_queue_drops"] >= 1
+        _assert_entries_consistent(cache)
+    finally:
+        st.gate.set()
+        cache.shutdown()
+
+
+class _SlowLog(BlockLogStore):
+    def write_patch(self, block_dict):
+        time.sleep(0.02)
+        return super().write_patch(block_dict)
+
+
+def test_full_slab_waits_for_flushes_instead_of_failing(tmp_path):
+    """Every entry dirty or flushing behind a slow block log: new blocks wait
+    for the flushes to return entries, and every block reads back current."""
+    B, NB = 8, 24
+    st = _SlowLog(str(tmp_path), B, NB, point_dim=G.POINT_DIM, verbose=False)
+    cache = _cache(st, max_ram_gb=4 * B * G.POINT_DIM * 4 / 1024 ** 3, block_size=B,
+                   capacity=8)
+    want = {}
+    try:
+        for i in range(40):
+            b = i % NB
+            want[b] = G.block_data(70_000 + i, B)
+            cache.upsert_dirty_blocks({b: want[b]})
+        cache.drain()
+        cache.flush_all_dirty()
+        fresh = st.read_blocks(sorted(want))
+        for b, t in want.items():
+            assert torch.equal(fresh[b], t), b
+        _assert_entries_consistent(cache)
+    finally:
+        cache.shutdown()

@@ -338,8 +338,13 @@ class PinnedBlockCache:
     the cached blocks exceed `eviction_threshold` of `max_ram_gb`, the least
     recently used 20 % leave (dirty ones through the flushing buffer and the
     block log). When a new block finds no free entry, the least recently
-    used clean block is evicted early; RuntimeError if every entry is dirty,
-    flushing or waiting to be written.
+    used clean block is evicted early. When every entry is dirty, flushing or
+    waiting to be written, the caller waits (up to `slab_wait_s`) for queued
+    flushes to return entries, and RuntimeError if none comes back.
+
+    Writes of one block reach the block log in the order they were queued: a
+    synchronous write (flush queue full, flush_all_dirty) first waits for the
+    queued ones, since the log keeps whichever write of a block came last.
 
     An entry is referenced by the cache, by the flushing buffer and by each
     queued flush job that writes it; it returns to the free list when the
@@ -349,7 +354,8 @@ class PinnedBlockCache:
     def __init__(self, storage_manager, max_ram_gb: float = 16.0, block_size: int = 4096,
                  point_dim: int = 59, prefetch_distance: int = 5,
                  eviction_threshold: float = 0.8, verbose: bool = True,
-                 capacity_blocks: Optional[int] = None, pin_memory: Optional[bool] = None):
+                 capacity_blocks: Optional[int] = None, pin_memory: Optional[bool] = None,
+                 slab_wait_s: float = 120.0):
         self.storage = storage_manager
         self.max_ram_bytes = int(max_ram_gb * 1024 * 1024 * 1024)
         self.block_size = int(block_size)
@@ -374,6 +380,8 @@ class PinnedBlockCache:
         self.dirty_set: Set[int] = set()
         self.block_versions: Dict[int, int] = {}
         self.cache_lock = threading.RLock()
+        self._entry_freed = threading.Condition(self.cache_lock)
+        self.slab_wait_s = float(slab_wait_s)
         self.flushing_buffer: Dict[int, Tuple[torch.Tensor, float, int]] = {}
         self.flushing_lock = threading.RLock()
         self.flush_queue: Queue = Queue(maxsize=128)
@@ -411,9 +419,11 @@ class PinnedBlockCache:
         return self.slab[entry, :rows]
 
     def _release(self, entry: int) -> None:
+        """Drops one reference (caller holds cache_lock)."""
         self._refs[entry] -= 1
         if self._refs[entry] == 0:
             self._free.append(entry)
+            self._entry_freed.notify_all()
 
     def _take_entry(self) -> int:
         """A free entry (caller holds cache_lock), after any DMA still
@@ -428,14 +438,25 @@ class PinnedBlockCache:
         return e
 
     def _make_room(self) -> None:
-        for b in list(self.cache_data.keys()):
-            if b not in self.dirty_set and self._refs[self._cache_entry[b]] == 1:
-                self.cache_data.pop(b)
-                self._release(self._cache_entry.pop(b))
-                self.stats["evictions"] += 1
-                return
-        raise RuntimeError(f"[TieredCache] slab of {self.capacity_blocks} entries is full "
-                           "(every entry dirty, flushing or shared)")
+        """Frees an entry (caller holds cache_lock): evicts the least recently
+        used clean block, else waits for queued flushes to return entries."""
+        deadline = None
+        while not self._free:
+            for b in list(self.cache_data.keys()):
+                if b not in self.dirty_set and self._refs[self._cache_entry[b]] == 1:
+                    self.cache_data.pop(b)
+                    self._release(self._cache_entry.pop(b))
+                    self.stats["evictions"] += 1
+                    return
+            with self.flushing_lock:
+                pending = bool(self.flushing_buffer) or self.flush_queue.unfinished_tasks > 0
+            now = time.monotonic()
+            deadline = now + self.slab_wait_s if deadline is None else deadline
+            if not pending or now >= deadline:
+                raise RuntimeError(f"[TieredCache] slab of {self.capacity_blocks} entries is full "
+                                   "(every entry dirty, flushing or shared)")
+            # releases cache_lock while waiting, so the flush worker can finish
+            self._entry_freed.wait(timeout=min(0.5, deadline - now))
 
     def _store(self, block_id: int, src: Optional[torch.Tensor], rows: int) -> torch.Tensor:
         """Puts a new entry for block_id (copy of src when given) at the MRU end
@@ -624,7 +645,16 @@ class PinnedBlockCache:
             for t in dirty_blocks.values():
                 self._refs[self._entry_of(t)] += 1
         if not self._enqueue_dirty_flush(dirty_blocks, versions, reason):
-            self._flush_dirty_blocks(dirty_blocks, block_versions=versions, mode="sync")
+            self._flush_in_order(dirty_blocks, versions)
+
+    def _flush_in_order(self, dirty_blocks: Dict[int, torch.Tensor],
+                        versions: Dict[int, int]) -> None:
+        """Synchronous write after every queued flush job: a queued job may
+        hold an older version of one of these blocks, and the block log keeps
+        whichever write of a block came last. The caller holds no lock."""
+        if threading.current_thread() is not self.flush_thread:
+            self.flush_queue.join()
+        self._flush_dirty_blocks(dirty_blocks, block_versions=versions, mode="sync")
 
     def _flush_dirty_blocks(self, dirty_blocks: Dict[int, torch.Tensor],
                             block_versions: Optional[Dict[int, int]] = None,
@@ -690,7 +720,7 @@ class PinnedBlockCache:
         except Full:
             self.stats["flush_queue_drops"] += 1
             print(f"[TieredCache] Flush queue full; falling back to synchronous write for "
-                  f"{len(dirty_blocks)} blocks")
+                  f"{len(dirty_blocks)} blocks (after the queued ones)")
             return False
 
     def _flush_worker(self) -> None:
@@ -863,7 +893,7 @@ class PinnedBlockCache:
                 else:
                     self._release(entries[b])
         if not self._enqueue_dirty_flush(blocks, versions, reason):
-            self._flush_dirty_blocks(blocks, block_versions=versions, mode="sync")
+            self._flush_in_order(blocks, versions)
         return len(blocks)
 
     # -- reads ---------------------------------------------------------------
@@ -1020,7 +1050,7 @@ class PinnedBlockCache:
             with self.cache_lock:
                 for t in blocks.values():
                     self._refs[self._entry_of(t)] += 1
-            self._flush_dirty_blocks(blocks, block_versions=versions, mode="sync")
+            self._flush_in_order(blocks, versions)
 
     def get_stats(self) -> Dict:
         with self.cache_lock:

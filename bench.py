@@ -115,6 +115,12 @@ ADAM_TRAFFIC_BYTES_PER_ROW = 1687.7
 # NVLink bandwidth per direction of one B200 measured on this box type (peer
 # copy), the denominator of the parameter gather's fraction
 NVLINK_GBPS = 770.0
+# From this many ranks the pull update is bound by NVLink (remote
+# contributions per owner grow with the camera split) and leaves HBM room for
+# the block materialization, which then runs beside it on the SMs the update
+# leaves free (OVERLAP_ADAM_CTAS of 148 for the update)
+OVERLAP_MIN_WORLD = 8
+OVERLAP_ADAM_CTAS = 120
 LRS = {"xyz": 1.6e-4, "opacity": 0.05, "scaling": 5e-3, "rotation": 1e-3, "features_dc": 2.5e-3,
        "features_rest": 1.25e-4}
 
@@ -429,7 +435,7 @@ class DeviceStep:
     new admission stamp (its moments read as zero)."""
 
     def __init__(self, device, sched: Schedule, trace: ScheduleTrace, world: int = 1,
-                 exchange: str = "pull"):
+                 exchange: str = "pull", overlap: bool = False, adam_ctas: int = 0):
         from tidegs_b200 import _lib, _ops
 
         self._lib, self._ops = _lib, _ops
@@ -514,6 +520,18 @@ class DeviceStep:
             self.param_gather = PeerParamGather(self.arena, B, device)
         self.adam_ms = []
         self.updated_rows = []
+        # pipelined materialization: step k's write-back of step k-1's dirty
+        # evicted blocks and its unpack of the incoming blocks run on a side
+        # stream while the update runs on the main one (step_overlapped)
+        self.overlap = bool(overlap)
+        self.adam_ctas = int(adam_ctas)
+        if self.overlap:
+            self.side = torch.cuda.Stream(device)
+            self.ev_main = torch.cuda.Event()   # update + bounds of the last step done
+            self.ev_side = torch.cuda.Event()   # unpack of the last step landed
+            self.ev_main.record()
+            self.ev_side.record()
+            self._pending_wb = None             # (selection, evicted blocks, slots) of step k-1
         torch.cuda.synchronize()
 
     def _upload_pos_end(self) -> None:
@@ -647,7 +665,7 @@ class DeviceStep:
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
         if self.pull is not None:
-            self.pull.launch(a, self.plan, stream, tables=tables)
+            self.pull.launch(a, self.plan, stream, tables=tables, max_ctas=self.adam_ctas)
         else:
             _lib.call("tgs_resident_adam_apply", a, stream)
         if timed:
@@ -676,8 +694,14 @@ class DeviceStep:
             self.phase_ms.setdefault(name, []).append(e0.elapsed_time(e1))
             self.host_ms.setdefault(name, []).append((h1 - h0) * 1e3)
         self._events = []
+        if self._side_events is not None:
+            s0, s1 = self._side_events
+            self.phase_ms.setdefault("side_pack_unpack", []).append(s0.elapsed_time(s1))
+            self._side_events = None
 
     def step(self, k: int, timed: bool = False) -> int:
+        if self.overlap:
+            return self.step_overlapped(k, timed)
         _ops = self._ops
         sched = self.sched
         self._events = []
@@ -737,6 +761,87 @@ class DeviceStep:
         self._phase("tables")
         return int(ids.numel())
 
+    def step_overlapped(self, k: int, timed: bool = False) -> int:
+        """Step k with the block materialization pipelined beside the update.
+        Side stream: write back step k-1's dirty evicted blocks (they left
+        the working set at the end of step k-1, after their last update),
+        then unpack step k's incoming blocks into the spare slots, which are
+        the slots those blocks left. Main stream: the update of step k,
+        dirty marks and bounds. Neither touches the other's slots. Step k+1's
+        update waits for step k's unpack; step k+1's write-back waits for
+        step k's update. Per step the same kernels run as in step(); a step
+        writes back the blocks the step before it evicted."""
+        _ops = self._ops
+        sched = self.sched
+        main = torch.cuda.current_stream(self.device)
+        self._events = []
+        self._phase("start")
+        main.wait_event(self.ev_side)     # step k-1's incoming blocks have landed
+        self.side.wait_event(self.ev_main)  # step k-1's update and bounds are done
+        evict_pos, incoming, dirty = self.trace.turn[k]
+        evict_slots = self.arena_of_pos[evict_pos]
+        evicted_blocks = self.arena_block[evict_slots]
+        pending = self._pending_wb
+        wb_ids = pending[0].wait() if pending is not None else []
+        with torch.cuda.stream(self.side):
+            if self.phase_ms is not None:
+                s0 = torch.cuda.Event(enable_timing=True)
+                s0.record()
+            if pending is not None and len(wb_ids):
+                _, sorted_blocks, sorted_slots = pending
+                wb_slots = sorted_slots[np.searchsorted(sorted_blocks,
+                                                        np.asarray(wb_ids, np.int64))]
+                _ops.pack_rows(self.arena, (wb_slots * B).tolist(), [B] * wb_slots.size,
+                               self.wb_staging[: wb_slots.size * B], self._lib.LAYOUT_CACHE)
+            src = self.incoming_pool[(k % 2) * TURNOVER * B:(k % 2 + 1) * TURNOVER * B]
+            ids_dev = _ops.i64_to_device(incoming, self.device)
+            _ops.unpack_rows(src, self._lib.LAYOUT_CACHE, self.arena, 0, global_ids=self.gids,
+                             block_ids=ids_dev, block_size=B, block_dst=self.spare * B)
+            self.ev_side.record(self.side)
+            if self.phase_ms is not None:
+                s1 = torch.cuda.Event(enable_timing=True)
+                s1.record()
+                self._side_events = (s0, s1)
+        if pending is not None and len(wb_ids):
+            _ops.dirty_mark(self.bitmap, wb_ids, False)
+        self._phase("side_issue")
+        if self.world > 1:
+            slots, ids = self.exchange_grads(k)
+            self._phase("exchange")
+        else:
+            slots = self.visible_arena(k)
+            ids = self.row_ids(slots)
+        self.adam(ids, timed)
+        self.plan_ahead(k)
+        _ops.dirty_mark(self.bitmap, self.arena_block[slots].tolist(), True)
+        _ops.block_bounds(self.arena["xyz"], (slots * B).tolist(), [B] * slots.size,
+                          self.bounds[: slots.size])
+        self.ev_main.record(main)
+        self._phase("dirty_bounds")
+        if dirty is not None:
+            _ops.dirty_mark(self.bitmap, evicted_blocks[dirty].tolist(), True)
+            _ops.dirty_mark(self.bitmap, evicted_blocks[~dirty].tolist(), False)
+        order = np.argsort(evicted_blocks, kind="stable")
+        self._pending_wb = (_ops.dirty_select_async(self.bitmap, evicted_blocks[order].tolist()),
+                            evicted_blocks[order], evict_slots[order])
+        self._phase("dirty_select")
+        new_slots = self.spare
+        self.arena_block, self.arena_of_pos, self.spare = self._after_turnover(k)
+        sched.slot_block[evict_pos] = incoming
+        self.stamp_host[new_slots] += 1
+        _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
+        self.slot_step.index_fill_(0, _ops.i64_to_device(new_slots, self.device), 0)
+        self._upload_pos_end()
+        self._phase("tables")
+        return int(ids.numel())
+
+    def drain(self) -> None:
+        """Makes the current stream wait for the side stream's last work
+        (the end of a timed region must cover it)."""
+        if self.overlap:
+            torch.cuda.current_stream(self.device).wait_event(self.ev_side)
+
+    _side_events = None
     param_gather = None
 
     def close(self):
@@ -761,6 +866,7 @@ class DeviceStep:
         one for the counts)."""
         from oracle.resident_adam import bias_pair, kernel_update
 
+        torch.cuda.synchronize()  # the side stream's blocks of the last step have landed
         W, me, sched = self.world, self.sched.rank, self.sched
         pos_all = sched.visible_positions(k)
         evict_pos = self.trace.turn[k][0]
@@ -1604,6 +1710,13 @@ def main(argv=None):
                     help="print a per-phase CUDA-event breakdown of the device step to stderr "
                          "(extra events; not used for the reported value)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--overlap", default="auto", choices=["auto", "on", "off"],
+                    help="run the write-back and unpack on a side stream beside the update "
+                         f"(auto: on from {OVERLAP_MIN_WORLD} ranks, where NVLink bounds the "
+                         "update and HBM has room)")
+    ap.add_argument("--adam-ctas", type=int, default=-1,
+                    help="cap on the streamed pull update's CTAs (-1: "
+                         f"{OVERLAP_ADAM_CTAS} with --overlap, else one per SM)")
     ap.add_argument("--exchange", default="pull", choices=["pull", "push", "nccl"],
                     help="N>1 gradient exchange: the owner's update kernel sums the senders' "
                          "gradients over NVLink (pull, default); a push kernel into receive "
@@ -1625,7 +1738,10 @@ def main(argv=None):
     n_trace = max(args.warmup + args.steps + 6, n_e2e + 1)
     trace = ScheduleTrace(world, rank, n_trace)
     sched = Schedule(rank, world)
-    dev = DeviceStep(device, sched, trace, world=world, exchange=args.exchange)
+    overlap = args.overlap == "on" or (args.overlap == "auto" and world >= OVERLAP_MIN_WORLD)
+    adam_ctas = args.adam_ctas if args.adam_ctas >= 0 else (OVERLAP_ADAM_CTAS if overlap else 0)
+    dev = DeviceStep(device, sched, trace, world=world, exchange=args.exchange, overlap=overlap,
+                     adam_ctas=adam_ctas)
     for k in range(args.warmup):
         dev.step(k)
     torch.cuda.synchronize()
@@ -1639,6 +1755,7 @@ def main(argv=None):
     rows = 0
     for k in range(args.warmup, args.warmup + args.steps):
         rows += dev.step(k, timed=True)
+    dev.drain()
     end.record()
     torch.cuda.synchronize()
     next_k = args.warmup + args.steps
@@ -1765,6 +1882,10 @@ def main(argv=None):
                                     else "direct NVLink push (tgs_grad_push) + ordered owner sum"
                                     if args.exchange == "push" else
                                     "pack + NCCL all-to-all + ordered owner sum"),
+                       "materialization": ("write-back of the previous step's evicted blocks "
+                                           "and unpack on a side stream beside the update "
+                                           f"(update capped at {adam_ctas} CTAs)" if overlap
+                                           else "after the update, on the same stream"),
                        "l2": "every input larger than L2 (126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak,

@@ -564,6 +564,11 @@ typedef struct {
    * once instead of all reading the same sender first; 0 = natural order. */
   int64_t rotate_rows;
   int32_t* err;                     /* [4] the error word of adam.err, writable */
+  /* Most CTAs the streamed kernel may use (it runs at most one per SM);
+   * 0 = one per SM. A smaller grid leaves SMs to kernels that run at the same
+   * time on another stream, which pays when NVLink, not HBM, bounds the
+   * update (many ranks, many remote contributions). */
+  int32_t max_ctas;
 } TgsResidentAdamSumArgs;
 
 TGS_API int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* args, void* stream);

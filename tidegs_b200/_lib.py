@@ -129,6 +129,7 @@ class ResidentAdamSumArgs(C.Structure):
         ("adam", ResidentAdamArgs), ("grad_src", _vp), ("grad_rows", _vp), ("n_ranks", _i32),
         ("seg_begin", _vp), ("n_segments", _i32), ("contrib_offsets", _vp),
         ("contrib_rank", _vp), ("contrib_row", _vp), ("rotate_rows", _i64), ("err", _vp),
+        ("max_ctas", _i32),
     ]
 
 

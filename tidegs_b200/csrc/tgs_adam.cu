@@ -1758,7 +1758,9 @@ extern "C" int tgs_resident_adam_apply_sum(const TgsResidentAdamSumArgs* a, void
   if (can_stream(q.a, false)) {
     static bool configured[2][64] = {};
     constexpr int smem = stream_smem_bytes<TGS_SUM_STAGED_CONTRIBS, TGS_SUM_STREAM_STAGES>();
-    const int sgrid = stream_grid(a->adam.n_rows, TGS_SUM_STREAM_CTAS);
+    TGS_CHECK_ARG(a->max_ctas >= 0, "tgs_resident_adam_apply_sum: max_ctas < 0");
+    int sgrid = stream_grid(a->adam.n_rows, TGS_SUM_STREAM_CTAS);
+    if (a->max_ctas > 0) sgrid = std::min(sgrid, static_cast<int>(a->max_ctas));
     const int rc2 = pow2 ? launch_stream(resident_adam_sum_stream_kernel<true>, q, smem, sgrid, s,
                                          configured[1])
                          : launch_stream(resident_adam_sum_stream_kernel<false>, q, smem, sgrid,

@@ -545,9 +545,12 @@ class PeerGradPull:
         self.launch(adam_args, plan, stream)
         self.barrier()
 
-    def launch(self, adam_args, plan: ExchangePlan, stream: int, tables=None) -> None:
+    def launch(self, adam_args, plan: ExchangePlan, stream: int, tables=None,
+               max_ctas: int = 0) -> None:
         """The fused update alone; the caller provides both barriers.
-        tables: the result of tables(plan), when the caller built it earlier."""
+        tables: the result of tables(plan), when the caller built it earlier.
+        max_ctas: cap on the streamed kernel's CTAs (0 = one per SM), to leave
+        SMs to work on another stream."""
         S = plan.n_out
         if int(adam_args.n_rows) != S * plan.block_size:
             raise ValueError("PeerGradPull: rows to update do not match the plan's blocks")
@@ -565,6 +568,7 @@ class PeerGradPull:
         # start at this rank's share of the rows, so that at any moment the
         # owners pull from different senders
         args.rotate_rows = (self.rank * S // max(1, self.world)) * plan.block_size
+        args.max_ctas = int(max_ctas)
         args.err = adam_args.err
         _lib.call("tgs_resident_adam_apply_sum", args, stream)
         cur = torch.cuda.current_stream(self.device)

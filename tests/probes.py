@@ -5,6 +5,7 @@
     python -m tests.probes --render [--steps K] [--warmup W]
     python -m tests.probes --accum  [--steps K] [--warmup W]
     python -m tests.probes --ref-kernels [--steps K] [--warmup W]
+    python -m tests.probes --dense  [--steps K] [--warmup W]
 
 Each prints one JSON line. They compare this library's kernels with the
 reference's own operations or kernels (built into oracle/_ref) and with the
@@ -597,6 +598,20 @@ def ref_kernels_probe(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Diagnostic: the dense masked optimizers alone (BASELINE configs[0] and [1])
+# ---------------------------------------------------------------------------
+def dense_probe(args):
+    """SelectiveAdam (configs[0]) and SelectiveSophia (configs[1]) steps as
+    the bench's configs leg runs them, without the rest of the bench (a
+    small program for ncu captures of dense_kernel)."""
+    dev = torch.device("cuda", 0)
+    adam = bn.bench_selective_adam(dev, steps=args.steps, warmup=max(3, args.warmup))
+    sophia = bn.bench_sophia(dev, steps=args.steps, k=10, warmup=max(3, args.warmup))
+    print(json.dumps({"probe": "dense", "selective_adam": adam, "sophia": sophia}), flush=True)
+    return 0
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--steps", type=int, default=5)
@@ -611,6 +626,8 @@ def main(argv=None):
                     help="render path, ours vs the reference gsplat kernels")
     ap.add_argument("--ref-kernels", action="store_true",
                     help="the reference's Triton kernels (oracle/_ref/triton) beside ours")
+    ap.add_argument("--dense", action="store_true",
+                    help="SelectiveAdam / SelectiveSophia steps alone (configs[0] and [1])")
     ap.add_argument("--accum", action="store_true",
                     help="touched-only gradient accumulation of a camera batch against the "
                          "reference's torch operations")
@@ -628,7 +645,9 @@ def main(argv=None):
         return accum_probe(args)
     if args.ref_kernels:
         return ref_kernels_probe(args)
-    ap.error("choose one of --pull, --cull, --render, --accum")
+    if args.dense:
+        return dense_probe(args)
+    ap.error("choose one of --pull, --cull, --render, --accum, --ref-kernels, --dense")
     return 2
 
 

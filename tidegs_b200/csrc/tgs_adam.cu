@@ -1400,9 +1400,9 @@ __device__ __forceinline__ void sophia_elem(float& p, float& m, float& h, float 
 
 // Eight CTAs of 256 threads fill every warp slot of an SM: the kernel is
 // bound by load latency (one float4 per array in flight per thread), so the
-// 32-register cap (a few bytes of spill in the Sophia variant) buys more
+// 32-register cap (20 bytes of spill in the SelectiveAdam variant) buys more
 // loads in flight than it costs: 0.178 / 1.29 ms per SelectiveAdam / Sophia
-// step against 0.187 / 1.47 ms with 34 / 40 registers at six CTAs.
+// step against 0.187 / 1.47 ms at six CTAs per SM.
 template <bool kSophia>
 __global__ void __launch_bounds__(kDenseThreads, 8) dense_kernel(const DenseParams a) {
   int gi = 0;

@@ -437,8 +437,7 @@ class DeviceStep:
     new admission stamp (its moments read as zero)."""
 
     def __init__(self, device, sched: Schedule, trace: ScheduleTrace, world: int = 1,
-                 exchange: str = "pull", overlap: bool = False, adam_ctas: int = 0,
-                 defer_writeback: bool = False):
+                 exchange: str = "pull", overlap: bool = False, adam_ctas: int = 0):
         from tidegs_b200 import _lib, _ops
 
         self._lib, self._ops = _lib, _ops
@@ -523,21 +522,18 @@ class DeviceStep:
             self.param_gather = PeerParamGather(self.arena, B, device)
         self.adam_ms = []
         self.updated_rows = []
-        # pipelined materialization (step_pipelined): step k writes back step
-        # k-1's dirty evicted blocks, then unpacks its incoming blocks, either
-        # on the main stream ahead of the update (defer_writeback) or on a
-        # side stream beside it (overlap)
+        # pipelined materialization: step k's write-back of step k-1's dirty
+        # evicted blocks and its unpack of the incoming blocks run on a side
+        # stream while the update runs on the main one (step_overlapped)
         self.overlap = bool(overlap)
-        self.pipelined = self.overlap or bool(defer_writeback)
         self.adam_ctas = int(adam_ctas)
-        self.side = None
         if self.overlap:
             self.side = torch.cuda.Stream(device)
             self.ev_main = torch.cuda.Event()   # update + bounds of the last step done
             self.ev_side = torch.cuda.Event()   # unpack of the last step landed
             self.ev_main.record()
             self.ev_side.record()
-        self._pending_wb = None                 # (selection, evicted blocks, slots) of step k-1
+            self._pending_wb = None             # (selection, evicted blocks, slots) of step k-1
         torch.cuda.synchronize()
 
     def _upload_pos_end(self) -> None:
@@ -706,8 +702,8 @@ class DeviceStep:
             self._side_events = None
 
     def step(self, k: int, timed: bool = False) -> int:
-        if self.pipelined:
-            return self.step_pipelined(k, timed)
+        if self.overlap:
+            return self.step_overlapped(k, timed)
         _ops = self._ops
         sched = self.sched
         self._events = []
@@ -767,33 +763,29 @@ class DeviceStep:
         self._phase("tables")
         return int(ids.numel())
 
-    def step_pipelined(self, k: int, timed: bool = False) -> int:
-        """Step k with the block materialization pipelined: first write back
-        step k-1's dirty evicted blocks (they left the working set at the end
-        of step k-1, after their last update), then unpack step k's incoming
-        blocks into the spare slots, which are the slots those blocks left;
-        then the update of step k, dirty marks and bounds, which touch none
-        of those slots. With a side stream (overlap) the write-back and
-        unpack run beside the update: step k+1's update waits for step k's
-        unpack and step k+1's write-back waits for step k's update. Without
-        one they run ahead of the update on the main stream. Either way the
-        host never waits for the step's own dirty list (it is read one step
-        later), and per step the same kernels run as in step()."""
+    def step_overlapped(self, k: int, timed: bool = False) -> int:
+        """Step k with the block materialization pipelined beside the update.
+        Side stream: write back step k-1's dirty evicted blocks (they left
+        the working set at the end of step k-1, after their last update),
+        then unpack step k's incoming blocks into the spare slots, which are
+        the slots those blocks left. Main stream: the update of step k,
+        dirty marks and bounds. Neither touches the other's slots. Step k+1's
+        update waits for step k's unpack; step k+1's write-back waits for
+        step k's update. Per step the same kernels run as in step(); a step
+        writes back the blocks the step before it evicted."""
         _ops = self._ops
         sched = self.sched
         main = torch.cuda.current_stream(self.device)
-        side = self.side if self.side is not None else main
         self._events = []
         self._phase("start")
-        if self.side is not None:
-            main.wait_event(self.ev_side)       # step k-1's incoming blocks have landed
-            self.side.wait_event(self.ev_main)  # step k-1's update and bounds are done
+        main.wait_event(self.ev_side)     # step k-1's incoming blocks have landed
+        self.side.wait_event(self.ev_main)  # step k-1's update and bounds are done
         evict_pos, incoming, dirty = self.trace.turn[k]
         evict_slots = self.arena_of_pos[evict_pos]
         evicted_blocks = self.arena_block[evict_slots]
         pending = self._pending_wb
         wb_ids = pending[0].wait() if pending is not None else []
-        with torch.cuda.stream(side):
+        with torch.cuda.stream(self.side):
             if self.phase_ms is not None:
                 s0 = torch.cuda.Event(enable_timing=True)
                 s0.record()
@@ -807,8 +799,7 @@ class DeviceStep:
             ids_dev = _ops.i64_to_device(incoming, self.device)
             _ops.unpack_rows(src, self._lib.LAYOUT_CACHE, self.arena, 0, global_ids=self.gids,
                              block_ids=ids_dev, block_size=B, block_dst=self.spare * B)
-            if self.side is not None:
-                self.ev_side.record(self.side)
+            self.ev_side.record(self.side)
             if self.phase_ms is not None:
                 s1 = torch.cuda.Event(enable_timing=True)
                 s1.record()
@@ -827,8 +818,7 @@ class DeviceStep:
         _ops.dirty_mark(self.bitmap, self.arena_block[slots].tolist(), True)
         _ops.block_bounds(self.arena["xyz"], (slots * B).tolist(), [B] * slots.size,
                           self.bounds[: slots.size])
-        if self.side is not None:
-            self.ev_main.record(main)
+        self.ev_main.record(main)
         self._phase("dirty_bounds")
         if dirty is not None:
             _ops.dirty_mark(self.bitmap, evicted_blocks[dirty].tolist(), True)
@@ -1726,10 +1716,6 @@ def main(argv=None):
                     help="run the write-back and unpack on a side stream beside the update "
                          "(auto: on from OVERLAP_MIN_WORLD ranks, where NVLink bounds the "
                          "update and HBM has room)")
-    ap.add_argument("--writeback", default="inline", choices=["inline", "deferred"],
-                    help="write back a step's dirty evicted blocks in the step (inline) or "
-                         "at the start of the next one, ahead of its unpack (deferred: the "
-                         "host never waits for the step's own dirty list)")
     ap.add_argument("--adam-ctas", type=int, default=-1,
                     help="cap on the streamed pull update's CTAs (-1: "
                          f"{OVERLAP_ADAM_CTAS} with --overlap, else one per SM)")
@@ -1757,7 +1743,7 @@ def main(argv=None):
     overlap = args.overlap == "on" or (args.overlap == "auto" and world >= OVERLAP_MIN_WORLD)
     adam_ctas = args.adam_ctas if args.adam_ctas >= 0 else (OVERLAP_ADAM_CTAS if overlap else 0)
     dev = DeviceStep(device, sched, trace, world=world, exchange=args.exchange, overlap=overlap,
-                     adam_ctas=adam_ctas, defer_writeback=args.writeback == "deferred")
+                     adam_ctas=adam_ctas)
     for k in range(args.warmup):
         dev.step(k)
     torch.cuda.synchronize()
@@ -1901,9 +1887,6 @@ def main(argv=None):
                        "materialization": ("write-back of the previous step's evicted blocks "
                                            "and unpack on a side stream beside the update "
                                            f"(update capped at {adam_ctas} CTAs)" if overlap
-                                           else "write-back of the previous step's evicted "
-                                           "blocks, then unpack, ahead of the update"
-                                           if args.writeback == "deferred"
                                            else "after the update, on the same stream"),
                        "l2": "every input larger than L2 (126 MB)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -43,66 +43,111 @@ __device__ __forceinline__ int find_position(const int64_t* __restrict__ pos_sta
 // Kernel A: validate the ids (in range, strictly ascending, inside a resident
 // position) and count touched rows per position.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) resident_count_kernel(
+constexpr int kCountThreads = 256;
+constexpr int kCountRows = 4;  // consecutive rows per thread: a warp covers four 32-row chunks
+
+__global__ void __launch_bounds__(kCountThreads) resident_count_kernel(
     const int64_t* __restrict__ ids, int64_t n, int64_t param_rows,
     const int64_t* __restrict__ pos_start, const int64_t* __restrict__ pos_end,
     const int32_t* __restrict__ pos_slot, int n_pos, int64_t block_size,
     int32_t* __restrict__ pos_count, int64_t* __restrict__ chunk_table,
     int32_t* __restrict__ err) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  // one lookup per row: position (and state row) of id, or an error code
-  int p = -1;
-  int64_t id = -1, sr = -1;
-  int code = TGS_DEV_OK;
-  if (i < n) {
-    id = ids[i];
-    if (id < 0 || id >= param_rows) {
+  const unsigned full = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int64_t i0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * kCountRows;
+  // The thread's rows i0 .. i0+3 (-1 past the end), two 16-byte loads when
+  // the array allows.
+  int64_t id[kCountRows];
+  if (i0 + kCountRows <= n && (reinterpret_cast<uintptr_t>(ids) & 15) == 0) {
+    const longlong2 a = __ldg(reinterpret_cast<const longlong2*>(ids + i0));
+    const longlong2 b = __ldg(reinterpret_cast<const longlong2*>(ids + i0) + 1);
+    id[0] = a.x; id[1] = a.y; id[2] = b.x; id[3] = b.y;
+  } else {
+#pragma unroll
+    for (int k = 0; k < kCountRows; ++k) id[k] = i0 + k < n ? __ldg(ids + i0 + k) : -1;
+  }
+  // The rows on either side of the thread's four: the neighbouring lanes'
+  // ids, or loads at the warp's ends.
+  int64_t before = __shfl_up_sync(full, id[kCountRows - 1], 1);
+  int64_t after = __shfl_down_sync(full, id[0], 1);
+  if (lane == 0) before = i0 > 0 && i0 <= n ? __ldg(ids + i0 - 1) : -1;
+  if (lane == 31) after = i0 + kCountRows < n ? __ldg(ids + i0 + kCountRows) : -1;
+
+  // One position lookup per row that leaves the previous row's position:
+  // position (and state row) of each row, or an error code.
+  int p[kCountRows];
+  int64_t sr[kCountRows];
+  int cp = -1;
+  int64_t cps = 0, cpe = 0, cslot = 0;
+#pragma unroll
+  for (int k = 0; k < kCountRows; ++k) {
+    p[k] = -1;
+    sr[k] = -1;
+    const int64_t i = i0 + k;
+    if (i >= n) continue;
+    const int64_t x = id[k];
+    const int64_t prev = k == 0 ? before : id[k - 1];
+    int code = TGS_DEV_OK;
+    if (x < 0 || x >= param_rows) {
       code = TGS_DEV_ID_OUT_OF_RANGE;
-    } else if (i > 0 && __ldg(ids + i - 1) >= id) {
+    } else if (i > 0 && prev >= x) {
       code = TGS_DEV_ID_NOT_SORTED;
     } else {
-      p = find_position(pos_start, pos_end, n_pos, block_size, id);
-      if (p >= n_pos || __ldg(pos_start + p) > id) {
+      if (!(cp >= 0 && x >= cps && x < cpe)) {
+        cp = find_position(pos_start, pos_end, n_pos, block_size, x);
+        if (cp < n_pos) {
+          cps = __ldg(pos_start + cp);
+          cpe = __ldg(pos_end + cp);
+          cslot = __ldg(pos_slot + cp);
+        }
+        if (cp >= n_pos || cps > x) cp = -1;
+      }
+      if (cp < 0) {
         code = TGS_DEV_ID_NOT_RESIDENT;
       } else {
-        sr = static_cast<int64_t>(__ldg(pos_slot + p)) * block_size + (id - __ldg(pos_start + p));
+        p[k] = cp;
+        sr[k] = cslot * block_size + (x - cps);
       }
     }
-    if (code != TGS_DEV_OK) {
-      report_error(err, code, i);
-      p = -1;
-      sr = -1;
-    }
+    if (code != TGS_DEV_OK) report_error(err, code, i);
   }
-  // A warp covers the 32-row chunk i / 32 (256-thread blocks): it records in
-  // the chunk table whether the chunk can be streamed by bulk copies -- all
-  // 32 rows valid, ids and state rows both consecutive (every lane checks
-  // its own row), first id a multiple of 4.
+
+  // Lanes 8j .. 8j+7 cover one 32-row chunk: the chunk table records whether
+  // the chunk can be streamed by bulk copies -- all 32 rows valid, ids and
+  // state rows both consecutive (every row checked), first id a multiple of 4.
   if (chunk_table != nullptr) {
-    const int lane = threadIdx.x & 31;
-    const unsigned full = 0xffffffffu;
-    const int64_t id0 = __shfl_sync(full, id, 0);
-    const int64_t sr0 = __shfl_sync(full, sr, 0);
-    const bool stream =
-        __all_sync(full, sr >= 0 && id == id0 + lane && sr == sr0 + lane) != 0 && (id0 & 3) == 0;
-    if (lane == 0 && i < n) {
-      const int64_t chunk = i >> 5;
-      chunk_table[2 * chunk] = stream ? id0 : -1;
-      chunk_table[2 * chunk + 1] = stream ? sr0 : -1;
+    bool ok = true;
+#pragma unroll
+    for (int k = 0; k < kCountRows; ++k)
+      ok = ok && sr[k] >= 0 && id[k] == id[0] + k && sr[k] == sr[0] + k;
+    const int64_t last_id = __shfl_up_sync(full, id[kCountRows - 1], 1);
+    const int64_t last_sr = __shfl_up_sync(full, sr[kCountRows - 1], 1);
+    if ((lane & 7) != 0) ok = ok && id[0] == last_id + 1 && sr[0] == last_sr + 1;
+    const unsigned votes = __ballot_sync(full, ok);
+    const bool stream = ((votes >> (lane & ~7)) & 0xffu) == 0xffu && (id[0] & 3) == 0;
+    if ((lane & 7) == 0 && i0 < n) {
+      const int64_t chunk = i0 >> 5;
+      chunk_table[2 * chunk] = stream ? id[0] : -1;
+      chunk_table[2 * chunk + 1] = stream ? sr[0] : -1;
     }
   }
-  if (i >= n) return;
+
   // Rows of a position are consecutive (ids ascending): its first row
   // subtracts its index and its last row adds its index + 1, so the count
   // costs two uncontended additions per position (an addition per row or per
   // warp serializes on one counter while a block's rows are counted). int32
   // wrap-around keeps the difference exact. Counts are only used when no row
   // reported an error.
-  if (p >= 0) {
-    if (i == 0 || __ldg(ids + i - 1) < __ldg(pos_start + p))
-      atomicSub(pos_count + p, static_cast<int32_t>(static_cast<uint32_t>(i)));
-    if (i == n - 1 || __ldg(ids + i + 1) >= __ldg(pos_end + p))
-      atomicAdd(pos_count + p, static_cast<int32_t>(static_cast<uint32_t>(i + 1)));
+#pragma unroll
+  for (int k = 0; k < kCountRows; ++k) {
+    if (p[k] < 0) continue;
+    const int64_t i = i0 + k;
+    const int64_t prev = k == 0 ? before : id[k - 1];
+    const int64_t next = k == kCountRows - 1 ? after : id[k + 1];
+    if (i == 0 || prev < __ldg(pos_start + p[k]))
+      atomicSub(pos_count + p[k], static_cast<int32_t>(static_cast<uint32_t>(i)));
+    if (i == n - 1 || next >= __ldg(pos_end + p[k]))
+      atomicAdd(pos_count + p[k], static_cast<int32_t>(static_cast<uint32_t>(i + 1)));
   }
 }
 
@@ -1561,9 +1606,9 @@ extern "C" int tgs_resident_adam_count(const TgsResidentCountArgs* a, void* stre
   TGS_CUDA(cudaMemsetAsync(a->pos_count, 0, sizeof(int32_t) * a->n_positions, s));
   TGS_CUDA(cudaMemsetAsync(a->err, 0, sizeof(int32_t) * 4, s));
   if (a->n_rows == 0) return TGS_OK;
-  const int64_t blocks = ceil_div<int64_t>(a->n_rows, 256);
+  const int64_t blocks = ceil_div<int64_t>(a->n_rows, int64_t(kCountThreads) * kCountRows);
   TGS_CHECK_ARG(blocks < (1ll << 31), "tgs_resident_adam_count: n_rows too large");
-  resident_count_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(
+  resident_count_kernel<<<static_cast<unsigned>(blocks), kCountThreads, 0, s>>>(
       a->local_ids, a->n_rows, a->param_rows, a->pos_start, a->pos_end, a->pos_slot,
       a->n_positions, a->block_size, a->pos_count, a->chunk_table, a->err);
   TGS_LAUNCH_CHECK();

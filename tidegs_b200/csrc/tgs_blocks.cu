@@ -314,13 +314,16 @@ __global__ void __launch_bounds__(kCopyThreads) copy_blocks_kernel(const CopyPar
 // ---------------------------------------------------------------------------
 // Global ids and block-start tables.
 // ---------------------------------------------------------------------------
+// shift >= 0: block_size == 1 << shift (a shift and a mask instead of a
+// 64-bit division per row).
 __global__ void fill_gids_kernel(int64_t* __restrict__ dst, int64_t offset,
                                  const int64_t* __restrict__ block_ids, int64_t n,
-                                 int64_t block_size) {
+                                 int64_t block_size, int shift) {
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < n;
        r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t pos = r / block_size;
-    dst[offset + r] = block_ids[pos] * block_size + (r - pos * block_size);
+    const int64_t pos = shift >= 0 ? r >> shift : r / block_size;
+    const int64_t in_block = shift >= 0 ? r & (block_size - 1) : r - pos * block_size;
+    dst[offset + r] = __ldg(block_ids + pos) * block_size + in_block;
   }
 }
 
@@ -711,8 +714,9 @@ extern "C" int tgs_fill_global_ids(int64_t* dst, int64_t offset, const int64_t* 
   TGS_CHECK_ARG(n_rows >= 0 && offset >= 0 && block_size >= 1, "tgs_fill_global_ids: bad sizes");
   if (n_rows == 0) return TGS_OK;
   TGS_CHECK_ARG(dst && block_ids, "tgs_fill_global_ids: NULL pointer");
+  const int shift = (block_size & (block_size - 1)) == 0 ? __builtin_ctzll(block_size) : -1;
   fill_gids_kernel<<<grid_for(n_rows, 256), 256, 0, as_stream(stream)>>>(dst, offset, block_ids,
-                                                                        n_rows, block_size);
+                                                                        n_rows, block_size, shift);
   TGS_LAUNCH_CHECK();
   return TGS_OK;
 }

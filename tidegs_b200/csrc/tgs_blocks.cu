@@ -47,6 +47,7 @@ struct UnpackParams {
   int use_bulk;  // packed is 16-byte aligned
   int32_t* err;
   const int64_t* block_dst;  // first target row per block, or null (contiguous)
+  int block_shift;           // block_size == 1 << block_shift, or -1
 };
 
 struct UnpackSmem {
@@ -55,6 +56,11 @@ struct UnpackSmem {
 };
 constexpr size_t kUnpackSmemBytes = sizeof(UnpackSmem);
 
+// Writes a staged tile's rows into the six components. A component range
+// that starts on a 16-byte boundary and holds a multiple of 4 floats (every
+// full tile of a 16-byte aligned component whose first row is a multiple of
+// 4) goes out as float4 stores, each thread gathering 4 consecutive floats of
+// the range from the staged rows; other ranges use one float per thread.
 template <int kLayout>
 __device__ __forceinline__ void scatter_tile(const float* __restrict__ tile, int rows,
                                              int64_t dst_row0, const Comp6& comp) {
@@ -64,6 +70,19 @@ __device__ __forceinline__ void scatter_tile(const float* __restrict__ tile, int
     const int src_col = layout_offset(kLayout, c);
     float* __restrict__ dst = comp.p[c] + dst_row0 * w;
     const int n = rows * w;
+    if ((n & 3) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+      for (int e4 = threadIdx.x; e4 < (n >> 2); e4 += kUnpackThreads) {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int e = 4 * e4 + j;
+          const int r = e / w;
+          v[j] = tile[r * kRowWidth + src_col + (e - r * w)];
+        }
+        *reinterpret_cast<float4*>(dst + 4 * e4) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+      continue;
+    }
     for (int e = threadIdx.x; e < n; e += kUnpackThreads) {
       const int r = e / w;
       const int k = e - r * w;
@@ -134,15 +153,17 @@ __global__ void __launch_bounds__(kUnpackThreads, kUnpackCtasPerSm) unpack_kerne
     }
     // a tile never straddles two blocks in the scatter mode (block_size is a
     // multiple of the tile), so its target rows stay contiguous
-    const int64_t dst_row0 =
-        a.block_dst != nullptr
-            ? a.block_dst[(t * kTileRows) / a.block_size] + (t * kTileRows) % a.block_size
-            : a.target_offset + t * kTileRows;
+    const int64_t row0 = t * kTileRows;
+    int64_t dst_row0 = a.target_offset + row0;
+    if (a.block_dst != nullptr) {  // block_size >= kTileRows here
+      const int64_t blk0 = a.block_shift >= 0 ? row0 >> a.block_shift : row0 / a.block_size;
+      dst_row0 = a.block_dst[blk0] + (row0 - blk0 * a.block_size);
+    }
     scatter_tile<kLayout>(tile, rows, dst_row0, a.comp);
     if (a.gids != nullptr) {
       for (int r = tid; r < rows; r += kUnpackThreads) {
-        const int64_t row = t * kTileRows + r;
-        const int64_t pos = row / a.block_size;
+        const int64_t row = row0 + r;
+        const int64_t pos = a.block_shift >= 0 ? row >> a.block_shift : row / a.block_size;
         a.gids[dst_row0 + r] = a.block_ids[pos] * a.block_size + (row - pos * a.block_size);
       }
     }
@@ -648,6 +669,8 @@ extern "C" int tgs_unpack_rows(const TgsUnpackArgs* a, void* stream) {
   p.use_bulk = aligned16(a->packed) ? 1 : 0;
   p.err = a->err;
   p.block_dst = a->block_dst;
+  p.block_shift = a->block_size >= 1 && (a->block_size & (a->block_size - 1)) == 0
+                      ? __builtin_ctzll(a->block_size) : -1;
   const int64_t n_tiles = ceil_div<int64_t>(a->n_rows, kTileRows);
   const int grid = static_cast<int>(
       std::min<int64_t>(n_tiles, static_cast<int64_t>(sm_count()) * kUnpackCtasPerSm));

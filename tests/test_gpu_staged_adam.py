@@ -318,14 +318,16 @@ def _rank_order_sum(vis, block, B):
     return s
 
 
-@pytest.mark.parametrize("W,B,reorder", [(3, 64, False), (2, 32, True), (4, 96, True),
-                                         (2, 48, False), (3, 2048, True)])
-def test_pull_staged_bit_exact_with_oracle(W, B, reorder):
+@pytest.mark.parametrize("W,B,reorder,ctas", [(3, 64, False, 0), (2, 32, True, 0),
+                                              (4, 96, True, 0), (2, 48, False, 0),
+                                              (3, 2048, True, 0), (3, 2048, False, 5)])
+def test_pull_staged_bit_exact_with_oracle(W, B, reorder, ctas):
     """The owner's pull update over whole exchanged blocks equals the oracle
     update on the rank-order sum of the senders' gradients, bit for bit;
     three steps with an eviction and re-admission before the last one.
     `reorder` puts the owned blocks in the working set in an order unlike
-    their slot order."""
+    their slot order; `ctas` caps the streamed kernel's grid (0: one CTA per
+    SM), so that few CTAs walk many chunks each."""
     from tidegs_b200 import GPUResidentAdam
     from tidegs_b200.sharded import PeerGradPull, make_plan
 
@@ -352,6 +354,7 @@ def test_pull_staged_bit_exact_with_oracle(W, B, reorder):
     opt.set_resident_blocks(owned)
     oracle.set_resident_blocks(owned)
     pull = PeerGradPull.in_process(grads, owner, B, "cuda")
+    pull.max_ctas = ctas
     ids = np.arange(rows, dtype=np.int64)
     summed = np.concatenate([_rank_order_sum(vis, b, B) for b in owned])
     ref_grads = {n: summed[:, ob.UNIFIED[n]:ob.UNIFIED[n] + w].copy() for n, w in ob.WIDTHS.items()}

@@ -511,6 +511,9 @@ class PeerGradPull:
         self._rows_dev = _ops.i64_to_device(self.rows, self.device)
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._grads = keep  # keeps the exported tensors alive
+        # cap on the streamed update's CTAs (0 = one per SM): leaves SMs to
+        # work on another stream while NVLink bounds the update
+        self.max_ctas = 0
         self._collective = collective
         self._closed = False
 
@@ -546,11 +549,11 @@ class PeerGradPull:
         self.barrier()
 
     def launch(self, adam_args, plan: ExchangePlan, stream: int, tables=None,
-               max_ctas: int = 0) -> None:
+               max_ctas: Optional[int] = None) -> None:
         """The fused update alone; the caller provides both barriers.
         tables: the result of tables(plan), when the caller built it earlier.
-        max_ctas: cap on the streamed kernel's CTAs (0 = one per SM), to leave
-        SMs to work on another stream."""
+        max_ctas: cap on the streamed kernel's CTAs (0 = one per SM; None =
+        self.max_ctas), to leave SMs to work on another stream."""
         S = plan.n_out
         if int(adam_args.n_rows) != S * plan.block_size:
             raise ValueError("PeerGradPull: rows to update do not match the plan's blocks")
@@ -568,7 +571,7 @@ class PeerGradPull:
         # start at this rank's share of the rows, so that at any moment the
         # owners pull from different senders
         args.rotate_rows = (self.rank * S // max(1, self.world)) * plan.block_size
-        args.max_ctas = int(max_ctas)
+        args.max_ctas = int(self.max_ctas if max_ctas is None else max_ctas)
         args.err = adam_args.err
         _lib.call("tgs_resident_adam_apply_sum", args, stream)
         cur = torch.cuda.current_stream(self.device)

@@ -538,9 +538,11 @@ TGS_API int tgs_peer_export(const void* dev_ptr, TgsPeerHandle* handle, int64_t*
 
 /* Owner-side reduction fused into the resident Adam step ("pull"): the
  * gradient of compact row i is read from the senders' own gradient buffers
- * (this rank's and peers' through IPC mappings, plain loads over NVLink) and
- * summed in listed (rank) order, one rounding per addition, then the update
- * of tgs_resident_adam_apply runs on it. Equal, bit for bit, to
+ * (this rank's and peers' through IPC mappings, over NVLink: non-multicast
+ * bulk copies into shared memory for streamable 32-row chunks inside one
+ * segment when adam.chunk_table is given, plain loads elsewhere) and summed
+ * in listed (rank) order, one rounding per addition, then the update of
+ * tgs_resident_adam_apply runs on it. Equal, bit for bit, to
  * tgs_grad_push / all-to-all + tgs_block_grad_sum + tgs_resident_adam_apply,
  * without the receive buffers, the push and the sum pass.
  * Compact rows are split into segments (normally one per visible block);

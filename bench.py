@@ -201,6 +201,16 @@ class ClockSampler:
         out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
         if self.proc is None:
             return out
+        # nvidia-smi takes a while to start (longer with one instance per
+        # rank); keep it until it has written a sample, at most 5 s
+        deadline = time.time() + 5.0
+        while time.time() < deadline and self.proc.poll() is None:
+            try:
+                if Path(self.path).read_text().count("\n") >= 1:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.05)
         time.sleep(0.25)
         self.proc.terminate()
         try:
@@ -771,8 +781,10 @@ class DeviceStep:
         the slots those blocks left. Main stream: the update of step k,
         dirty marks and bounds. Neither touches the other's slots. Step k+1's
         update waits for step k's unpack; step k+1's write-back waits for
-        step k's update. Per step the same kernels run as in step(); a step
-        writes back the blocks the step before it evicted."""
+        step k's update. The host queues the update first and the side
+        stream's work after it, so the main stream never idles while the host
+        prepares the write-back. Per step the same kernels run as in step();
+        a step writes back the blocks the step before it evicted."""
         _ops = self._ops
         sched = self.sched
         main = torch.cuda.current_stream(self.device)
@@ -783,6 +795,14 @@ class DeviceStep:
         evict_pos, incoming, dirty = self.trace.turn[k]
         evict_slots = self.arena_of_pos[evict_pos]
         evicted_blocks = self.arena_block[evict_slots]
+        if self.world > 1:
+            slots, ids = self.exchange_grads(k)
+            self._phase("exchange")
+        else:
+            slots = self.visible_arena(k)
+            ids = self.row_ids(slots)
+        self.adam(ids, timed)
+        # the side stream's work, queued while the GPU runs the update
         pending = self._pending_wb
         wb_ids = pending[0].wait() if pending is not None else []
         with torch.cuda.stream(self.side):
@@ -807,13 +827,6 @@ class DeviceStep:
         if pending is not None and len(wb_ids):
             _ops.dirty_mark(self.bitmap, wb_ids, False)
         self._phase("side_issue")
-        if self.world > 1:
-            slots, ids = self.exchange_grads(k)
-            self._phase("exchange")
-        else:
-            slots = self.visible_arena(k)
-            ids = self.row_ids(slots)
-        self.adam(ids, timed)
         self.plan_ahead(k)
         _ops.dirty_mark(self.bitmap, self.arena_block[slots].tolist(), True)
         _ops.block_bounds(self.arena["xyz"], (slots * B).tolist(), [B] * slots.size,

@@ -1757,11 +1757,13 @@ def main(argv=None):
     adam_ctas = args.adam_ctas if args.adam_ctas >= 0 else (OVERLAP_ADAM_CTAS if overlap else 0)
     dev = DeviceStep(device, sched, trace, world=world, exchange=args.exchange, overlap=overlap,
                      adam_ctas=adam_ctas)
+    # sampling starts before the warm-up so that nvidia-smi is running when
+    # the (short) timed region starts
+    clocks = ClockSampler(device)
     for k in range(args.warmup):
         dev.step(k)
     torch.cuda.synchronize()
     barrier(world)
-    clocks = ClockSampler(device)
     launches0 = _lib.launch_counter["kernels"]
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)

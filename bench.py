@@ -119,11 +119,12 @@ NVLINK_GBPS = 770.0
 # the pull update, on the SMs the update leaves free (OVERLAP_ADAM_CTAS of
 # 148 for the update): where NVLink bounds the update (remote contributions
 # per owner grow with the camera split), HBM has room for it. Measured on
-# B200: at 8 GPUs 11.50 G updates/s with 128 CTAs against 10.67 G without
-# the overlap (10.86 G with 148); at 1 and 2 GPUs the step is HBM-bound and
-# the overlap gains nothing.
-OVERLAP_MIN_WORLD = 8
-OVERLAP_ADAM_CTAS = 128
+# B200 (G updates/s, update CTAs): 8 GPUs 10.67 without the overlap, 10.86
+# (148), 11.50 (128), 11.97 (120), 12.48 (112), 12.24 (96), 11.33 (80);
+# 4 GPUs 7.47 without, 7.68 (128), 7.86 (112), 7.23 (96); 2 GPUs 4.16
+# without, 3.99 (112): there the step is HBM-bound.
+OVERLAP_MIN_WORLD = 4
+OVERLAP_ADAM_CTAS = 112
 LRS = {"xyz": 1.6e-4, "opacity": 0.05, "scaling": 5e-3, "rotation": 1e-3, "features_dc": 2.5e-3,
        "features_rest": 1.25e-4}
 

@@ -630,6 +630,20 @@ class DeviceStep:
         arena_of_pos[ev] = self.spare
         return arena_block, arena_of_pos, np.sort(freed)
 
+    def _turn_over(self, k: int, evict_pos: np.ndarray, incoming: np.ndarray) -> None:
+        """The spare slots hold step k's incoming blocks and the evicted
+        blocks' slots become the spare ones (no copy); the incoming slots get
+        new admission stamps (their moments read as zero) and step counters
+        of zero, and the working-set slices follow."""
+        _ops = self._ops
+        new_slots = self.spare
+        self.arena_block, self.arena_of_pos, self.spare = self._after_turnover(k)
+        self.sched.slot_block[evict_pos] = incoming
+        self.stamp_host[new_slots] += 1
+        _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
+        self.slot_step.index_fill_(0, _ops.i64_to_device(new_slots, self.device), 0)
+        self._upload_pos_end()
+
     def plan_ahead(self, k: int):
         """Builds step k+1's plan on the host while the GPU runs step k (the
         arena map after step k's turnover is known from the schedule)."""
@@ -717,7 +731,6 @@ class DeviceStep:
         if self.overlap:
             return self.step_overlapped(k, timed)
         _ops = self._ops
-        sched = self.sched
         self._events = []
         self._phase("start")
         if self.world > 1:
@@ -765,13 +778,7 @@ class DeviceStep:
         self._phase("writeback")
         # 5. the spare slots hold the incoming blocks; the evicted blocks'
         # slots become the spare ones (no copy). Incoming slots: new stamps.
-        new_slots = self.spare
-        self.arena_block, self.arena_of_pos, self.spare = self._after_turnover(k)
-        sched.slot_block[evict_pos] = incoming
-        self.stamp_host[new_slots] += 1
-        _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
-        self.slot_step.index_fill_(0, _ops.i64_to_device(new_slots, self.device), 0)
-        self._upload_pos_end()
+        self._turn_over(k, evict_pos, incoming)
         self._phase("tables")
         return int(ids.numel())
 
@@ -788,7 +795,6 @@ class DeviceStep:
         prepares the write-back. Per step the same kernels run as in step();
         a step writes back the blocks the step before it evicted."""
         _ops = self._ops
-        sched = self.sched
         main = torch.cuda.current_stream(self.device)
         self._events = []
         self._phase("start")
@@ -842,13 +848,7 @@ class DeviceStep:
         self._pending_wb = (_ops.dirty_select_async(self.bitmap, evicted_blocks[order].tolist()),
                             evicted_blocks[order], evict_slots[order])
         self._phase("dirty_select")
-        new_slots = self.spare
-        self.arena_block, self.arena_of_pos, self.spare = self._after_turnover(k)
-        sched.slot_block[evict_pos] = incoming
-        self.stamp_host[new_slots] += 1
-        _ops.upload_into(self.slot_stamp, self.stamp_host.view(np.int32))
-        self.slot_step.index_fill_(0, _ops.i64_to_device(new_slots, self.device), 0)
-        self._upload_pos_end()
+        self._turn_over(k, evict_pos, incoming)
         self._phase("tables")
         return int(ids.numel())
 
